@@ -1,0 +1,369 @@
+// C ABI of the mxgg library (see include/mxgg.h): argument validation,
+// TMA descriptor construction and kernel launches.  Host code never
+// synchronises (except mxgg_device_status) and never allocates.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mxgg.h"
+#include "grouped_gemm.cuh"
+#include "quantize.cuh"
+#include "tile_map.cuh"
+
+namespace mxgg {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define MXGG_CUDA_TRY(expr)                                                                   \
+  do {                                                                                        \
+    cudaError_t e_ = (expr);                                                                  \
+    if (e_ != cudaSuccess) return fail(MXGG_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// device-side error word raised by bounded waits
+__device__ uint32_t g_status_word;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool init = false;
+  int num_sms = 0;
+  uint32_t* status = nullptr;   // device address of g_status_word
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+int g_tile_n = 0;
+int g_group_m = 0;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int get_device_state(DeviceState** out) {
+  int dev = 0;
+  MXGG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(MXGG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    int major = 0, minor = 0;
+    MXGG_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MXGG_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      return fail(MXGG_ERR_UNSUPPORTED, "mxgg kernels are built for sm_100a; device %d is sm_%d%d", dev, major,
+                  minor);
+    MXGG_CUDA_TRY(cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    void* p = nullptr;
+    MXGG_CUDA_TRY(cudaGetSymbolAddress(&p, g_status_word));
+    st.status = static_cast<uint32_t*>(p);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      MXGG_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+      if (q != cudaDriverEntryPointSuccess || !fn)
+        return fail(MXGG_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    st.init = true;
+  }
+  *out = &st;
+  return MXGG_OK;
+}
+
+// 2-D tensor map over a row-major (rows, cols) matrix.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esize, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swz) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * (uint64_t)esize};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MXGG_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu stride=%llu box=%ux%u",
+                (int)r, (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)row_stride_elems,
+                box_rows, box_cols);
+  return MXGG_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int out_esize(int out_dtype) { return out_dtype == MXGG_DTYPE_F32 ? 4 : 2; }
+
+CUtensorMapDataType out_tmap_dtype(int out_dtype) {
+  switch (out_dtype) {
+    case MXGG_DTYPE_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case MXGG_DTYPE_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  }
+}
+
+template <int BN, int STAGES, int ACC, typename OutT>
+int launch_gemm_t(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                  const GemmParams& p, long long max_units, cudaStream_t stream) {
+  using S = SmemLayout<BN, STAGES, OutT>;
+  constexpr size_t kSmem = sizeof(S) + 1024;
+  static_assert(kSmem <= 232448, "shared memory budget");
+  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, OutT>;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  MXGG_CUDA_TRY(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    attr_done[dev] = true;
+  }
+  const long long grid = std::max(1LL, std::min<long long>(st.num_sms, max_units));
+  kern<<<(unsigned)grid, kThreads, kSmem, stream>>>(ta, tb, to, p);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+template <int BN, int STAGES, int ACC>
+int launch_gemm_bn(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                   const GemmParams& p, long long max_units, int out_dtype, cudaStream_t stream) {
+  switch (out_dtype) {
+    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, __half>(st, ta, tb, to, p, max_units, stream);
+    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, float>(st, ta, tb, to, p, max_units, stream);
+    default: return launch_gemm_t<BN, STAGES, ACC, __nv_bfloat16>(st, ta, tb, to, p, max_units, stream);
+  }
+}
+
+int pick_tile_n(int64_t n_extent) {
+  if (g_tile_n == 128 || g_tile_n == 256) return g_tile_n;
+  return n_extent >= 256 ? 256 : 128;
+}
+
+int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const void* b_scale,
+             const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
+             void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const char* what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
+  if (out_dtype != MXGG_DTYPE_BF16 && out_dtype != MXGG_DTYPE_F16 && out_dtype != MXGG_DTYPE_F32)
+    return fail(MXGG_ERR_INVALID, "%s: unknown out_dtype %d", what, out_dtype);
+  if (M < 0 || N < 0 || K < 0 || E < 1)
+    return fail(MXGG_ERR_INVALID, "%s: bad sizes M=%lld N=%lld K=%lld E=%lld", what, (long long)M, (long long)N,
+                (long long)K, (long long)E);
+  if (E > kMaxGroups) return fail(MXGG_ERR_UNSUPPORTED, "%s: E=%lld exceeds %d groups", what, (long long)E, kMaxGroups);
+  // contraction length: fwd K, wgrad tokens M
+  const int64_t C = mode == kFwd ? K : M;
+  const int64_t rows_a = mode == kFwd ? M : N;
+  const int64_t rows_b = mode == kFwd ? E * N : K;
+  const int64_t out_cols = mode == kFwd ? N : K;
+  const int64_t out_rows = mode == kFwd ? M : E * N;
+  if (C % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "%s: contraction length %lld must be a multiple of 32", what, (long long)C);
+  if (out_rows == 0 || out_cols == 0) return MXGG_OK;
+  if (!out) return fail(MXGG_ERR_INVALID, "%s: null output", what);
+  const int64_t lim = (int64_t)1 << 31;
+  if (rows_a >= lim || rows_b >= lim || out_rows >= lim || C >= lim || out_cols >= lim)
+    return fail(MXGG_ERR_UNSUPPORTED, "%s: extents beyond 2^31", what);
+  if (C == 0) {
+    // empty contraction: every product is the zero accumulator (the
+    // reference's loops run zero times and store zeros, backward.py:67,
+    // forward.py:207-212)
+    MXGG_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(out_rows * out_cols * out_esize(out_dtype)), stream));
+    return MXGG_OK;
+  }
+  if (!a || !b || !a_scale || !b_scale || !offs) return fail(MXGG_ERR_INVALID, "%s: null input pointer", what);
+  if (!aligned(a, 16) || !aligned(b, 16))
+    return fail(MXGG_ERR_INVALID, "%s: e4m3 operands must be 16-byte aligned", what);
+
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+
+  const int bn = pick_tile_n(out_cols);
+  GemmParams p{};
+  p.mode = mode;
+  p.E = (int)E;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.rows_a = (int)rows_a;
+  p.rows_b = (int)rows_b;
+  p.contraction = (int)C;
+  p.offs = offs;
+  p.sfa = static_cast<const uint8_t*>(a_scale);
+  p.sfb = static_cast<const uint8_t*>(b_scale);
+  p.sf_ld = C / 32;
+  p.out = out;
+  p.out_ld = out_cols;
+  p.out_rows = out_rows;
+  p.out_cols = (int)out_cols;
+  p.sf_fast = (C % 128 == 0) && aligned(a_scale, 4) && aligned(b_scale, 4);
+  const int es = out_esize(out_dtype);
+  p.tma_store = aligned(out, 16) && ((out_cols * es) % 16 == 0);
+  p.group_m = g_group_m > 0 ? g_group_m : 16;
+  p.status = st->status;
+
+  CUtensorMap ta, tb, to;
+  if (int rc = make_tmap_2d(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
+                            kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_tmap_2d(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C, (uint64_t)C,
+                            kBK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (p.tma_store) {
+    if (int rc = make_tmap_2d(&to, out, out_tmap_dtype(out_dtype), es, (uint64_t)out_rows, (uint64_t)out_cols,
+                              (uint64_t)out_cols, 64 / es, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+  } else {
+    std::memset(&to, 0, sizeof(to));
+  }
+
+  long long max_units;
+  if (mode == kFwd) {
+    const long long mt_ub = (M + kBM - 1) / kBM + (E - 1);
+    max_units = mt_ub * ((N + bn - 1) / bn);
+  } else {
+    max_units = E * ((N + kBM - 1) / kBM) * ((K + bn - 1) / bn);
+  }
+  if (bn == 256) return launch_gemm_bn<256, 4, 1>(*st, ta, tb, to, p, max_units, out_dtype, stream);
+  return launch_gemm_bn<128, 6, 2>(*st, ta, tb, to, p, max_units, out_dtype, stream);
+}
+
+}  // namespace
+}  // namespace mxgg
+
+using namespace mxgg;
+
+extern "C" {
+
+int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                    const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E, void* out,
+                    int out_dtype, void* stream) {
+  return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, stream);
+}
+
+int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+               const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
+               int out_dtype, void* stream) {
+  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, stream);
+}
+
+int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales, int mode,
+                     int scale_layout, void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (rows < 0 || cols < 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: negative size");
+  if (rows == 0 || cols == 0) return MXGG_OK;
+  if (!x || !q || !scales) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: null pointer");
+  if (x_dtype != MXGG_DTYPE_BF16 && x_dtype != MXGG_DTYPE_F16 && x_dtype != MXGG_DTYPE_F32)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown x_dtype %d", x_dtype);
+  if (scale_layout != MXGG_SCALE_ROW_MAJOR && scale_layout != MXGG_SCALE_BLOCKED)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown scale layout %d", scale_layout);
+  if (!aligned(x, 16) || !aligned(q, 8))
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: x must be 16-byte and q 8-byte aligned");
+  if (mode != MXGG_QUANT_ROWS && mode != MXGG_QUANT_COLS)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown mode %d", mode);
+  if (mode == MXGG_QUANT_ROWS && cols % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: cols=%lld not a multiple of 32", (long long)cols);
+  if (mode == MXGG_QUANT_COLS && rows % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: rows=%lld not a multiple of 32", (long long)rows);
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const int nthreads = 256;
+  if (mode == MXGG_QUANT_ROWS) {
+    if (cols % 32 != 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: cols=%lld not a multiple of 32", (long long)cols);
+    const long long work = rows * cols / 8;
+    const long long blocks = std::max(1LL, std::min<long long>((work + nthreads - 1) / nthreads, (long long)st->num_sms * 16));
+    switch (x_dtype) {
+      case MXGG_DTYPE_BF16:
+        quantize_rows_e4m3<__nv_bfloat16><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+        break;
+      case MXGG_DTYPE_F16:
+        quantize_rows_e4m3<__half><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const __half*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+        break;
+      default:
+        quantize_rows_e4m3<float><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const float*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+    }
+  } else if (mode == MXGG_QUANT_COLS) {
+    if (rows % 32 != 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: rows=%lld not a multiple of 32", (long long)rows);
+    if (cols % 8 != 0) return fail(MXGG_ERR_UNSUPPORTED, "mxgg_quantize_mx: column mode needs cols %% 8 == 0");
+    const long long tiles = (rows / 32) * ((cols + 63) / 64);
+    const long long blocks = std::max(1LL, std::min<long long>(tiles, (long long)st->num_sms * 8));
+    switch (x_dtype) {
+      case MXGG_DTYPE_BF16:
+        quantize_cols_e4m3<__nv_bfloat16><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+        break;
+      case MXGG_DTYPE_F16:
+        quantize_cols_e4m3<__half><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const __half*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+        break;
+      default:
+        quantize_cols_e4m3<float><<<(unsigned)blocks, nthreads, 0, stream>>>(
+            static_cast<const float*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+    }
+  } else {
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown mode %d", mode);
+  }
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_build_tile_map(const int32_t* offs, int64_t E, int64_t M, int32_t block_m, int32_t* out, void* stream_v) {
+  if (E < 1 || M < 0 || block_m < 1 || !offs || !out)
+    return fail(MXGG_ERR_INVALID, "mxgg_build_tile_map: bad arguments");
+  if (E > (1 << 16)) return fail(MXGG_ERR_UNSUPPORTED, "mxgg_build_tile_map: E beyond 65536");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long grid_m_ub = (M + block_m - 1) / block_m + (E - 1);
+  const long long n = 2 * E + 1 + grid_m_ub;
+  tile_map_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream_v)>>>(
+      offs, (int)E, (int)block_m, (int)grid_m_ub, out);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_set_tile_config(int32_t tile_n, int32_t group_m) {
+  if (tile_n != 0 && tile_n != 128 && tile_n != 256)
+    return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: tile_n must be 0, 128 or 256");
+  if (group_m < 0) return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: group_m must be >= 0");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_tile_n = tile_n;
+  g_group_m = group_m;
+  return MXGG_OK;
+}
+
+int mxgg_device_status(uint32_t* status_out, int clear, void* stream_v) {
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  uint32_t v = 0;
+  MXGG_CUDA_TRY(cudaMemcpyAsync(&v, st->status, sizeof(v), cudaMemcpyDeviceToHost, stream));
+  MXGG_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (clear) {
+    MXGG_CUDA_TRY(cudaMemsetAsync(st->status, 0, sizeof(uint32_t), stream));
+    MXGG_CUDA_TRY(cudaStreamSynchronize(stream));
+  }
+  if (status_out) *status_out = v;
+  return MXGG_OK;
+}
+
+const char* mxgg_last_error(void) { return g_last_error.c_str(); }
+
+int32_t mxgg_version(void) { return 1; }
+
+}  // extern "C"

@@ -1,0 +1,214 @@
+// MX quantiser (FLOOR scaling, 32-element blocks) for sm_100a.
+//
+// Bit-exact restatement of the reference's utils.to_mx (utils.py:67-105):
+//   amax    = max |x| over the block (NaN propagates, utils.py:86)
+//   e       = biased exponent of max(amax, FLT_MIN)            (utils.py:88-92)
+//   s       = clamp(e - emax, 0, 254)   emax = 8 (e4m3), 2 (e2m1)  (utils.py:93-95)
+//   q       = cast(clamp(x * 2^(127 - s), -max, max))           (utils.py:97-101)
+// x * 2^(127-s) equals the reference's x / 2^(s-127) exactly: both are the
+// correctly rounded value of the same real number, and 2^(127-s) is a normal
+// float for every reachable s.  NaN keeps its sign (0x7F / 0xFF), like the
+// reference's CPU cast.
+//
+// Layout: each thread owns 8 consecutive elements (one 16-byte bf16 vector),
+// four neighbouring lanes form a 32-block and reduce the amax with two xor
+// shuffles; stores are 8-byte vectors.  The kernel is HBM-bound: it reads
+// 2 B/elem (bf16), writes 1 B/elem + 1 B/32 elem.
+//
+// Two modes:
+//   rows  : quantise along the contiguous last dim (the reference's to_mx).
+//   cols  : quantise along the leading dim and write the transposed result
+//           (to_mx(x.t().contiguous()) fused into one pass) -- the operand
+//           layout the wgrad pass consumes (scales along tokens).
+// Scales are written row-major (the reference layout) or, on request, in the
+// 128x4 blocked scale-factor atom layout used by Blackwell block-scaled MMAs.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include <cstdint>
+
+namespace mxgg {
+
+enum : int { kInBF16 = 0, kInF16 = 1, kInF32 = 2 };
+enum : int { kScaleRowMajor = 0, kScaleBlocked = 1 };
+
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+// 8 consecutive inputs -> float
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+// scale byte from the (NaN-propagating) max of |x| bit patterns
+__device__ __forceinline__ uint32_t floor_scale(uint32_t amax_bits, int emax) {
+  const uint32_t b = max(amax_bits, 0x00800000u);     // clamp(min = FLT_MIN)
+  const int e = (int)(b >> 23);                       // biased exponent (sign already clear)
+  return (uint32_t)min(max(e - emax, 0), 254);
+}
+
+// e4m3 byte of x * mult, with the reference's clamp and NaN sign rule
+__device__ __forceinline__ uint32_t e4m3_byte(float x, float mult) {
+  if (x != x) return (__float_as_uint(x) >> 31) ? 0xFFu : 0x7Fu;
+  float v = x * mult;
+  v = fminf(fmaxf(v, -448.0f), 448.0f);
+  return (uint32_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+
+// offset of scale (r, c) of a (R, C) scale matrix in the blocked atom layout
+__device__ __forceinline__ long long blocked_sf_offset(long long r, long long c, long long C) {
+  const long long cb = (C + 3) / 4;
+  const long long atom = (r / 128) * cb + (c / 4);
+  return atom * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
+}
+
+// -------------------------------------------------------------- row mode
+// x: (R, C) contiguous, C % 32 == 0.  q: (R, C) e4m3.  s: scales.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ x, long long R, long long C,
+                                                          uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+                                                          int scale_layout) {
+  const long long total8 = R * C / 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const long long SC = C / 32;
+  // every thread of a warp runs the same number of iterations (the shuffles
+  // need the whole quad), so iterate over warp-rounded ranges
+  const long long total8_w = (total8 + 31) / 32 * 32;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total8_w; i += stride) {
+    const bool live = i < total8;
+    float f[8];
+    uint32_t m = 0;
+    if (live) {
+      load8<T>(x + i * 8, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m = max(m, abs_bits(f[k]));
+    }
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (!live) continue;
+    const uint32_t sc = floor_scale(m, 8);
+    const float mult = __uint_as_float((254u - sc) << 23);    // 2^(127 - s)
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) lo |= e4m3_byte(f[k], mult) << (8 * k);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) hi |= e4m3_byte(f[4 + k], mult) << (8 * k);
+    *reinterpret_cast<uint2*>(q + i * 8) = make_uint2(lo, hi);
+    if ((lane & 3) == 0) {
+      const long long blk = i / 4;
+      if (scale_layout == kScaleRowMajor) {
+        s[blk] = (uint8_t)sc;
+      } else {
+        const long long r = blk / SC, c = blk - r * SC;
+        s[blocked_sf_offset(r, c, SC)] = (uint8_t)sc;
+      }
+    }
+  }
+}
+
+// -------------------------------------------------------------- col mode
+// x: (R, C) contiguous, R % 32 == 0.  Quantises along R and writes the
+// transposed result: qt (C, R) e4m3, scales (C, R/32).
+// A CTA stages a 32 x 64 tile (32 rows of the block dimension, 64 columns)
+// through shared memory so both the reads of x and the writes of qt are
+// coalesced.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_cols_e4m3(const T* __restrict__ x, long long R, long long C,
+                                                          uint8_t* __restrict__ qt, uint8_t* __restrict__ s,
+                                                          int scale_layout) {
+  __shared__ float tile[32][65];
+  const long long RB = R / 32;
+  const long long CT = (C + 63) / 64;
+  const long long ntiles = RB * CT;
+  const int tid = threadIdx.x;
+  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const long long rb = t / CT, ct = t - rb * CT;
+    const long long r0 = rb * 32, c0 = ct * 64;
+    // load 32 rows x 64 cols: each thread 8 elements along a row
+    {
+      const int rr = tid >> 3;          // 0..31
+      const int cc = (tid & 7) * 8;     // 0..56
+      float f[8];
+      if (c0 + cc + 8 <= C) {
+        load8<T>(x + (r0 + rr) * C + c0 + cc, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) f[k] = (c0 + cc + k < C) ? to_f32(x[(r0 + rr) * C + c0 + cc + k]) : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) tile[rr][cc + k] = f[k];
+    }
+    __syncthreads();
+    // 64 output rows (columns of x); 4 threads per output row, 8 elements each
+    {
+      const int oc = tid >> 2;          // 0..63 : column of x = output row
+      const int part = tid & 3;         // which 8 of the 32 block elements
+      float f[8];
+      uint32_t m = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        f[k] = tile[part * 8 + k][oc];
+        m = max(m, abs_bits(f[k]));
+      }
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      const long long orow = c0 + oc;
+      if (orow < C) {
+        const uint32_t sc = floor_scale(m, 8);
+        const float mult = __uint_as_float((254u - sc) << 23);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) lo |= e4m3_byte(f[k], mult) << (8 * k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) hi |= e4m3_byte(f[4 + k], mult) << (8 * k);
+        *reinterpret_cast<uint2*>(qt + orow * R + r0 + part * 8) = make_uint2(lo, hi);
+        if (part == 0) {
+          if (scale_layout == kScaleRowMajor)
+            s[orow * RB + rb] = (uint8_t)sc;
+          else
+            s[blocked_sf_offset(orow, rb, RB)] = (uint8_t)sc;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace mxgg

@@ -1,0 +1,14 @@
+"""Availability probe shared by the grouped-GEMM entry points.
+
+Mirrors the reference's ``kernels/_common.py:17-27``.  The exported name
+``_rocm_mxfp8_available`` is kept so callers written against the reference
+keep importing; here it is True when the sm_100a library loads and the
+current device is a B200-class GPU (compute capability 10.0).
+"""
+
+import mxgg
+
+_UNAVAILABLE_MSG = "MXFP8 grouped-GEMM kernels require an sm_100 (B200) GPU and the built libmxgg.so"
+
+_mxfp8_available = mxgg.available()
+_rocm_mxfp8_available = _mxfp8_available

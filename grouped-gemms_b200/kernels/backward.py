@@ -1,0 +1,42 @@
+"""Weight-gradient MXFP8 grouped GEMM: ``triton_mxfp8_wgrad``.
+
+Same signature and argument meaning as the reference
+(``kernels/backward.py:217-305``): ``grad_W[g] = grad_output[group_g]^T @
+input_act[group_g]`` with both inputs dim1-quantised (scales along tokens).
+The reference stores bf16 whatever ``out_dtype`` says (backward.py:103,214);
+this implementation honours ``out_dtype`` (bf16, fp16 or fp32).  The Triton
+tile keywords are accepted and ignored.
+"""
+
+import torch
+
+import mxgg
+
+from ._common import _UNAVAILABLE_MSG, _mxfp8_available
+
+
+def triton_mxfp8_wgrad(
+    go_t: torch.Tensor,
+    go_scale: torch.Tensor,
+    ia_t: torch.Tensor,
+    ia_scale: torch.Tensor,
+    group_end_offsets: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    BLOCK_N: int = 256,
+    BLOCK_K: int = 256,
+    BLOCK_M: int = 64,
+    num_warps: int = 8,
+    num_stages: int = 2,
+) -> torch.Tensor:
+    """MXFP8 weight gradient: ``grad_W[g] = grad_output[group_g]^T @ input_act[group_g]``.
+
+    Args:
+        go_t: ``(N, M)`` float8_e4m3fn, with ``go_scale`` ``(N, M//32)``.
+        ia_t: ``(K, M)`` float8_e4m3fn, with ``ia_scale`` ``(K, M//32)``.
+        group_end_offsets: ``(E,)`` int32, multiples of 32.
+
+    Returns ``(E, N, K)`` of ``out_dtype``; empty groups give zeros.
+    """
+    if not _mxfp8_available:
+        raise NotImplementedError(_UNAVAILABLE_MSG)
+    return mxgg.wgrad_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)

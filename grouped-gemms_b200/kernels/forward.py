@@ -1,0 +1,59 @@
+"""Forward / dgrad MXFP8 grouped GEMM: ``triton_mxfp8_grouped_mm``.
+
+Same signature and argument meaning as the reference
+(``kernels/forward.py:461-606``): ``output[g] = input_act[group_g] @
+weight[g]^T`` per expert group over jagged token offsets.  The dgrad pass uses
+the same call with ``input_act = grad_output`` quantised along N and
+``weight = W^T`` (E, K, N) quantised along N.
+
+The Triton/AMD tuning keywords (BLOCK_*, GROUP_M, XCD_SWIZZLE, num_warps,
+num_stages, matrix_instr_nonkdim, waves_per_eu, kpack, cache hints) are
+accepted for drop-in compatibility (the reference's tuner passes them,
+tune_worker.py:87-91) and ignored: the sm_100a kernel picks its own tiles.
+"""
+
+import torch
+
+import mxgg
+
+from ._common import _UNAVAILABLE_MSG, _mxfp8_available
+
+
+def triton_mxfp8_grouped_mm(
+    input_act: torch.Tensor,
+    weight: torch.Tensor,
+    input_act_scales: torch.Tensor,
+    weight_scales: torch.Tensor,
+    group_end_offsets: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    BLOCK_M: int = None,
+    BLOCK_N: int = None,
+    BLOCK_K: int = None,
+    GROUP_M: int = None,
+    XCD_SWIZZLE: int = None,
+    num_warps: int = None,
+    num_stages: int = None,
+    matrix_instr_nonkdim: int = None,
+    waves_per_eu: int = None,
+    kpack: int = 1,
+    w_cache_modifier: str = None,
+    x_evict_policy: str = None,
+) -> torch.Tensor:
+    """MXFP8 grouped GEMM: ``output[g] = input_act[group_g] @ weight[g]^T``.
+
+    Args:
+        input_act: ``(M, K)`` float8_e4m3fn, row-major.
+        weight: ``(E, N, K)`` float8_e4m3fn, row-major.
+        input_act_scales: ``(M, K//32)`` e8m0 (uint8 or float8_e8m0fnu).
+        weight_scales: ``(E, N, K//32)`` e8m0.
+        group_end_offsets: ``(E,)`` int32 cumulative token counts per expert.
+
+    Returns ``(M, N)`` of ``out_dtype``; rows at or past ``group_end_offsets[-1]``
+    are left unwritten, like the reference (forward.py:583).
+    """
+    if not _mxfp8_available:
+        raise NotImplementedError(_UNAVAILABLE_MSG)
+    M, K = input_act.shape
+    E, N, K2 = weight.shape
+    assert K == K2, f"K mismatch: A={K}, B={K2}"
+    return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)

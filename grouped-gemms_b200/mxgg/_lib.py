@@ -1,0 +1,77 @@
+"""ctypes binding of the in-tree C ABI ``libmxgg.so`` (declared in include/mxgg.h).
+
+Loading fails loudly: there is no CPU or Triton fallback anywhere in the
+library.  Build the shared object with ``python grouped-gemms_b200/build.py``.
+"""
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmxgg.so")
+
+MXGG_OK = 0
+DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+QUANT_ROWS, QUANT_COLS = 0, 1
+SCALE_ROW_MAJOR, SCALE_BLOCKED = 0, 1
+
+# every symbol include/mxgg.h declares, with (restype, argtypes)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_int = ctypes.c_int
+SIGNATURES = {
+    "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
+    "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
+    "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
+    "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
+    "mxgg_set_tile_config": (_int, [_i32, _i32]),
+    "mxgg_device_status": (_int, [ctypes.POINTER(ctypes.c_uint32), _int, _vp]),
+    "mxgg_last_error": (ctypes.c_char_p, []),
+    "mxgg_version": (_i32, []),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class MxggError(RuntimeError):
+    pass
+
+
+def load():
+    """Load libmxgg.so (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise MxggError(
+                f"mxgg CUDA library not found at {LIB_PATH}; build it with "
+                "`python grouped-gemms_b200/build.py` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != MXGG_OK:
+        msg = load().mxgg_last_error().decode(errors="replace")
+        raise MxggError(f"{what} failed (code {rc}): {msg}")
+
+
+def device_status(clear: bool = True, stream=None) -> int:
+    v = ctypes.c_uint32(0)
+    check(load().mxgg_device_status(ctypes.byref(v), int(clear), stream), "mxgg_device_status")
+    return v.value
+
+
+def set_tile_config(tile_n: int = 0, group_m: int = 0) -> None:
+    check(load().mxgg_set_tile_config(tile_n, group_m), "mxgg_set_tile_config")

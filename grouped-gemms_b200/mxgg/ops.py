@@ -1,0 +1,147 @@
+"""torch.library custom ops over the mxgg C ABI.
+
+``mxgg::to_mx``, ``mxgg::grouped_mm`` and ``mxgg::wgrad`` enqueue the sm_100a
+kernels on the current CUDA stream through ctypes; nothing here synchronises,
+so the ops are safe inside CUDA graphs.  Each op has a fake (meta) kernel so
+``torch.compile`` can trace callers.  There is no CPU implementation: CPU
+tensors raise.
+"""
+
+import ctypes
+from typing import Tuple
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_OUT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16, torch.float32: _lib.DTYPE_F32}
+_IN_DTYPES = dict(_OUT_DTYPES)
+
+
+def _ptr(t: Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*ts: Tensor, what: str) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError(f"{what}: mxgg runs only on CUDA (sm_100a) tensors; got a {t.device} tensor")
+
+
+def as_u8(t: Tensor) -> Tensor:
+    """Scales may be uint8 or float8_e8m0fnu (reference forward.py:534-535)."""
+    return t if t.dtype == torch.uint8 else t.view(torch.uint8)
+
+
+# --------------------------------------------------------------------- to_mx
+@torch.library.custom_op("mxgg::to_mx", mutates_args=())
+def to_mx_op(x: Tensor, mode: int, scale_layout: int) -> Tuple[Tensor, Tensor]:
+    _require_cuda(x, what="mxgg::to_mx")
+    if x.dtype not in _IN_DTYPES:
+        raise TypeError(f"mxgg::to_mx: unsupported input dtype {x.dtype}")
+    x = x.contiguous()
+    R, C = x.shape
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        if mode == _lib.QUANT_ROWS:
+            q = torch.empty((R, C), dtype=torch.float8_e4m3fn, device=x.device)
+            sr, sc = R, C // 32
+        else:
+            q = torch.empty((C, R), dtype=torch.float8_e4m3fn, device=x.device)
+            sr, sc = C, R // 32
+        if scale_layout == _lib.SCALE_BLOCKED:
+            s = torch.zeros(((sr + 127) // 128 * 128) * ((sc + 3) // 4 * 4), dtype=torch.uint8, device=x.device)
+        else:
+            s = torch.empty((sr, sc), dtype=torch.uint8, device=x.device)
+        _lib.check(lib.mxgg_quantize_mx(_ptr(x), _IN_DTYPES[x.dtype], R, C, _ptr(q), _ptr(s), mode,
+                                        scale_layout, _stream(x.device)), "mxgg_quantize_mx")
+    return s, q
+
+
+@to_mx_op.register_fake
+def _(x, mode, scale_layout):
+    R, C = x.shape
+    if mode == _lib.QUANT_ROWS:
+        q = x.new_empty((R, C), dtype=torch.float8_e4m3fn)
+        sr, sc = R, C // 32
+    else:
+        q = x.new_empty((C, R), dtype=torch.float8_e4m3fn)
+        sr, sc = C, R // 32
+    if scale_layout == _lib.SCALE_BLOCKED:
+        s = x.new_empty(((sr + 127) // 128 * 128) * ((sc + 3) // 4 * 4), dtype=torch.uint8)
+    else:
+        s = x.new_empty((sr, sc), dtype=torch.uint8)
+    return s, q
+
+
+# ---------------------------------------------------------------- grouped_mm
+@torch.library.custom_op("mxgg::grouped_mm", mutates_args=())
+def grouped_mm_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
+                  out_dtype: torch.dtype) -> Tensor:
+    _require_cuda(a, b, a_scale, b_scale, offs, what="mxgg::grouped_mm")
+    if out_dtype not in _OUT_DTYPES:
+        raise TypeError(f"mxgg::grouped_mm: unsupported out_dtype {out_dtype}")
+    M, K = a.shape
+    E, N, _ = b.shape
+    a = a.contiguous()
+    b = b.contiguous()
+    a_scale = as_u8(a_scale).contiguous()
+    b_scale = as_u8(b_scale).contiguous()
+    offs = offs.to(torch.int32).contiguous()
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    with torch.cuda.device(a.device):
+        _lib.check(_lib.load().mxgg_grouped_mm(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
+                                               M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype],
+                                               _stream(a.device)), "mxgg_grouped_mm")
+    return out
+
+
+@grouped_mm_op.register_fake
+def _(a, b, a_scale, b_scale, offs, out_dtype):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
+
+
+# --------------------------------------------------------------------- wgrad
+@torch.library.custom_op("mxgg::wgrad", mutates_args=())
+def wgrad_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
+             out_dtype: torch.dtype) -> Tensor:
+    _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, what="mxgg::wgrad")
+    if out_dtype not in _OUT_DTYPES:
+        raise TypeError(f"mxgg::wgrad: unsupported out_dtype {out_dtype}")
+    N, M = go_t.shape
+    K = ia_t.shape[0]
+    E = offs.shape[0]
+    go_t = go_t.contiguous()
+    ia_t = ia_t.contiguous()
+    go_scale = as_u8(go_scale).contiguous()
+    ia_scale = as_u8(ia_scale).contiguous()
+    offs = offs.to(torch.int32).contiguous()
+    out = torch.empty((E, N, K), dtype=out_dtype, device=go_t.device)
+    with torch.cuda.device(go_t.device):
+        _lib.check(_lib.load().mxgg_wgrad(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
+                                          N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _stream(go_t.device)),
+                   "mxgg_wgrad")
+    return out
+
+
+@wgrad_op.register_fake
+def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype):
+    return go_t.new_empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype)
+
+
+def build_tile_map(offs: Tensor, M: int, block_m: int) -> Tensor:
+    """Routing tables in the reference's _build_expt_data layout (forward.py:340-365)."""
+    _require_cuda(offs, what="mxgg.build_tile_map")
+    offs = offs.to(torch.int32).contiguous()
+    E = offs.shape[0]
+    n = 2 * E + 1 + (M + block_m - 1) // block_m + max(E - 1, 0)
+    out = torch.empty(n, dtype=torch.int32, device=offs.device)
+    with torch.cuda.device(offs.device):
+        _lib.check(_lib.load().mxgg_build_tile_map(_ptr(offs), E, M, block_m, _ptr(out), _stream(offs.device)),
+                   "mxgg_build_tile_map")
+    return out

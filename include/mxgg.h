@@ -1,0 +1,115 @@
+/*
+ * mxgg -- Blackwell (sm_100a) MXFP8 grouped-GEMM library, C ABI.
+ *
+ * Drop-in replacement for the hot path of indianspeedster/grouped-gemms:
+ * the two grouped-GEMM entry points and the MX quantiser.  Every function
+ * takes plain device pointers, element counts and a CUDA stream passed as
+ * `void*` (a cudaStream_t / CUstream; NULL = legacy default stream), enqueues
+ * its work on that stream, never synchronises and never allocates.
+ * All functions return MXGG_OK (0) or an error code; mxgg_last_error()
+ * returns a message for the calling thread's last failure.
+ *
+ * Data formats (as produced by the reference's utils.to_mx, utils.py:67-105):
+ *   - element data: float8_e4m3fn bytes, row-major, quantised along the
+ *     contiguous (contraction) dimension;
+ *   - scales: e8m0 bytes (uint8 or float8_e8m0fnu), one per 32 contiguous
+ *     elements, row-major (rows, contraction / 32);
+ *   - group_end_offsets: int32 cumulative group ends (E,), device memory.
+ */
+#ifndef MXGG_H_
+#define MXGG_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MXGG_OK 0
+#define MXGG_ERR_INVALID 1     /* bad argument: shape, alignment, null pointer */
+#define MXGG_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define MXGG_ERR_UNSUPPORTED 3 /* valid request outside what this build handles */
+
+/* element types for inputs / outputs */
+#define MXGG_DTYPE_BF16 0
+#define MXGG_DTYPE_F16 1
+#define MXGG_DTYPE_F32 2
+
+/* quantiser modes */
+#define MXGG_QUANT_ROWS 0 /* blocks along the contiguous last dim (reference to_mx) */
+#define MXGG_QUANT_COLS 1 /* blocks along the leading dim, output transposed */
+
+/* scale layouts */
+#define MXGG_SCALE_ROW_MAJOR 0 /* (rows, cols/32), the reference layout */
+#define MXGG_SCALE_BLOCKED 1   /* 128x4 atoms (rows padded to 128, cols/32 to 4) */
+
+/*
+ * Forward / dgrad grouped GEMM: out[rows of group g] = A[rows] @ B[g]^T.
+ * Replaces triton_mxfp8_grouped_mm (reference kernels/forward.py:461-606).
+ *   a        (M, K) e4m3            a_scale (M, K/32) e8m0
+ *   b        (E, N, K) e4m3         b_scale (E, N, K/32) e8m0
+ *   group_end_offsets (E,) int32, device; group g owns rows
+ *            [offs[g-1], offs[g]) (offs[-1] := 0).  Any row boundaries work.
+ *   out      (M, N) of out_dtype (MXGG_DTYPE_BF16/F16/F32).  Rows at or past
+ *            offs[E-1] are not written (forward.py:583 leaves them unset).
+ * Requirements: K % 32 == 0; a, b 16-byte aligned; 1 <= E <= 256.
+ */
+int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                    const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
+                    void* out, int out_dtype, void* stream);
+
+/*
+ * Weight-gradient grouped GEMM: out[g] = GO_t[:, group g] @ X_t[:, group g]^T.
+ * Replaces triton_mxfp8_wgrad (reference kernels/backward.py:217-305).
+ *   go_t     (N, M) e4m3 (quantised along tokens)   go_scale (N, M/32)
+ *   ia_t     (K, M) e4m3 (quantised along tokens)   ia_scale (K, M/32)
+ *   group_end_offsets (E,) int32, device, multiples of 32 (the reference's
+ *            own requirement: a 32-token scale block never spans two groups)
+ *   out      (E, N, K) of out_dtype; empty groups produce zeros.
+ * Requirements: M % 32 == 0; go_t, ia_t 16-byte aligned; 1 <= E <= 256.
+ */
+int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+               const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
+               int out_dtype, void* stream);
+
+/*
+ * MX quantiser, FLOOR scaling, e4m3 elements, 32-element blocks.
+ * Bit-exact with the reference's to_mx (utils.py:67-105).
+ *   x        (rows, cols) of x_dtype, contiguous.
+ *   mode     MXGG_QUANT_ROWS: blocks along cols (cols % 32 == 0);
+ *              q (rows, cols), scales (rows, cols/32).
+ *            MXGG_QUANT_COLS: blocks along rows (rows % 32 == 0), output
+ *              transposed: q (cols, rows), scales (cols, rows/32) -- the
+ *              reference's to_mx(x.t().contiguous()) in one pass.
+ *   scale_layout MXGG_SCALE_ROW_MAJOR or MXGG_SCALE_BLOCKED (the caller
+ *              zero-fills the padding of a blocked buffer).
+ */
+int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
+                     int mode, int scale_layout, void* stream);
+
+/*
+ * Routing tables of the reference's _build_expt_data (forward.py:340-365),
+ * built on the device: out must hold 2*E + 1 + cdiv(M, block_m) + max(E-1, 0)
+ * int32: [hist (E) | start offsets (E) | total tiles (1) | tile map], tile
+ * map entries (block << 16) | group, or -1 past the last tile.
+ */
+int mxgg_build_tile_map(const int32_t* group_end_offsets, int64_t E, int64_t M, int32_t block_m, int32_t* out,
+                        void* stream);
+
+/* Tile configuration for later GEMM calls on this process: tile_n in
+ * {0 (auto), 128, 256}; group_m >= 1 rasterisation band (0 = auto). */
+int mxgg_set_tile_config(int32_t tile_n, int32_t group_m);
+
+/* Error bits raised by device-side bounded waits since the last clear
+ * (0 = none).  Synchronises `stream`.  clear != 0 resets the word. */
+int mxgg_device_status(uint32_t* status_out, int clear, void* stream);
+
+const char* mxgg_last_error(void);
+int32_t mxgg_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXGG_H_ */

@@ -1,0 +1,51 @@
+"""Shared helpers for the parity tests (the oracle is the checker only)."""
+import os
+import sys
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "grouped-gemms_b200"))
+sys.path.insert(0, ROOT)
+
+from oracle import mx_oracle as O  # noqa: E402
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().view(torch.uint8).cpu().numpy()
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 -> fp32 (round to nearest even)."""
+    return O.bf16_bits_to_f32(O.f32_to_bf16_bits(np.ascontiguousarray(x, dtype=np.float32)))
+
+
+def randn_bf16(shape, scale=1.0, seed=0, device="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(torch.bfloat16).to(device)
+
+
+def as_oracle_input(t: torch.Tensor) -> np.ndarray:
+    """Exact float32 values of a bf16/fp16/fp32 tensor."""
+    return t.detach().float().cpu().numpy()
+
+
+def quantize_ref(x: torch.Tensor):
+    """Oracle quantisation of a torch tensor: (scales u8, e4m3 bytes)."""
+    return O.to_mx(as_oracle_input(x))
+
+
+def offsets(E, M, multiple_of=32, seed=0):
+    import random
+    rng = random.Random(seed)
+    return O.generate_jagged_offs(E, M, multiple_of, rng=rng)
+
+
+def gpu_status_clear():
+    import mxgg
+    return mxgg.device_status(clear=True)

@@ -1,0 +1,96 @@
+"""The C ABI on a machine without a GPU: the library loads, exports every
+symbol include/mxgg.h declares, and rejects bad arguments before touching
+the device (no kernel launches here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from helpers import ROOT
+
+import mxgg
+from mxgg import _lib
+
+HEADER = os.path.join(ROOT, "include", "mxgg.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(mxgg_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_header_symbols():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert len(syms) >= 8
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in mxgg.h but not exported"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+    assert lib.mxgg_version() >= 1
+
+
+def _err(rc):
+    return rc, _lib.load().mxgg_last_error().decode()
+
+
+def test_grouped_mm_rejects_bad_contraction():
+    lib = _lib.load()
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 48, 1, ctypes.c_void_p(16), 0, None))
+    assert rc == 1 and "multiple of 32" in msg
+
+
+def test_grouped_mm_rejects_bad_dtype_and_groups():
+    lib = _lib.load()
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 7, None))
+    assert rc == 1 and "out_dtype" in msg
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 0, ctypes.c_void_p(16), 0, None))
+    assert rc == 1
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 300, ctypes.c_void_p(16), 0, None))
+    assert rc == 3 and "groups" in msg
+
+
+def test_grouped_mm_rejects_null_and_misaligned():
+    lib = _lib.load()
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None))
+    assert rc == 1 and "null" in msg
+    p = ctypes.c_void_p(0x1001)
+    rc, msg = _err(lib.mxgg_grouped_mm(p, p, p, p, p, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None))
+    assert rc == 1 and "aligned" in msg
+
+
+def test_wgrad_rejects_bad_tokens():
+    lib = _lib.load()
+    rc, msg = _err(lib.mxgg_wgrad(None, None, None, None, None, 64, 64, 40, 2, ctypes.c_void_p(16), 0, None))
+    assert rc == 1 and "multiple of 32" in msg
+
+
+def test_quantize_rejects_bad_shapes():
+    lib = _lib.load()
+    p = ctypes.c_void_p(0x1000)
+    rc, msg = _err(lib.mxgg_quantize_mx(p, 0, 4, 48, p, p, 0, 0, None))
+    assert rc == 1 and "multiple of 32" in msg
+    rc, msg = _err(lib.mxgg_quantize_mx(p, 0, 40, 64, p, p, 1, 0, None))
+    assert rc == 1 and "multiple of 32" in msg
+    rc, msg = _err(lib.mxgg_quantize_mx(p, 9, 32, 64, p, p, 0, 0, None))
+    assert rc == 1 and "x_dtype" in msg
+    rc, msg = _err(lib.mxgg_quantize_mx(p, 0, 32, 64, p, p, 0, 5, None))
+    assert rc == 1 and "layout" in msg
+
+
+def test_tile_config_validation():
+    lib = _lib.load()
+    assert lib.mxgg_set_tile_config(192, 0) == 1
+    assert lib.mxgg_set_tile_config(128, 8) == 0
+    assert lib.mxgg_set_tile_config(0, 0) == 0
+
+
+def test_no_cpu_fallback():
+    import torch
+    import utils
+    with pytest.raises(RuntimeError, match="CUDA"):
+        utils.to_mx(torch.randn(4, 64, dtype=torch.bfloat16))
+    import kernels
+    if not kernels._mxfp8_available:
+        with pytest.raises(NotImplementedError):
+            kernels.triton_mxfp8_grouped_mm(None, torch.empty(1, 1, 1), None, None, None)

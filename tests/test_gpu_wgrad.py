@@ -1,0 +1,141 @@
+"""Weight-gradient grouped GEMM on the GPU against the oracle.
+
+rel-L2 <= 1e-3 for bf16 outputs (compared after rounding the oracle to bf16),
+<= 1e-5 for fp32 outputs; empty groups must be exact zeros.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import O, bf16_round, f32, gpu_status_clear, offsets, u8
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K_():
+    import kernels
+    assert kernels._mxfp8_available
+    return kernels
+
+
+@pytest.fixture(scope="module")
+def U():
+    import utils
+    return utils
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    gpu_status_clear()
+    yield
+    assert gpu_status_clear() == 0, "a device-side wait timed out"
+
+
+def _inputs(M, N, K, seed):
+    import utils
+    g = torch.Generator().manual_seed(seed)
+    go = torch.randn(M, N, generator=g).to(torch.bfloat16).cuda()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    go_s, go_q = utils.to_mx_dim1(go)      # (N, M/32), (N, M)
+    ia_s, ia_q = utils.to_mx_dim1(x)       # (K, M/32), (K, M)
+    return go, x, go_s, go_q, ia_s, ia_q
+
+
+def _oracle(go_q, go_s, ia_q, ia_s, offs):
+    return O.wgrad(u8(go_q), u8(go_s), u8(ia_q), u8(ia_s), np.asarray(offs), acc=np.float32)
+
+
+def _check(out, ref, out_dtype):
+    if out_dtype == torch.float32:
+        err = O.rel_l2(f32(out), ref)
+        assert err <= 1e-5, err
+    else:
+        err = O.rel_l2(f32(out), bf16_round(ref))
+        assert err <= 1e-3, err
+
+
+def test_golden_small(K_, golden):
+    dev = lambda k, dt=torch.uint8: torch.from_numpy(golden[k]).cuda().view(dt)  # noqa: E731
+    out = K_.triton_mxfp8_wgrad(dev("wg_go_q", torch.float8_e4m3fn), dev("wg_go_s"),
+                                dev("wg_ia_q", torch.float8_e4m3fn), dev("wg_ia_s"),
+                                torch.from_numpy(golden["wg_offs"]).cuda(), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _check(out, golden["wg_out_f32"], torch.float32)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("E,M,N,K", [(1, 1024, 256, 512), (4, 2048, 384, 256), (8, 4096, 256, 768)])
+def test_random_vs_oracle(K_, out_dtype, E, M, N, K):
+    offs = offsets(E, M, 32, seed=E * 7 + K)
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=E)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    _check(out, _oracle(go_q, go_s, ia_q, ia_s, offs), out_dtype)
+
+
+def test_empty_and_unaligned_groups(K_):
+    # groups that start/end off the 128-token stage grid, and empty groups
+    E, M, N, K = 6, 1024, 256, 256
+    offs = [0, 32, 32, 480, 992, 1024]
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=5)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref = _oracle(go_q, go_s, ia_q, ia_s, offs)
+    _check(out, ref, torch.float32)
+    assert torch.count_nonzero(out[0]) == 0 and torch.count_nonzero(out[2]) == 0
+
+
+def test_tokens_not_multiple_of_128(K_):
+    # M % 128 != 0 -> scale rows are not 4-byte aligned: byte-gather path
+    E, M, N, K = 3, 544, 128, 256
+    offs = [96, 320, 544]
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=8)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _check(out, _oracle(go_q, go_s, ia_q, ia_s, offs), torch.float32)
+
+
+def test_matches_hp_sqnr(K_):
+    E, M, N, K = 4, 2048, 512, 512
+    offs = offsets(E, M, 32, seed=2)
+    go, x, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=2)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o)
+    ref = torch.zeros(E, N, K, device="cuda")
+    prev = 0
+    for g, e in enumerate(offs):
+        ref[g] = go[prev:e].float().t() @ x[prev:e].float()
+        prev = e
+    assert O.compute_error(f32(ref), f32(out)) >= 27.0
+
+
+def test_full_size_sampled(K_, U):
+    """Full Llama4 sweep shape E=8, N=K=8192 checked on sampled output rows."""
+    E, M, N, K = 8, 16640, 8192, 8192
+    offs = O.llama4_offsets(123)[35]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    go = torch.randn(M, N, device="cuda", dtype=torch.bfloat16, generator=g)
+    go_s, go_q = U.to_mx_dim1(go)
+    del go
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    ia_s, ia_q = U.to_mx_dim1(x)
+    del x
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(1)
+    rows = np.sort(rng.choice(N, 16, replace=False))
+    cols = np.sort(rng.choice(K, 64, replace=False))
+    rt, ct = torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()
+    GOd = O.dequant(u8(go_q[rt]), u8(go_s[rt])).astype(np.float32)       # (16, M)
+    IAd = O.dequant(u8(ia_q[ct]), u8(ia_s[ct])).astype(np.float32)       # (64, M)
+    got_all = f32(out[:, rt][:, :, ct])
+    prev = 0
+    for gi, e in enumerate(offs):
+        ref = GOd[:, prev:e] @ IAd[:, prev:e].T
+        assert O.rel_l2(got_all[gi], bf16_round(ref)) <= 1e-3
+        prev = e
