@@ -1,0 +1,515 @@
+#!/usr/bin/env python
+"""MXFP8 grouped-GEMM benchmark: TFLOPS geomean over the 36 Llama4 shapes x
+{forward, dgrad, wgrad} on B200, printed as one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mxgg|reference]
+
+* Shapes and offsets follow the reference bench (bench.py:113-122, 243-257):
+  E in {1,2,4,8}, M = 16640 tokens, N, K in {2048, 5120, 8192}; offsets from
+  ``generate_jagged_offs(E, M, 32)`` after ``random.seed(123)`` in the same
+  shape order.  Inputs are seeded synthetic bf16 ~N(0,1), quantised on the
+  GPU outside the timed region (the reference times the GEMM only).
+* One step = one pass over all 108 (shape, pass) GEMMs.  Each launch is
+  preceded by an L2 flush (a 512 MiB memset, outside the events) and
+  bracketed by CUDA events on the launching stream.
+* TFLOPS = 2*M*N*K / t per (shape, pass) (bench.py:200); ``value`` is the
+  geomean over the 108 points, summed over ranks for N > 1 (each rank runs
+  the full sweep on its own GPU: weak scaling, replicas).
+* ``e2e``: the same geomean measured through the public entry points with
+  host (pinned) inputs: H2D of the fp8 operands, scales and offsets, the GEMM,
+  and D2H of the output, all inside the events.
+* ``--impl reference``: the reference's CPU path (dequantise + per-group fp32
+  matmul, the oracle restatement -- the reference's Triton kernels are
+  ROCm-only) timed on this host's cores over a bounded sample.
+"""
+
+import argparse
+import json
+import math
+import os
+import random
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "grouped-gemms_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "MXFP8 grouped-GEMM TFLOPS geomean, 36 shapes fwd/dgrad/wgrad, % of B200 peak"
+NOMINAL_MXFP8_TFLOPS = 4500.0
+M_TOKENS = 16640
+
+
+def llama4_shapes():
+    return [(e, M_TOKENS, n, k) for e in (1, 2, 4, 8) for n in (2048, 5120, 8192) for k in (2048, 5120, 8192)]
+
+
+def geomean(xs):
+    xs = [x for x in xs if x > 0 and math.isfinite(x)]
+    return math.exp(sum(math.log(x) for x in xs) / len(xs)) if xs else float("nan")
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ inputs
+def build_problems(device, shapes, passes, seed=123):
+    """Quantised operands for every (shape, pass); offsets as the reference draws them."""
+    import torch
+    import utils
+
+    random.seed(seed)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    probs = []
+    for (E, M, N, K) in shapes:
+        offs = utils.generate_jagged_offs(E, M, multiple_of=32, device=device)
+        A = torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=gen)
+        W = torch.randn(E, N, K, device=device, dtype=torch.bfloat16, generator=gen)
+        G = torch.randn(M, N, device=device, dtype=torch.bfloat16, generator=gen)
+        if "fwd" in passes:
+            a_s, a_q = utils.to_mx(A)
+            b_s, b_q = utils.to_mx(W)
+            probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K,
+                              args=(a_q, b_q, a_s, b_s, offs)))
+        if "dgrad" in passes:
+            g_s, g_q = utils.to_mx(G)                                  # along N
+            wt = [utils.to_mx_dim1(W[e]) for e in range(E)]            # W[e]^T (K, N), along N
+            wt_s = torch.stack([s for s, _ in wt])
+            wt_q = torch.stack([q for _, q in wt])
+            probs.append(dict(pass_="dgrad", shape=(E, M, N, K), flops=2.0 * M * N * K,
+                              args=(g_q, wt_q, g_s, wt_s, offs)))
+        if "wgrad" in passes:
+            go_s, go_q = utils.to_mx_dim1(G)                           # (N, M), along tokens
+            ia_s, ia_q = utils.to_mx_dim1(A)                           # (K, M), along tokens
+            probs.append(dict(pass_="wgrad", shape=(E, M, N, K), flops=2.0 * M * N * K,
+                              args=(go_q, go_s, ia_q, ia_s, offs)))
+        del A, W, G
+    torch.cuda.synchronize()
+    return probs
+
+
+def run_problem(p):
+    import kernels
+    if p["pass_"] == "wgrad":
+        return kernels.triton_mxfp8_wgrad(*p["args"])
+    return kernels.triton_mxfp8_grouped_mm(*p["args"])
+
+
+# ------------------------------------------------------------------ peaks
+def measured_mxfp8_ceiling(device):
+    """cuBLAS MXFP8 dense GEMM (torch._scaled_mm, 8192^3, e8m0 1x32 scales),
+    best of 10 -- the MXFP8 tensor ceiling of this GPU in this run."""
+    import torch
+    import utils
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=device, dtype=torch.bfloat16)
+        b = torch.randn(n, n, device=device, dtype=torch.bfloat16)
+        sa, qa = utils.to_mx_blocked_scales(a)
+        sb, qb = utils.to_mx_blocked_scales(b)
+        sa = sa.view(torch.float8_e8m0fnu)
+        sb = sb.view(torch.float8_e8m0fnu)
+        fn = lambda: torch._scaled_mm(qa, qb.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)  # noqa: E731
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e) * 1e-3)
+        return {"tflops": round(2 * n ** 3 / best / 1e12, 1), "how": "torch._scaled_mm MXFP8 8192^3, best of 10"}
+    except Exception as exc:  # pragma: no cover - reported, not fatal
+        return {"tflops": None, "how": f"torch._scaled_mm MXFP8 unavailable: {type(exc).__name__}: {exc}"[:200]}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+# ------------------------------------------------------------------ CPU arm
+class CpuReferenceSample:
+    """The reference's CPU path (dequantise, per-group fp32 matmul) over a
+    bounded sample of the sweep: three (E, N, K) shapes x three passes with the
+    token dimension cut to 2048 (group sizes drawn the same way).  Inputs are
+    quantised once; each timed run dequantises and multiplies."""
+
+    SHAPES = [(1, 2048, 2048), (2, 5120, 2048), (4, 2048, 5120)]
+    TOKENS = 2048
+
+    def __init__(self, threads=None):
+        import numpy as np
+        from oracle import mx_oracle as O
+        if threads:
+            try:
+                import threadpoolctl
+                threadpoolctl.threadpool_limits(threads)
+            except Exception:
+                pass
+        self.O, self.np = O, np
+        rng = np.random.default_rng(0)
+        Ms = self.TOKENS
+        self.points = []
+        for (E, N, K) in self.SHAPES:
+            offs = O.generate_jagged_offs(E, Ms, 32, rng=random.Random(E))
+            for pass_ in ("fwd", "dgrad", "wgrad"):
+                if pass_ == "fwd":
+                    a, b = rng.standard_normal((Ms, K)), rng.standard_normal((E, N, K))
+                elif pass_ == "dgrad":
+                    a, b = rng.standard_normal((Ms, N)), rng.standard_normal((E, K, N))
+                else:
+                    a, b = rng.standard_normal((N, Ms)), rng.standard_normal((K, Ms))
+                a_s, a_q = O.to_mx(a.astype(np.float32))
+                b_s, b_q = O.to_mx(b.astype(np.float32))
+                self.points.append((pass_, 2.0 * Ms * N * K, (a_q, a_s, b_q, b_s, offs)))
+
+    def describe(self):
+        return (f"{len(self.points)} (shape, pass) points: (E,N,K) in {self.SHAPES} x fwd/dgrad/wgrad, "
+                f"tokens cut to {self.TOKENS}; dequantise + per-group fp32 matmul (numpy oracle restatement)")
+
+    def run(self):
+        tf = []
+        for pass_, flops, (a_q, a_s, b_q, b_s, offs) in self.points:
+            t0 = time.perf_counter()
+            if pass_ == "wgrad":
+                self.O.wgrad(a_q, a_s, b_q, b_s, offs, acc=self.np.float32)
+            else:
+                self.O.grouped_mm(a_q, a_s, b_q, b_s, offs, acc=self.np.float32)
+            tf.append(flops / (time.perf_counter() - t0) / 1e12)
+        return geomean(tf)
+
+
+def gpu_smi_id(dev):
+    """nvidia-smi -i accepts the GPU UUID, which survives CUDA_VISIBLE_DEVICES remapping."""
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return str(dev.index or 0)
+
+
+def quantize_bandwidth(dev, hbm_gbs):
+    """to_mx over a full sweep operand (16640 x 8192 bf16), L2 flushed, median of 20."""
+    import torch
+    import utils
+    x = torch.randn(M_TOKENS, 8192, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        utils.to_mx(x)
+    ts = []
+    for _ in range(20):
+        utils.flush_l2(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        utils.to_mx(x)
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e) * 1e-3)
+    t = sorted(ts)[len(ts) // 2]
+    nbytes = x.numel() * 2 + x.numel() + x.numel() // 32
+    gbs = nbytes / t / 1e9
+    return {"bound": "hbm", "kernel": "mxgg::quantize_rows_e4m3", "achieved": round(gbs, 1), "peak": hbm_gbs,
+            "unit": "GB/s", "frac": round(gbs / hbm_gbs, 4), "us": round(t * 1e6, 1),
+            "algorithmic_bytes": nbytes}
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count()
+
+
+# ------------------------------------------------------------------ main arms
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def allreduce_max(vals, world):
+    import torch
+    if world == 1:
+        return vals
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def time_problems(probs, steps, warmup, world, flush):
+    """Per-problem mean device time (s) over `steps` timed steps."""
+    import torch
+    n = len(probs)
+    for _ in range(warmup):
+        for p in probs:
+            flush()
+            run_problem(p)
+    barrier(world)
+    starts = [[torch.cuda.Event(enable_timing=True) for _ in range(n)] for _ in range(steps)]
+    ends = [[torch.cuda.Event(enable_timing=True) for _ in range(n)] for _ in range(steps)]
+    barrier(world)
+    step_s = torch.cuda.Event(enable_timing=True)
+    step_e = torch.cuda.Event(enable_timing=True)
+    step_s.record()
+    for s in range(steps):
+        for i, p in enumerate(probs):
+            flush()
+            starts[s][i].record()
+            run_problem(p)
+            ends[s][i].record()
+    step_e.record()
+    barrier(world)
+    per = [sum(starts[s][i].elapsed_time(ends[s][i]) for s in range(steps)) / steps * 1e-3 for i in range(n)]
+    wall_ms = step_s.elapsed_time(step_e) / steps
+    return per, wall_ms
+
+
+def time_e2e(probs, steps, warmup, world):
+    """Same sweep through the public API with pinned host inputs/outputs."""
+    import torch
+    max_in = max(sum(t.numel() * t.element_size() for t in p["args"]) for p in probs)
+    host_in = torch.empty(max_in + 4096 * 8, dtype=torch.uint8, pin_memory=True)
+    per = []
+    h2d_total, d2h_total = 0, 0
+    for p in probs:
+        # stage this problem's inputs in pinned host memory (untimed)
+        host_views, off = [], 0
+        for t in p["args"]:
+            nb = t.numel() * t.element_size()
+            hv = host_in[off:off + nb]
+            hv.copy_(t.contiguous().view(torch.uint8).reshape(-1))
+            host_views.append((hv, t.shape, t.dtype))
+            off += (nb + 511) // 512 * 512
+        dev_args = [torch.empty(shape, dtype=dt, device="cuda") for (_, shape, dt) in host_views]
+        out_like = run_problem(p)
+        host_out = torch.empty(out_like.shape, dtype=out_like.dtype, pin_memory=True)
+        del out_like
+        q = dict(p)
+        q["args"] = tuple(dev_args)
+        ts = []
+        for it in range(warmup + steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for (hv, shape, dt), d in zip(host_views, dev_args):
+                d.view(torch.uint8).reshape(-1).copy_(hv, non_blocking=True)
+            out = run_problem(q)
+            host_out.copy_(out, non_blocking=True)
+            e.record()
+            torch.cuda.synchronize()
+            if it >= warmup:
+                ts.append(s.elapsed_time(e) * 1e-3)
+        per.append(sum(ts) / len(ts))
+        h2d_total += sum(hv.numel() for hv, _, _ in host_views)
+        d2h_total += host_out.numel() * host_out.element_size()
+        del dev_args, host_out
+    per = allreduce_max(per, world)
+    return per, h2d_total, d2h_total
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mxgg", choices=["mxgg", "reference"])
+    ap.add_argument("--passes", default="fwd,dgrad,wgrad")
+    ap.add_argument("--shapes", default="all", help="'all' or comma list of shape indices 0..35")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip e2e, the CPU sample, the cuBLAS ceiling and the quantiser line (profiling runs)")
+    ap.add_argument("--detail", action="store_true", help="also print one JSON line per (shape, pass) to stderr")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    passes = [p for p in args.passes.split(",") if p]
+    shapes = llama4_shapes()
+    idx = list(range(36)) if args.shapes == "all" else [int(i) for i in args.shapes.split(",")]
+    cfg = {"workload": "llama4-36-shapes x {" + ",".join(passes) + "}", "shapes": len(idx), "M": M_TOKENS,
+           "E": [1, 2, 4, 8], "N": [2048, 5120, 8192], "K": [2048, 5120, 8192], "offs": "generate_jagged_offs(seed 123, multiple_of 32)",
+           "l2": "flushed (512 MiB memset) before every timed launch", "parallelism": f"replicas x{args.gpus}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        threads = cpu_cores()
+        ref = CpuReferenceSample(threads=threads)
+        vals = []
+        for it in range(args.warmup + args.steps):
+            v = ref.run()
+            if it >= args.warmup:
+                vals.append(v)
+        v = sum(vals) / len(vals)
+        line = {"metric": METRIC, "value": round(v, 4), "unit": "TFLOPS", "impl": "reference", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "e4m3xe4m3->f32", "data": "synthetic", "config": cfg,
+                "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                                 "sample": ref.describe()},
+                "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    world, rank, local = dist_setup(args)
+    import mxgg
+    import utils
+    dev = torch.device("cuda", torch.cuda.current_device())
+    mxgg.device_status(clear=True)
+
+    probs = build_problems(dev, [shapes[i] for i in idx], passes)
+    utils.flush_l2(dev)
+    flush = lambda: utils.flush_l2(dev)  # noqa: E731
+
+    with ClockSampler(gpu_smi_id(dev)) as clk:
+        per, wall_ms = time_problems(probs, args.steps, args.warmup, world, flush)
+    per = allreduce_max(per, world)
+    status = mxgg.device_status(clear=True)
+
+    tf = [p["flops"] / t / 1e12 for p, t in zip(probs, per)]
+    by_pass = {ps: round(geomean([x for x, p in zip(tf, probs) if p["pass_"] == ps]), 1) for ps in passes}
+    gm = geomean(tf)
+    total_flops = sum(p["flops"] for p in probs)
+    total_time = sum(per)
+    achieved = total_flops / total_time / 1e12
+
+    e2e = None
+    if args.no_extras:
+        args.no_e2e = args.no_cpu = True
+    if not args.no_e2e:
+        per_e, h2d, d2h = time_e2e(probs, max(1, min(args.steps, 3)), 1, world)
+        e2e = {"value": round(world * geomean([p["flops"] / t / 1e12 for p, t in zip(probs, per_e)]), 1),
+               "unit": "TFLOPS", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    if rank == 0 and args.detail:
+        for p, t in zip(probs, per):
+            print(json.dumps({"pass": p["pass_"], "shape": p["shape"], "us": round(t * 1e6, 1),
+                              "tflops": round(p["flops"] / t / 1e12, 1)}), file=sys.stderr)
+
+    ceiling = measured_mxfp8_ceiling(dev) if rank == 0 and not args.no_extras else None
+    peaks, peaks_src = load_peaks()
+    traffic = load_traffic()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        ref = CpuReferenceSample(threads=cpu_cores())
+        ref.run()
+        cpu = {"value": round(ref.run(), 4), "unit": "TFLOPS", "cores": cpu_cores(), "kind": "port",
+               "sample": ref.describe()}
+    quant = quantize_bandwidth(dev, peaks.get("hbm_gbs", 6650.0)) if rank == 0 and not args.no_extras else None
+
+    if rank == 0:
+        peak = ceiling["tflops"] if ceiling and ceiling["tflops"] else 2.0 * peaks.get("bf16_tflops", 1590.0)
+        roof = {"bound": "tensor", "kernel": "mxgg::grouped_gemm_kernel", "achieved": round(achieved, 1),
+                "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": (ceiling["how"] if ceiling and ceiling["tflops"] else
+                                f"2 x bf16 {peaks_src} ({ceiling['how'] if ceiling else ''})"),
+                "frac_of_nominal_4500": round(achieved / NOMINAL_MXFP8_TFLOPS, 4),
+                "traffic": traffic.get("grouped_gemm_bytes_per_launch")}
+        line = {"metric": METRIC, "value": round(world * gm, 1), "unit": "TFLOPS", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_time * 1e3, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "e4m3xe4m3->f32 (bf16 out)", "data": "synthetic", "config": cfg,
+                "per_pass_geomean": by_pass, "pct_of_nominal_peak": round(100 * gm / NOMINAL_MXFP8_TFLOPS, 2),
+                "pct_of_measured_mxfp8": round(100 * gm / peak, 2),
+                "roofline": roof, "quantize_roofline": quant, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": len(probs) * args.steps, "clocks": clk.summary(),
+                "device_status": status, "wall_ms_per_step": round(wall_ms, 3)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier(world)
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
