@@ -209,7 +209,21 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.out_ld = out_cols;
   p.out_rows = out_rows;
   p.out_cols = (int)out_cols;
-  p.sf_fast = (C % 128 == 0) && aligned(a_scale, 4) && aligned(b_scale, 4);
+  {
+    // widest aligned scale gather: a stage's 4 scale bytes per row are one
+    // 4-byte word; a load may cover 4, 2 or 1 consecutive stages
+    const int64_t row_bytes = C / 32;
+    int vec = 0;
+    if (C % 128 == 0) {
+      for (int v : {4, 2, 1}) {
+        if (row_bytes % (4 * v) == 0 && aligned(a_scale, 4 * v) && aligned(b_scale, 4 * v)) {
+          vec = v;
+          break;
+        }
+      }
+    }
+    p.sf_vec = vec;
+  }
   const int es = out_esize(out_dtype);
   p.tma_store = aligned(out, 16) && ((out_cols * es) % 16 == 0);
   p.group_m = g_group_m > 0 ? g_group_m : 16;

@@ -13,10 +13,11 @@
 //   warp 0      TMA producer: A and B tiles (128 B swizzle) into a STAGES ring
 //   warp 1      MMA issuer: tcgen05.cp of the scales into TMEM, then
 //               tcgen05.mma.kind::mxf8f6f4.block_scale (M=128, N=BN, K=32)
-//   warp 2      scale gatherer: cp.async 4-byte gathers that turn the caller's
-//               row-major (rows, contraction/32) scales into the 128x4 scale
-//               atom layout tcgen05.cp expects -- no separate re-layout pass
-//   warp 3      prologue only (group table)
+//   warps 2-3   scale gatherers (A side, B side): vector loads of the
+//               caller's row-major (rows, contraction/32) scales, transposed
+//               in registers into the 128x4 scale atom layout tcgen05.cp
+//               expects -- no separate re-layout pass over HBM
+//   warp 3      also builds the group table in the prologue
 //   warps 4-7   epilogue: TMEM -> registers -> bf16/fp32 -> swizzled smem ->
 //               TMA store; ragged group edges fall back to predicated stores
 //
@@ -67,7 +68,7 @@ struct GemmParams {
   long long out_ld;          // elements per output row
   long long out_rows;        // rows of the output tensor
   int out_cols;              // valid output columns (fwd: N, wgrad: K)
-  int sf_fast;               // 1: 4-byte cp.async scale gathers are aligned
+  int sf_vec;                // scale gather width in 4-byte words (4, 2, 1), 0 = byte gathers
   int tma_store;             // 1: output rows are 16-byte aligned for TMA stores
   int group_m;               // rasterisation band (m-tiles) for the forward pass
   uint32_t* status;          // error word (device memory), 0 = ok
@@ -226,11 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
-  static_assert(ACC * BN + 4 + BN / 32 <= kTmemCols, "tensor memory budget");
+  static_assert(ACC * BN + 2 * (4 + BN / 32) <= kTmemCols, "tensor memory budget");
   using S = SmemLayout<BN, STAGES, OutT>;
   constexpr int kEpiCols = S::kEpiCols;
-  constexpr int kSfaCol = ACC * BN;
-  constexpr int kSfbCol = ACC * BN + 4;
+  constexpr int kSfaCol = ACC * BN;            // two scale buffers follow the accumulators
+  constexpr uint32_t kSfCols = 4 + BN / 32;
   constexpr uint32_t kStageBytes = (kBM + BN) * kBK;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------------------------------------ prologue
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&sm->full[s]), 1 + 32);
+      ptx::mbar_init(ptx::smem_u32(&sm->full[s]), 3);   // TMA producer + two scale gatherers
       ptx::mbar_init(ptx::smem_u32(&sm->empty[s]), 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -317,6 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdesc = ptx::idesc_mxf8(kBM, BN, 0, 0);
+      constexpr uint32_t kAStep = (kBM * kBK) >> 4;     // descriptor start-address step per stage
+      constexpr uint32_t kBStep = (BN * kBK) >> 4;
+      const uint64_t adesc0 = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->a[0]));
+      const uint64_t bdesc0 = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->b[0]));
+      const uint64_t sfadesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfa[0]));
+      const uint64_t sfbdesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfb[0]));
       uint32_t it = 0, ai = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x, ++ai) {
@@ -331,31 +338,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         uint32_t accumulate = 0;
         for (int s = 0; s < u.st_count; ++s, ++it) {
-          const int stage = it % STAGES;
+          const uint32_t stage = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!ptx::mbar_wait(ptx::smem_u32(&sm->full[stage]), ph, abort)) {
             raise_error(p, abort, kErrMmaWait);
             ok = false;
             break;
           }
-          ptx::fence_proxy_async_smem();   // scales were gathered through the generic proxy
-          ptx::tc_fence_after();
-          const uint32_t sfa_t = tmem_base + kSfaCol;
-          const uint32_t sfb_t = tmem_base + kSfbCol;
-          ptx::tc_cp_32x128b_warpx4(sfa_t, ptx::sf_copy_desc(ptx::smem_u32(sm->sfa[stage])));
+          // scale factors of this stage -> TMEM (double-buffered so the copy
+          // never waits on the previous stage's MMAs)
+          const uint32_t sfa_t = tmem_base + kSfaCol + (it & 1u) * kSfCols;
+          const uint32_t sfb_t = sfa_t + 4;
+          ptx::tc_cp_32x128b_warpx4(sfa_t, sfadesc0 + (uint64_t)(stage * ((kBM * 4) >> 4)));
 #pragma unroll
           for (int b = 0; b < BN / 128; ++b)
-            ptx::tc_cp_32x128b_warpx4(sfb_t + 4 * b, ptx::sf_copy_desc(ptx::smem_u32(sm->sfb[stage]) + 512 * b));
-          const uint64_t adesc = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->a[stage]));
-          const uint64_t bdesc = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->b[stage]));
+            ptx::tc_cp_32x128b_warpx4(sfb_t + 4 * b, sfbdesc0 + (uint64_t)(stage * ((BN * 4) >> 4) + b * (512 >> 4)));
+          const uint64_t adesc = adesc0 + (uint64_t)(stage * kAStep);
+          const uint64_t bdesc = bdesc0 + (uint64_t)(stage * kBStep);
           const int base = (u.st_begin + s) * kBK;
           const int j0 = max(0, (u.c_begin - base) / 32);
           const int j1 = min(4, (u.c_end - base + 31) / 32);
-          for (int j = j0; j < j1; ++j) {
-            ptx::tc_mma_mxf8(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j),
-                             ptx::idesc_with_sf(kIdesc, j, j), sfa_t | (uint32_t(j) << 30),
-                             sfb_t | (uint32_t(j) << 30), accumulate);
+          if (j0 == 0 && j1 == 4) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              ptx::tc_mma_mxf8(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j),
+                               ptx::idesc_with_sf(kIdesc, j, j), sfa_t | (uint32_t(j) << 30),
+                               sfb_t | (uint32_t(j) << 30), (j == 0) ? accumulate : 1u);
+            }
             accumulate = 1;
+          } else {
+            for (int j = j0; j < j1; ++j) {
+              ptx::tc_mma_mxf8(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j),
+                               ptx::idesc_with_sf(kIdesc, j, j), sfa_t | (uint32_t(j) << 30),
+                               sfb_t | (uint32_t(j) << 30), accumulate);
+              accumulate = 1;
+            }
           }
           ptx::tc_commit(ptx::smem_u32(&sm->empty[stage]));
         }
@@ -367,72 +384,94 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int never = 0;
       if (!ptx::mbar_wait(ptx::smem_u32(&sm->drain), 0, &never)) atomicOr(p.status, kErrDrain);
     }
-  } else if (warp == 2) {
+  } else if (warp == 2 || warp == 3) {
     // -------------------------------------------------------- scale gather
+    // Warp 2 gathers the A-side scales, warp 3 the B-side ones, from the
+    // caller's row-major (rows, contraction/32) layout into the 128x4 atom
+    // layout tcgen05.cp reads: atom byte (r % 32) * 16 + (r / 32) * 4 + k.
+    // Lane l owns rows l + 32 i; one vector load per row fetches the scales of
+    // kVec consecutive stages, and a register transpose turns four rows into
+    // the lane's 16-byte atom row.  Each stage is fenced into the async proxy
+    // by the writers and published with one arrive, so the MMA thread never
+    // fences.
+    const bool side_a = (warp == 2);
+    constexpr int kMaxRows = BN / 32;                 // rows per lane on the B side (A side: 4)
+    const int nrows_lane = side_a ? 4 : kMaxRows;
+    const uint8_t* sf = side_a ? p.sfa : p.sfb;
+    const int rows_total = side_a ? p.rows_a : p.rows_b;
+    const int vec = p.sf_vec;                        // words per load: 4, 2, 1; 0 = byte gathers
+    const int G = vec > 0 ? vec : 1;                 // stages per load
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x) {
       const Unit u = decode_unit<BN>(sm, p, t);
-      for (int s = 0; s < u.st_count; ++s, ++it) {
-        const int stage = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1u;
-        if (!ptx::mbar_wait(ptx::smem_u32(&sm->empty[stage]), ph ^ 1u, abort)) {
-          raise_error(p, abort, kErrScaleWait);
-          ok = false;
-          break;
+      const int rbase = side_a ? u.a_row : u.b_row;
+      const uint8_t* rowp[kMaxRows];
+#pragma unroll
+      for (int i = 0; i < kMaxRows; ++i) {
+        const int row = min(max(rbase + lane + 32 * i, 0), rows_total - 1);
+        rowp[i] = sf + (long long)row * p.sf_ld;
+      }
+      int s = 0;
+      while (s < u.st_count && ok) {
+        const int st0 = u.st_begin + s;
+        const int cst = st0 - st0 % G;               // first stage of the loaded chunk
+        const int cend = min(cst + G, u.st_begin + u.st_count);
+        uint32_t w[kMaxRows][4];
+#pragma unroll
+        for (int i = 0; i < kMaxRows; ++i) {
+          if (i < nrows_lane) {
+            const uint8_t* q = rowp[i] + 4LL * cst;
+            if (vec == 4) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
+              w[i][0] = v.x; w[i][1] = v.y; w[i][2] = v.z; w[i][3] = v.w;
+            } else if (vec == 2) {
+              const uint2 v = __ldg(reinterpret_cast<const uint2*>(q));
+              w[i][0] = v.x; w[i][1] = v.y; w[i][2] = 0; w[i][3] = 0;
+            } else if (vec == 1) {
+              w[i][0] = __ldg(reinterpret_cast<const uint32_t*>(q)); w[i][1] = w[i][2] = w[i][3] = 0;
+            } else {
+              uint32_t x = 0;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const long long cc = 4LL * cst + j;
+                const uint32_t b = (cc < p.sf_ld) ? (uint32_t)__ldg(rowp[i] + cc) : 127u;
+                x |= b << (8 * j);
+              }
+              w[i][0] = x; w[i][1] = w[i][2] = w[i][3] = 0;
+            }
+          }
         }
-        const long long col = (long long)(u.st_begin + s) * (kBK / 32);
-        const uint32_t fb = ptx::smem_u32(&sm->full[stage]);
-        const uint32_t sa = ptx::smem_u32(sm->sfa[stage]) + lane * 16;
-        const uint32_t sb = ptx::smem_u32(sm->sfb[stage]) + lane * 16;
-        if (p.sf_fast) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int row = min(max(u.a_row + lane + 32 * c, 0), p.rows_a - 1);
-            ptx::cp_async_4(sa + 4 * c, p.sfa + (long long)row * p.sf_ld + col);
+        for (int st = st0; st < cend; ++st, ++s, ++it) {
+          const int stage = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!ptx::mbar_wait(ptx::smem_u32(&sm->empty[stage]), ph ^ 1u, abort)) {
+            raise_error(p, abort, kErrScaleWait);
+            ok = false;
+            break;
           }
+          const int wi = st - cst;
+          const uint32_t dst = (side_a ? ptx::smem_u32(sm->sfa[stage]) : ptx::smem_u32(sm->sfb[stage])) + lane * 16;
 #pragma unroll
-          for (int b = 0; b < BN / 128; ++b) {
+          for (int a = 0; a < kMaxRows / 4; ++a) {
+            if (4 * a < nrows_lane) {
+              uint32_t x[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int row = min(max(u.b_row + 128 * b + lane + 32 * c, 0), p.rows_b - 1);
-              ptx::cp_async_4(sb + 512 * b + 4 * c, p.sfb + (long long)row * p.sf_ld + col);
-            }
-          }
-          ptx::cp_async_mbar_arrive_noinc(fb);
-        } else {
-          const long long ncols = p.sf_ld;
-          auto gather = [&](const uint8_t* base, int row) -> uint32_t {
-            uint32_t w = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const long long cc = col + j;
-              const uint32_t v = (cc < ncols) ? (uint32_t)__ldg(base + (long long)row * p.sf_ld + cc) : 127u;
-              w |= v << (8 * j);
-            }
-            return w;
-          };
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int row = min(max(u.a_row + lane + 32 * c, 0), p.rows_a - 1);
-            const uint32_t w = gather(p.sfa, row);
-            asm volatile("st.shared.u32 [%0], %1;" ::"r"(sa + 4 * c), "r"(w) : "memory");
-          }
-#pragma unroll
-          for (int b = 0; b < BN / 128; ++b) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int row = min(max(u.b_row + 128 * b + lane + 32 * c, 0), p.rows_b - 1);
-              const uint32_t w = gather(p.sfb, row);
-              asm volatile("st.shared.u32 [%0], %1;" ::"r"(sb + 512 * b + 4 * c), "r"(w) : "memory");
+              for (int c = 0; c < 4; ++c) {
+                const uint32_t* r = w[4 * a + c];
+                x[c] = (wi == 0) ? r[0] : (wi == 1) ? r[1] : (wi == 2) ? r[2] : r[3];
+              }
+              asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 512 * a), "r"(x[0]), "r"(x[1]),
+                           "r"(x[2]), "r"(x[3])
+                           : "memory");
             }
           }
           ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive(fb);
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&sm->full[stage]));
         }
       }
     }
-    ptx::cp_async_wait_all();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lane quarter this warp may access
@@ -506,13 +545,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (lane < rows_here && grow < p.out_rows) {
           OutT* dst = reinterpret_cast<OutT*>(p.out) + grow * p.out_ld + col0;
           const int ncols = min(kEpiCols, p.out_cols - col0);
-          const OutT* srcv = reinterpret_cast<const OutT*>(w);
           if (ncols == kEpiCols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
             uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
             for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          } else if constexpr (sizeof(OutT) == 4) {
+            uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (j < ncols) d[j] = w[j];
           } else {
-            for (int j = 0; j < ncols; ++j) dst[j] = srcv[j];
+            uint16_t* d = reinterpret_cast<uint16_t*>(dst);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) d[j] = (uint16_t)(w[j >> 1] >> ((j & 1) * 16));
           }
         }
       }
