@@ -14,6 +14,7 @@
 #include "../../include/mxgg.h"
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
+#include "scale_pack.cuh"
 #include "tile_map.cuh"
 
 namespace mxgg {
@@ -50,6 +51,7 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
+int g_tile_m = 0;
 int g_tile_n = 0;
 int g_group_m = 0;
 
@@ -118,44 +120,98 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
   }
 }
 
-template <int BN, int STAGES, int ACC, typename OutT>
-int launch_gemm_t(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                  const GemmParams& p, long long max_units, cudaStream_t stream) {
-  using S = SmemLayout<BN, STAGES, OutT>;
+struct Maps {
+  CUtensorMap a, b, sfa, sfb, out;
+};
+
+template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
+int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units,
+                  cudaStream_t stream) {
+  using S = SmemLayout<BN, STAGES, PAIR, OutT>;
   constexpr size_t kSmem = sizeof(S) + 1024;
   static_assert(kSmem <= 232448, "shared memory budget");
-  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, OutT>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, PAIR, OutT>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   MXGG_CUDA_TRY(cudaGetDevice(&dev));
   if (!attr_done[dev]) {
     MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    if (PAIR > 1) MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
     attr_done[dev] = true;
   }
-  const long long grid = std::max(1LL, std::min<long long>(st.num_sms, max_units));
-  kern<<<(unsigned)grid, kThreads, kSmem, stream>>>(ta, tb, to, p);
-  MXGG_CUDA_TRY(cudaGetLastError());
+  const long long units = std::max(1LL, std::min<long long>(st.num_sms / PAIR, max_units));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(units * PAIR), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.sfa, m.sfb, m.out, p));
   return MXGG_OK;
 }
 
-template <int BN, int STAGES, int ACC>
-int launch_gemm_bn(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                   const GemmParams& p, long long max_units, int out_dtype, cudaStream_t stream) {
+template <int BN, int STAGES, int ACC, int PAIR>
+int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
+                    cudaStream_t stream) {
   switch (out_dtype) {
-    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, __half>(st, ta, tb, to, p, max_units, stream);
-    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, float>(st, ta, tb, to, p, max_units, stream);
-    default: return launch_gemm_t<BN, STAGES, ACC, __nv_bfloat16>(st, ta, tb, to, p, max_units, stream);
+    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, PAIR, __half>(st, m, p, max_units, stream);
+    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, PAIR, float>(st, m, p, max_units, stream);
+    default: return launch_gemm_t<BN, STAGES, ACC, PAIR, __nv_bfloat16>(st, m, p, max_units, stream);
   }
 }
 
-int pick_tile_n(int64_t n_extent) {
-  if (g_tile_n == 128 || g_tile_n == 256) return g_tile_n;
-  return n_extent >= 256 ? 256 : 128;
+// Packed-scale workspace of one GEMM call: [A atoms | B atoms], each part
+// 1 KiB aligned.  Sized for the larger of the two tile heights so a size
+// query does not depend on the tile configuration chosen at launch.
+struct WsPlan {
+  long long a_subtiles, b_tiles, stages, a_bytes, b_bytes, total;
+};
+
+WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int tile_m, int tile_n) {
+  WsPlan w{};
+  const int64_t C = mode == kFwd ? K : M;
+  w.stages = (C + kBK - 1) / kBK;
+  if (mode == kFwd) {
+    w.a_subtiles = ((M + tile_m - 1) / tile_m + (E - 1)) * (tile_m / kBM);
+    w.b_tiles = E * ((N + tile_n - 1) / tile_n);
+  } else {
+    w.a_subtiles = ((N + tile_m - 1) / tile_m) * (tile_m / kBM);
+    w.b_tiles = (K + tile_n - 1) / tile_n;
+  }
+  w.a_bytes = (w.a_subtiles * w.stages * 512 + 1023) / 1024 * 1024;
+  w.b_bytes = (w.b_tiles * w.stages * (tile_n / 128) * 512 + 1023) / 1024 * 1024;
+  w.total = w.a_bytes + w.b_bytes;
+  return w;
+}
+
+int64_t workspace_upper_bound(int mode, int64_t M, int64_t N, int64_t K, int64_t E) {
+  int64_t best = 0;
+  for (int tm : {128, 256})
+    for (int tn : {128, 256}) best = std::max<int64_t>(best, plan_workspace(mode, M, N, K, E, tm, tn).total);
+  return best;
+}
+
+struct TileChoice {
+  int tile_m;   // 128: one CTA per tile; 256: a CTA pair per tile
+  int tile_n;   // 128 or 256
+};
+
+TileChoice pick_tiles(int64_t n_extent) {
+  TileChoice c;
+  c.tile_m = (g_tile_m == 128 || g_tile_m == 256) ? g_tile_m : 256;
+  c.tile_n = (g_tile_n == 128 || g_tile_n == 256) ? g_tile_n : (n_extent >= 256 ? 256 : 128);
+  return c;
 }
 
 int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const void* b_scale,
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
-             void* stream_v) {
+             void* workspace, int64_t workspace_bytes, void* stream_v) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   const char* what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (out_dtype != MXGG_DTYPE_BF16 && out_dtype != MXGG_DTYPE_F16 && out_dtype != MXGG_DTYPE_F32)
@@ -191,7 +247,48 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   DeviceState* st = nullptr;
   if (int rc = get_device_state(&st)) return rc;
 
-  const int bn = pick_tile_n(out_cols);
+  const TileChoice tc = pick_tiles(out_cols);
+  const int bn = tc.tile_n;
+  const int pair = tc.tile_m / kBM;
+  const WsPlan ws = plan_workspace(mode, M, N, K, E, tc.tile_m, bn);
+  if (!workspace || workspace_bytes < ws.total || !aligned(workspace, 1024))
+    return fail(MXGG_ERR_INVALID, "%s: workspace of %lld bytes (1 KiB aligned) required, got %lld at %p", what,
+                (long long)ws.total, (long long)workspace_bytes, workspace);
+  uint8_t* ws_a = static_cast<uint8_t*>(workspace);
+  uint8_t* ws_b = ws_a + ws.a_bytes;
+
+  // 1) pack the row-major scales into the atoms the GEMM loads
+  {
+    PackParams pp{};
+    pp.mode = mode;
+    pp.E = (int)E;
+    pp.M = (int)M;
+    pp.N = (int)N;
+    pp.K = (int)K;
+    pp.tile_m = tc.tile_m;
+    pp.tile_n = bn;
+    pp.stages = (int)ws.stages;
+    pp.offs = offs;
+    pp.sfa = static_cast<const uint8_t*>(a_scale);
+    pp.sfb = static_cast<const uint8_t*>(b_scale);
+    pp.rows_a = (int)rows_a;
+    pp.rows_b = (int)rows_b;
+    pp.sf_ld = C / 32;
+    const int64_t ld = C / 32;
+    if (ld % 16 == 0 && aligned(a_scale, 16) && aligned(b_scale, 16)) pp.vec = 4;
+    else if (ld % 4 == 0 && aligned(a_scale, 4) && aligned(b_scale, 4)) pp.vec = 1;
+    else pp.vec = 0;
+    pp.a_subtiles = (int)ws.a_subtiles;
+    pp.b_tiles = (int)ws.b_tiles;
+    pp.a_out = ws_a;
+    pp.b_out = ws_b;
+    const long long chunks = (ws.stages + 3) / 4;
+    const long long warps = (ws.a_subtiles + ws.b_tiles * (bn / 128)) * chunks;
+    const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
+    pack_scales_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pp);
+    MXGG_CUDA_TRY(cudaGetLastError());
+  }
+
   GemmParams p{};
   p.mode = mode;
   p.E = (int)E;
@@ -202,57 +299,52 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.rows_b = (int)rows_b;
   p.contraction = (int)C;
   p.offs = offs;
-  p.sfa = static_cast<const uint8_t*>(a_scale);
-  p.sfb = static_cast<const uint8_t*>(b_scale);
-  p.sf_ld = C / 32;
+  p.stages = (int)ws.stages;
   p.out = out;
   p.out_ld = out_cols;
   p.out_rows = out_rows;
   p.out_cols = (int)out_cols;
-  {
-    // widest aligned scale gather: a stage's 4 scale bytes per row are one
-    // 4-byte word; a load may cover 4, 2 or 1 consecutive stages
-    const int64_t row_bytes = C / 32;
-    int vec = 0;
-    if (C % 128 == 0) {
-      for (int v : {4, 2, 1}) {
-        if (row_bytes % (4 * v) == 0 && aligned(a_scale, 4 * v) && aligned(b_scale, 4 * v)) {
-          vec = v;
-          break;
-        }
-      }
-    }
-    p.sf_vec = vec;
-  }
   const int es = out_esize(out_dtype);
   p.tma_store = aligned(out, 16) && ((out_cols * es) % 16 == 0);
   p.group_m = g_group_m > 0 ? g_group_m : 16;
   p.status = st->status;
 
-  CUtensorMap ta, tb, to;
-  if (int rc = make_tmap_2d(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
+  Maps maps;
+  if (int rc = make_tmap_2d(&maps.a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
                             kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = make_tmap_2d(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C, (uint64_t)C,
-                            kBK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C, (uint64_t)C,
+                            kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_tmap_2d(&maps.sfa, ws_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                            (uint64_t)(ws.a_subtiles * ws.stages * 4), 128, 128, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  if (int rc = make_tmap_2d(&maps.sfb, ws_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                            (uint64_t)(ws.b_tiles * ws.stages * 4 * (bn / 128)), 128, 128, 128, 4 * (bn / 128),
+                            CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   if (p.tma_store) {
-    if (int rc = make_tmap_2d(&to, out, out_tmap_dtype(out_dtype), es, (uint64_t)out_rows, (uint64_t)out_cols,
+    if (int rc = make_tmap_2d(&maps.out, out, out_tmap_dtype(out_dtype), es, (uint64_t)out_rows, (uint64_t)out_cols,
                               (uint64_t)out_cols, 64 / es, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return rc;
   } else {
-    std::memset(&to, 0, sizeof(to));
+    std::memset(&maps.out, 0, sizeof(maps.out));
   }
 
   long long max_units;
+  const int tile_m = tc.tile_m;
   if (mode == kFwd) {
-    const long long mt_ub = (M + kBM - 1) / kBM + (E - 1);
+    const long long mt_ub = (M + tile_m - 1) / tile_m + (E - 1);
     max_units = mt_ub * ((N + bn - 1) / bn);
   } else {
-    max_units = E * ((N + kBM - 1) / kBM) * ((K + bn - 1) / bn);
+    max_units = E * ((N + tile_m - 1) / tile_m) * ((K + bn - 1) / bn);
   }
-  if (bn == 256) return launch_gemm_bn<256, 4, 1>(*st, ta, tb, to, p, max_units, out_dtype, stream);
-  return launch_gemm_bn<128, 6, 2>(*st, ta, tb, to, p, max_units, out_dtype, stream);
+  if (pair == 2) {
+    if (bn == 256) return launch_gemm_cfg<256, 6, 2, 2>(*st, maps, p, max_units, out_dtype, stream);
+    return launch_gemm_cfg<128, 8, 2, 2>(*st, maps, p, max_units, out_dtype, stream);
+  }
+  if (bn == 256) return launch_gemm_cfg<256, 4, 2, 1>(*st, maps, p, max_units, out_dtype, stream);
+  return launch_gemm_cfg<128, 6, 2, 1>(*st, maps, p, max_units, out_dtype, stream);
 }
 
 }  // namespace
@@ -262,16 +354,28 @@ using namespace mxgg;
 
 extern "C" {
 
+int64_t mxgg_grouped_mm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t E) {
+  if (M < 0 || N < 0 || K < 0 || E < 1) return -1;
+  return workspace_upper_bound(kFwd, M, N, K, E);
+}
+
+int64_t mxgg_wgrad_workspace_size(int64_t N, int64_t K, int64_t M, int64_t E) {
+  if (M < 0 || N < 0 || K < 0 || E < 1) return -1;
+  return workspace_upper_bound(kWgrad, M, N, K, E);
+}
+
 int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
                     const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E, void* out,
-                    int out_dtype, void* stream) {
-  return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, stream);
+                    int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
+                  workspace_bytes, stream);
 }
 
 int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
                const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
-               int out_dtype, void* stream) {
-  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, stream);
+               int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
+                  workspace_bytes, stream);
 }
 
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales, int mode,
@@ -351,11 +455,14 @@ int mxgg_build_tile_map(const int32_t* offs, int64_t E, int64_t M, int32_t block
   return MXGG_OK;
 }
 
-int mxgg_set_tile_config(int32_t tile_n, int32_t group_m) {
+int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m) {
+  if (tile_m != 0 && tile_m != 128 && tile_m != 256)
+    return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: tile_m must be 0, 128 or 256");
   if (tile_n != 0 && tile_n != 128 && tile_n != 256)
     return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: tile_n must be 0, 128 or 256");
   if (group_m < 0) return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: group_m must be >= 0");
   std::lock_guard<std::mutex> lk(g_mu);
+  g_tile_m = tile_m;
   g_tile_n = tile_n;
   g_group_m = group_m;
   return MXGG_OK;

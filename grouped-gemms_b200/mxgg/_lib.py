@@ -22,11 +22,13 @@ _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
 _int = ctypes.c_int
 SIGNATURES = {
-    "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
-    "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
+    "mxgg_grouped_mm_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
+    "mxgg_wgrad_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
+    "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
+    "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
-    "mxgg_set_tile_config": (_int, [_i32, _i32]),
+    "mxgg_set_tile_config": (_int, [_i32, _i32, _i32]),
     "mxgg_device_status": (_int, [ctypes.POINTER(ctypes.c_uint32), _int, _vp]),
     "mxgg_last_error": (ctypes.c_char_p, []),
     "mxgg_version": (_i32, []),
@@ -73,5 +75,7 @@ def device_status(clear: bool = True, stream=None) -> int:
     return v.value
 
 
-def set_tile_config(tile_n: int = 0, group_m: int = 0) -> None:
-    check(load().mxgg_set_tile_config(tile_n, group_m), "mxgg_set_tile_config")
+def set_tile_config(tile_m: int = 0, tile_n: int = 0, group_m: int = 0) -> None:
+    """Tile shape for later GEMM calls (0 = automatic): tile_m 128 (one CTA)
+    or 256 (a CTA pair), tile_n 128 or 256, group_m the rasterisation band."""
+    check(load().mxgg_set_tile_config(tile_m, tile_n, group_m), "mxgg_set_tile_config")

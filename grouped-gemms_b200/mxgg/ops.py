@@ -33,6 +33,15 @@ def _require_cuda(*ts: Tensor, what: str) -> None:
             raise RuntimeError(f"{what}: mxgg runs only on CUDA (sm_100a) tensors; got a {t.device} tensor")
 
 
+def _workspace(nbytes: int, device: torch.device) -> Tensor:
+    """Scratch for one GEMM call from torch's caching allocator (1 KiB aligned)."""
+    if nbytes < 0:
+        raise ValueError("mxgg: invalid GEMM sizes")
+    buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=device)
+    off = (-buf.data_ptr()) % 1024
+    return buf[off:off + nbytes] if nbytes else buf[:0]
+
+
 def as_u8(t: Tensor) -> Tensor:
     """Scales may be uint8 or float8_e8m0fnu (reference forward.py:534-535)."""
     return t if t.dtype == torch.uint8 else t.view(torch.uint8)
@@ -94,10 +103,12 @@ def grouped_mm_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: 
     b_scale = as_u8(b_scale).contiguous()
     offs = offs.to(torch.int32).contiguous()
     out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    lib = _lib.load()
+    ws = _workspace(lib.mxgg_grouped_mm_workspace_size(M, N, K, E), a.device)
     with torch.cuda.device(a.device):
-        _lib.check(_lib.load().mxgg_grouped_mm(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
-                                               M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype],
-                                               _stream(a.device)), "mxgg_grouped_mm")
+        _lib.check(lib.mxgg_grouped_mm(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
+                                       M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(),
+                                       _stream(a.device)), "mxgg_grouped_mm")
     return out
 
 
@@ -122,10 +133,12 @@ def wgrad_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, off
     ia_scale = as_u8(ia_scale).contiguous()
     offs = offs.to(torch.int32).contiguous()
     out = torch.empty((E, N, K), dtype=out_dtype, device=go_t.device)
+    lib = _lib.load()
+    ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
-        _lib.check(_lib.load().mxgg_wgrad(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
-                                          N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _stream(go_t.device)),
-                   "mxgg_wgrad")
+        _lib.check(lib.mxgg_wgrad(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
+                                  N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(),
+                                  _stream(go_t.device)), "mxgg_wgrad")
     return out
 
 

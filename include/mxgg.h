@@ -5,7 +5,8 @@
  * the two grouped-GEMM entry points and the MX quantiser.  Every function
  * takes plain device pointers, element counts and a CUDA stream passed as
  * `void*` (a cudaStream_t / CUstream; NULL = legacy default stream), enqueues
- * its work on that stream, never synchronises and never allocates.
+ * its work on that stream, never synchronises and never allocates: scratch
+ * memory a call needs is passed in by the caller (see *_workspace_size).
  * All functions return MXGG_OK (0) or an error code; mxgg_last_error()
  * returns a message for the calling thread's last failure.
  *
@@ -45,6 +46,18 @@ extern "C" {
 #define MXGG_SCALE_BLOCKED 1   /* 128x4 atoms (rows padded to 128, cols/32 to 4) */
 
 /*
+ * Scratch ("workspace") for one grouped-GEMM call: the row-major scales are
+ * re-laid into the 128x4 atoms the tensor cores read, one atom per 128-row
+ * slab and 128-element contraction stage (the reference re-lays its scales on
+ * every call too, forward.py:537-561).  Returns the bytes to pass as
+ * `workspace_bytes` (1 KiB-aligned device memory), or -1 for bad sizes.
+ * The workspace is scratch: its contents need not survive between calls, and
+ * calls that run concurrently need separate workspaces.
+ */
+int64_t mxgg_grouped_mm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t E);
+int64_t mxgg_wgrad_workspace_size(int64_t N, int64_t K, int64_t M, int64_t E);
+
+/*
  * Forward / dgrad grouped GEMM: out[rows of group g] = A[rows] @ B[g]^T.
  * Replaces triton_mxfp8_grouped_mm (reference kernels/forward.py:461-606).
  *   a        (M, K) e4m3            a_scale (M, K/32) e8m0
@@ -53,11 +66,12 @@ extern "C" {
  *            [offs[g-1], offs[g]) (offs[-1] := 0).  Any row boundaries work.
  *   out      (M, N) of out_dtype (MXGG_DTYPE_BF16/F16/F32).  Rows at or past
  *            offs[E-1] are not written (forward.py:583 leaves them unset).
+ *   workspace  >= mxgg_grouped_mm_workspace_size(M, N, K, E) bytes.
  * Requirements: K % 32 == 0; a, b 16-byte aligned; 1 <= E <= 256.
  */
 int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
                     const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
-                    void* out, int out_dtype, void* stream);
+                    void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Weight-gradient grouped GEMM: out[g] = GO_t[:, group g] @ X_t[:, group g]^T.
@@ -67,11 +81,12 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
  *   group_end_offsets (E,) int32, device, multiples of 32 (the reference's
  *            own requirement: a 32-token scale block never spans two groups)
  *   out      (E, N, K) of out_dtype; empty groups produce zeros.
+ *   workspace  >= mxgg_wgrad_workspace_size(N, K, M, E) bytes.
  * Requirements: M % 32 == 0; go_t, ia_t 16-byte aligned; 1 <= E <= 256.
  */
 int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
                const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
-               int out_dtype, void* stream);
+               int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * MX quantiser, FLOOR scaling, e4m3 elements, 32-element blocks.
@@ -97,9 +112,10 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
 int mxgg_build_tile_map(const int32_t* group_end_offsets, int64_t E, int64_t M, int32_t block_m, int32_t* out,
                         void* stream);
 
-/* Tile configuration for later GEMM calls on this process: tile_n in
- * {0 (auto), 128, 256}; group_m >= 1 rasterisation band (0 = auto). */
-int mxgg_set_tile_config(int32_t tile_n, int32_t group_m);
+/* Tile configuration for later GEMM calls on this process (0 = automatic):
+ * tile_m in {128 (one CTA per tile), 256 (a CTA pair per tile)},
+ * tile_n in {128, 256}, group_m >= 1 rasterisation band in m-tiles. */
+int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m);
 
 /* Error bits raised by device-side bounded waits since the last clear
  * (0 = none).  Synchronises `stream`.  clear != 0 resets the word. */

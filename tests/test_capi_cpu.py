@@ -36,32 +36,32 @@ def _err(rc):
 
 def test_grouped_mm_rejects_bad_contraction():
     lib = _lib.load()
-    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 48, 1, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 48, 1, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 1 and "multiple of 32" in msg
 
 
 def test_grouped_mm_rejects_bad_dtype_and_groups():
     lib = _lib.load()
-    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 7, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 7, None, 0, None))
     assert rc == 1 and "out_dtype" in msg
-    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 0, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 0, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 1
-    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 300, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 300, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 3 and "groups" in msg
 
 
 def test_grouped_mm_rejects_null_and_misaligned():
     lib = _lib.load()
-    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(None, None, None, None, None, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 1 and "null" in msg
     p = ctypes.c_void_p(0x1001)
-    rc, msg = _err(lib.mxgg_grouped_mm(p, p, p, p, p, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_grouped_mm(p, p, p, p, p, 64, 64, 64, 1, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 1 and "aligned" in msg
 
 
 def test_wgrad_rejects_bad_tokens():
     lib = _lib.load()
-    rc, msg = _err(lib.mxgg_wgrad(None, None, None, None, None, 64, 64, 40, 2, ctypes.c_void_p(16), 0, None))
+    rc, msg = _err(lib.mxgg_wgrad(None, None, None, None, None, 64, 64, 40, 2, ctypes.c_void_p(16), 0, None, 0, None))
     assert rc == 1 and "multiple of 32" in msg
 
 
@@ -78,11 +78,22 @@ def test_quantize_rejects_bad_shapes():
     assert rc == 1 and "layout" in msg
 
 
+def test_workspace_size_query():
+    lib = _lib.load()
+    # A atoms for every 128-row slab x 128-element stage plus the B atoms, 1 KiB aligned
+    n = lib.mxgg_grouped_mm_workspace_size(16640, 8192, 8192, 8)
+    assert n > 0 and n % 1024 == 0
+    assert n >= (16640 // 128 + 7) * 64 * 512 + 8 * 8192 // 128 * 64 * 512
+    assert lib.mxgg_grouped_mm_workspace_size(-1, 8, 8, 1) == -1
+    assert lib.mxgg_wgrad_workspace_size(256, 256, 1024, 4) > 0
+
+
 def test_tile_config_validation():
     lib = _lib.load()
-    assert lib.mxgg_set_tile_config(192, 0) == 1
-    assert lib.mxgg_set_tile_config(128, 8) == 0
-    assert lib.mxgg_set_tile_config(0, 0) == 0
+    assert lib.mxgg_set_tile_config(0, 192, 0) == 1
+    assert lib.mxgg_set_tile_config(64, 128, 0) == 1
+    assert lib.mxgg_set_tile_config(256, 128, 8) == 0
+    assert lib.mxgg_set_tile_config(0, 0, 0) == 0
 
 
 def test_no_cpu_fallback():

@@ -97,19 +97,19 @@ def test_reference_shapes_sqnr(K_, U, E, M, N, K):
     _check(out, _oracle(a_q, a_s, b_q, b_s, offs), torch.bfloat16)
 
 
-@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("tile_m,tile_n", [(128, 128), (128, 256), (256, 128), (256, 256)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
-def test_tile_configs_and_dtypes(K_, tile_n, out_dtype):
+def test_tile_configs_and_dtypes(K_, tile_m, tile_n, out_dtype):
     import mxgg
     E, M, N, K = 3, 700, 512, 384
     offs = [96, 96 + 352, 700]
     _, _, a_s, a_q, b_s, b_q, o = _make(E, M, N, K, offs, seed=3)
-    mxgg.set_tile_config(tile_n, 0)
+    mxgg.set_tile_config(tile_m, tile_n, 0)
     try:
         out = K_.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, o, out_dtype=out_dtype)
         torch.cuda.synchronize()
     finally:
-        mxgg.set_tile_config(0, 0)
+        mxgg.set_tile_config(0, 0, 0)
     ref = _oracle(a_q, a_s, b_q, b_s, o)
     if out_dtype == torch.float16:
         valid = ~np.isnan(ref)
@@ -154,10 +154,14 @@ def test_edge_cases(K_, case):
     out = torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda")
     from mxgg import _lib
     lib = _lib.load()
+    wsb = lib.mxgg_grouped_mm_workspace_size(M, N, K, E)
+    ws = torch.empty(wsb + 1024, dtype=torch.uint8, device="cuda")
+    wp = ws.data_ptr() + (-ws.data_ptr()) % 1024
     rc = lib.mxgg_grouped_mm(ctypes.c_void_p(a_q.data_ptr()), ctypes.c_void_p(b_q.data_ptr()),
                              ctypes.c_void_p(a_s.data_ptr()), ctypes.c_void_p(b_s.data_ptr()),
                              ctypes.c_void_p(o.data_ptr()), M, N, K, E, ctypes.c_void_p(out.data_ptr()),
-                             _lib.DTYPE_BF16, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+                             _lib.DTYPE_BF16, ctypes.c_void_p(wp), wsb,
+                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "mxgg_grouped_mm")
     torch.cuda.synchronize()
     ref = _oracle(a_q, a_s, b_q, b_s, o)
