@@ -251,8 +251,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   const int bn = tc.tile_n;
   const int pair = tc.tile_m / kBM;
   const WsPlan ws = plan_workspace(mode, M, N, K, E, tc.tile_m, bn);
-  if (!workspace || workspace_bytes < ws.total || !aligned(workspace, 1024))
-    return fail(MXGG_ERR_INVALID, "%s: workspace of %lld bytes (1 KiB aligned) required, got %lld at %p", what,
+  if (!workspace || workspace_bytes < ws.total || !aligned(workspace, 256))
+    return fail(MXGG_ERR_INVALID, "%s: workspace of %lld bytes (256-byte aligned) required, got %lld at %p", what,
                 (long long)ws.total, (long long)workspace_bytes, workspace);
   uint8_t* ws_a = static_cast<uint8_t*>(workspace);
   uint8_t* ws_b = ws_a + ws.a_bytes;

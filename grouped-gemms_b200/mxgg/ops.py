@@ -34,12 +34,12 @@ def _require_cuda(*ts: Tensor, what: str) -> None:
 
 
 def _workspace(nbytes: int, device: torch.device) -> Tensor:
-    """Scratch for one GEMM call from torch's caching allocator (1 KiB aligned)."""
+    """Scratch for one GEMM call from torch's caching allocator (256-byte aligned)."""
     if nbytes < 0:
         raise ValueError("mxgg: invalid GEMM sizes")
-    buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=device)
-    off = (-buf.data_ptr()) % 1024
-    return buf[off:off + nbytes] if nbytes else buf[:0]
+    buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+    off = (-buf.data_ptr()) % 256
+    return buf[off:off + nbytes]
 
 
 def as_u8(t: Tensor) -> Tensor:

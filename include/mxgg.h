@@ -50,7 +50,7 @@ extern "C" {
  * re-laid into the 128x4 atoms the tensor cores read, one atom per 128-row
  * slab and 128-element contraction stage (the reference re-lays its scales on
  * every call too, forward.py:537-561).  Returns the bytes to pass as
- * `workspace_bytes` (1 KiB-aligned device memory), or -1 for bad sizes.
+ * `workspace_bytes` (256-byte aligned device memory), or -1 for bad sizes.
  * The workspace is scratch: its contents need not survive between calls, and
  * calls that run concurrently need separate workspaces.
  */
