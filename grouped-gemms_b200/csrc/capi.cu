@@ -347,6 +347,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   return launch_gemm_cfg<128, 6, 2, 1>(*st, maps, p, max_units, out_dtype, stream);
 }
 
+// Scratch of mxgg_grouped_mm_noalloc: a fixed array in device memory that
+// every GPU which loads this library holds until the process exits.  Host
+// code cannot use the name `g_noalloc_scratch` as an address (on the host it
+// is only a stand-in object); the device address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+constexpr int64_t kNoAllocScratchBytes = 32ll << 20;   // 32 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDevices] = {};
+
 }  // namespace
 }  // namespace mxgg
 
@@ -369,6 +378,35 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
                     int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
                   workspace_bytes, stream);
+}
+
+int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                            const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
+                            void* out, int out_dtype, void* stream) {
+  if (M >= 0 && N >= 0 && K >= 0 && E >= 1) {
+    const int64_t need = workspace_upper_bound(kFwd, M, N, K, E);
+    if (need > kNoAllocScratchBytes)
+      return fail(MXGG_ERR_UNSUPPORTED,
+                  "mxgg_grouped_mm_noalloc: this problem needs %lld bytes of scratch, more than the %lld-byte "
+                  "static array; call mxgg_grouped_mm with a workspace instead",
+                  (long long)need, (long long)kNoAllocScratchBytes);
+  }
+  int dev = 0;
+  MXGG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(MXGG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_noalloc_ptr[dev]) {
+      // first call on this device: resolve the array's device address
+      void* p = nullptr;
+      MXGG_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      g_noalloc_ptr[dev] = p;
+    }
+    ws = g_noalloc_ptr[dev];
+  }
+  return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, ws,
+                  kNoAllocScratchBytes, stream);
 }
 
 int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,

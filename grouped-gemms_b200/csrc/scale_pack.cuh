@@ -74,7 +74,6 @@ __device__ __forceinline__ void load_row_words(const uint8_t* row, const PackPar
 // row it writes for each stage, so every atom store is a coalesced 512 B.
 __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
   __shared__ int s_start[kMaxGroups];
-  __shared__ int s_end[kMaxGroups];
   __shared__ int s_cum[kMaxGroups + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (p.mode == kFwd) {
@@ -102,7 +101,6 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
         }
         if (i < p.E) {
           s_start[i] = prev;
-          s_end[i] = v;
           s_cum[i] = carry_sum + incl - t;
         }
         carry_max = __shfl_sync(0xffffffffu, v, 31);

@@ -74,6 +74,29 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
                     void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Forward / dgrad grouped GEMM that allocates nothing and takes no workspace.
+ * No counterpart in the reference: it exists for callers that cannot get
+ * device memory at call time -- code running where the allocator must not be
+ * entered (a runtime that reserved all device memory up front, an inference
+ * server or plugin host that forbids allocation after start-up, a
+ * latency-critical loop that must not risk cudaMalloc's implicit device
+ * synchronisation) and that cannot hold a workspace of its own.
+ * Same arguments and results as mxgg_grouped_mm minus the workspace.  Its
+ * scratch is one fixed 32 MiB array in device memory that every GPU loading
+ * this library keeps until the process exits; problems whose scratch exceeds
+ * it (mxgg_grouped_mm_workspace_size > 32 MiB) are rejected with
+ * MXGG_ERR_UNSUPPORTED.  The first call on a device resolves the array's
+ * address on that device (the device must be current); make that first call
+ * before any stream capture.  All calls share the array, which keeps the last
+ * call's contents (nothing in it needs to start zeroed: each call rewrites
+ * what it reads): calls whose work overlaps on the GPU, e.g. on two streams,
+ * race on it and must be serialised by the caller.
+ */
+int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                            const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
+                            void* out, int out_dtype, void* stream);
+
+/*
  * Weight-gradient grouped GEMM: out[g] = GO_t[:, group g] @ X_t[:, group g]^T.
  * Replaces triton_mxfp8_wgrad (reference kernels/backward.py:217-305).
  *   go_t     (N, M) e4m3 (quantised along tokens)   go_scale (N, M/32)
