@@ -109,6 +109,7 @@ struct SmemLayout {
   int g_start[kMaxGroups];
   int g_end[kMaxGroups];
   int g_cum[kMaxGroups + 1];
+  int g_order[kMaxGroups];   // wgrad: groups by decreasing token count
 };
 
 __device__ __forceinline__ int cdiv_i(int a, int b) { return (a + b - 1) / b; }
@@ -152,6 +153,28 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
   if (lane == 0) sm->g_cum[p.E] = carry_sum;
 }
 
+// wgrad work per tile is proportional to the group's token count: visit the
+// largest groups first so that the snake-ordered static schedule
+// (unit_at) spreads big and small tiles evenly over the CTAs.
+template <class S>
+__device__ __forceinline__ void build_group_order(S* sm, int E) {
+  const int lane = ptx::lane_id();
+  for (int i = lane; i < E; i += 32) {
+    const int si = sm->g_end[i] - sm->g_start[i];
+    int rank = 0;
+    for (int j = 0; j < E; ++j) {
+      const int sj = sm->g_end[j] - sm->g_start[j];
+      rank += (sj > si) || (sj == si && j < i);
+    }
+    sm->g_order[rank] = i;
+  }
+}
+
+// k-th unit of the CTA (pair) `i` of `P`: rounds of P consecutive units,
+// alternately dealt forwards and backwards, so the costliest units of every
+// round do not always land on the same CTAs.
+__device__ __forceinline__ int unit_at(int k, int i, int P) { return k * P + ((k & 1) ? (P - 1 - i) : i); }
+
 template <int BN, int TILE_M, class S>
 __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, int t) {
   Unit u;
@@ -187,8 +210,9 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
   } else {
     const int NT = cdiv_i(p.N, TILE_M);
     const int KT = cdiv_i(p.K, BN);
-    const int g = t / (NT * KT);
-    const int r = t - g * NT * KT;
+    const int gi = t / (NT * KT);
+    const int g = sm->g_order[gi];
+    const int r = t - gi * NT * KT;
     const int nt = r / KT;
     const int kt = r - nt * KT;
     const int s = sm->g_start[g], e = sm->g_end[g];
@@ -316,6 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 3) {
     build_group_table(sm, p, p.M, kTileM);   // fwd: rows of A; wgrad: tokens
     __syncwarp();
+    if (p.mode == kWgrad) {
+      build_group_order(sm, p.E);
+      __syncwarp();
+    }
     if (lane == 0) {
       if (p.mode == kFwd)
         sm->num_units = sm->g_cum[p.E] * cdiv_i(p.N, BN);
@@ -336,7 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = unit0; t < num_units && ok; t += unit_stride) {
+      for (int k = 0; ok; ++k) {
+        const int t = unit_at(k, unit0, unit_stride);
+        if (t >= num_units) break;
         const Unit u = decode_unit<BN, kTileM>(sm, p, t);
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const int stage = it % STAGES;
@@ -389,7 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t sfbdesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfb[0]));
       uint32_t it = 0, ai = 0;
       bool ok = true;
-      for (int t = unit0; t < num_units && ok; t += unit_stride, ++ai) {
+      for (int k = 0; ok; ++k, ++ai) {
+        const int t = unit_at(k, unit0, unit_stride);
+        if (t >= num_units) break;
         const Unit u = decode_unit<BN, kTileM>(sm, p, t);
         const int acc = ai & 1;
         const uint32_t aph = (ai >> 1) & 1u;
@@ -470,7 +502,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     uint32_t ai = 0;
     int buf = 0;
-    for (int t = unit0; t < num_units; t += unit_stride, ++ai) {
+    for (int k = 0;; ++k, ++ai) {
+      const int t = unit_at(k, unit0, unit_stride);
+      if (t >= num_units) break;
       const Unit u = decode_unit<BN, kTileM>(sm, p, t);
       const int acc = ai & 1;
       const uint32_t aph = (ai >> 1) & 1u;
