@@ -70,7 +70,7 @@ struct GemmParams {
   int out_cols;              // valid output columns (fwd: N, wgrad: K)
   int stages;                // 128-element contraction stages of the packed scales
   int tma_store;             // 1: output rows are 16-byte aligned for TMA stores
-  int group_m;               // rasterisation band (m-tiles) for the forward pass
+  int group_m;               // rasterisation band in row tiles (row tile fastest inside a band)
   uint32_t* status;          // error word (device memory), 0 = ok
 };
 
@@ -212,9 +212,16 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     const int KT = cdiv_i(p.K, BN);
     const int gi = t / (NT * KT);
     const int g = sm->g_order[gi];
+    // inside a group: bands of group_m row tiles (of GO_t), row tile fastest,
+    // as in the forward pass
     const int r = t - gi * NT * KT;
-    const int nt = r / KT;
-    const int kt = r - nt * KT;
+    const int gm = p.group_m;
+    const int band = r / (gm * KT);
+    const int rb = r - band * gm * KT;
+    const int m0 = band * gm;
+    const int gsz = min(gm, NT - m0);
+    const int kt = rb / gsz;
+    const int nt = m0 + (rb - kt * gsz);
     const int s = sm->g_start[g], e = sm->g_end[g];
     u.a_row = nt * TILE_M;
     u.b_row = kt * BN;
