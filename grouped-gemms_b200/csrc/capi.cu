@@ -448,7 +448,7 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
   if (mode == MXGG_QUANT_ROWS) {
     if (cols % 32 != 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: cols=%lld not a multiple of 32", (long long)cols);
     const long long work = rows * cols / 8;
-    const long long blocks = std::max(1LL, std::min<long long>((work + nthreads - 1) / nthreads, (long long)st->num_sms * 16));
+    const long long blocks = std::max(1LL, std::min<long long>((work + nthreads - 1) / nthreads, (long long)st->num_sms * 8));
     switch (x_dtype) {
       case MXGG_DTYPE_BF16:
         quantize_rows_e4m3<__nv_bfloat16><<<(unsigned)blocks, nthreads, 0, stream>>>(

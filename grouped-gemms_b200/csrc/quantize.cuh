@@ -91,6 +91,28 @@ __device__ __forceinline__ uint32_t e4m3_byte(float x, float mult) {
 
 __device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
 
+// Eight inputs of one 32-block -> eight e4m3 bytes (two words).  Blocks
+// without NaN (amax bit pattern <= +inf) take the paired conversion: the
+// satfinite cvt saturates exactly like the reference's clamp to +-448 followed
+// by the cast (an infinite input lands on 448 too).  A block holding a NaN
+// converts element by element so each NaN keeps its sign.
+__device__ __forceinline__ uint2 e4m3x8(const float (&f)[8], float mult, uint32_t amax_bits) {
+  if (amax_bits <= 0x7F800000u) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(f[2 * k] * mult, f[2 * k + 1] * mult), __NV_SATFINITE,
+                                                __NV_E4M3);
+    return make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+  }
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) lo |= e4m3_byte(f[k], mult) << (8 * k);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) hi |= e4m3_byte(f[4 + k], mult) << (8 * k);
+  return make_uint2(lo, hi);
+}
+
 // offset of scale (r, c) of a (R, C) scale matrix in the blocked atom layout
 __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c, long long C) {
   const long long cb = (C + 3) / 4;
@@ -100,44 +122,57 @@ __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c,
 
 // -------------------------------------------------------------- row mode
 // x: (R, C) contiguous, C % 32 == 0.  q: (R, C) e4m3.  s: scales.
+// Each thread handles kUnroll 8-element slots a grid-stride apart and issues
+// all their loads before converting, so kUnroll 16-byte loads are in flight.
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ x, long long R, long long C,
                                                           uint8_t* __restrict__ q, uint8_t* __restrict__ s,
                                                           int scale_layout) {
-  const long long total8 = R * C / 8;
+  constexpr int kUnroll = 4;
+  const long long total8 = R * C / 8;                  // a multiple of 4: a 32-block never straddles slots
   const long long stride = (long long)gridDim.x * blockDim.x;
   const int lane = threadIdx.x & 31;
   const long long SC = C / 32;
-  // every thread of a warp runs the same number of iterations (the shuffles
+  // every lane of a warp runs the same number of iterations (the shuffles
   // need the whole quad), so iterate over warp-rounded ranges
   const long long total8_w = (total8 + 31) / 32 * 32;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total8_w; i += stride) {
-    const bool live = i < total8;
-    float f[8];
-    uint32_t m = 0;
-    if (live) {
-      load8<T>(x + i * 8, f);
+  for (long long base = (long long)blockIdx.x * blockDim.x + threadIdx.x; base < total8_w;
+       base += kUnroll * stride) {
+    float f[kUnroll][8];
+    uint32_t m[kUnroll];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m = max(m, abs_bits(f[k]));
-    }
-    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    if (!live) continue;
-    const uint32_t sc = floor_scale(m, 8);
-    const float mult = __uint_as_float((254u - sc) << 23);    // 2^(127 - s)
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) lo |= e4m3_byte(f[k], mult) << (8 * k);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) hi |= e4m3_byte(f[4 + k], mult) << (8 * k);
-    *reinterpret_cast<uint2*>(q + i * 8) = make_uint2(lo, hi);
-    if ((lane & 3) == 0) {
-      const long long blk = i / 4;
-      if (scale_layout == kScaleRowMajor) {
-        s[blk] = (uint8_t)sc;
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * stride;
+      m[u] = 0;
+      if (i < total8) {
+        load8<T>(x + i * 8, f[u]);
       } else {
-        const long long r = blk / SC, c = blk - r * SC;
-        s[blocked_sf_offset(r, c, SC)] = (uint8_t)sc;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) f[u][k] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[u] = max(m[u], abs_bits(f[u][k]));
+      m[u] = max(m[u], __shfl_xor_sync(0xffffffffu, m[u], 1));
+      m[u] = max(m[u], __shfl_xor_sync(0xffffffffu, m[u], 2));
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * stride;
+      if (i >= total8) continue;
+      const uint32_t sc = floor_scale(m[u], 8);
+      const float mult = __uint_as_float((254u - sc) << 23);    // 2^(127 - s)
+      *reinterpret_cast<uint2*>(q + i * 8) = e4m3x8(f[u], mult, m[u]);
+      if ((lane & 3) == 0) {
+        const long long blk = i / 4;
+        if (scale_layout == kScaleRowMajor) {
+          s[blk] = (uint8_t)sc;
+        } else {
+          const long long r = blk / SC, c = blk - r * SC;
+          s[blocked_sf_offset(r, c, SC)] = (uint8_t)sc;
+        }
       }
     }
   }
@@ -193,12 +228,7 @@ __global__ void __launch_bounds__(256) quantize_cols_e4m3(const T* __restrict__ 
       if (orow < C) {
         const uint32_t sc = floor_scale(m, 8);
         const float mult = __uint_as_float((254u - sc) << 23);
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) lo |= e4m3_byte(f[k], mult) << (8 * k);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) hi |= e4m3_byte(f[4 + k], mult) << (8 * k);
-        *reinterpret_cast<uint2*>(qt + orow * R + r0 + part * 8) = make_uint2(lo, hi);
+        *reinterpret_cast<uint2*>(qt + orow * R + r0 + part * 8) = e4m3x8(f, mult, m);
         if (part == 0) {
           if (scale_layout == kScaleRowMajor)
             s[orow * RB + rb] = (uint8_t)sc;
