@@ -434,6 +434,10 @@ def main():
     ap.add_argument("--detail", action="store_true", help="also print one JSON line per (shape, pass) to stderr")
     ap.add_argument("--tile-m", type=int, default=0, help="GEMM tile rows: 128 (one CTA) or 256 (CTA pair); 0 = auto")
     ap.add_argument("--tile-n", type=int, default=0, help="GEMM tile columns: 128 or 256; 0 = auto")
+    ap.add_argument("--schedule", default="default", choices=["default", "tiles", "split_tail"],
+                    help="GEMM work schedule: split the last partial round's tiles (split_tail, the default) "
+                         "or deal whole tiles")
+    ap.add_argument("--split-max", type=int, default=0, help="most pieces per split tile (0 = automatic)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -473,6 +477,8 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     mxgg.device_status(clear=True)
     mxgg.set_tile_config(args.tile_m, args.tile_n, 0)
+    mxgg.set_schedule({"default": mxgg._lib.SCHED_DEFAULT, "tiles": mxgg._lib.SCHED_TILES,
+                       "split_tail": mxgg._lib.SCHED_SPLIT_TAIL}[args.schedule], args.split_max)
 
     probs = build_problems(dev, [shapes[i] for i in idx], passes)
     utils.flush_l2(dev)

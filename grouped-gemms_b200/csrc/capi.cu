@@ -54,6 +54,8 @@ DeviceState g_dev[kMaxDevices];
 int g_tile_m = 0;
 int g_tile_n = 0;
 int g_group_m = 0;
+int g_schedule = MXGG_SCHED_DEFAULT;
+int g_split_max = 0;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -120,6 +122,10 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
   }
 }
 
+// The grid never holds more CTAs than this (B200: 148 SMs); it bounds the
+// split-tail scratch, which is therefore independent of the problem.
+constexpr int kMaxGridCtas = 160;
+
 struct Maps {
   CUtensorMap a, b, sfa, sfb, out;
 };
@@ -139,7 +145,7 @@ int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, lon
     if (PAIR > 1) MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
     attr_done[dev] = true;
   }
-  const long long units = std::max(1LL, std::min<long long>(st.num_sms / PAIR, max_units));
+  const long long units = std::max(1LL, std::min<long long>(std::min(st.num_sms, kMaxGridCtas) / PAIR, max_units));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(units * PAIR), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -170,8 +176,12 @@ int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, l
 // 1 KiB aligned.  Sized for the larger of the two tile heights so a size
 // query does not depend on the tile configuration chosen at launch.
 struct WsPlan {
-  long long a_subtiles, b_tiles, stages, a_bytes, b_bytes, total;
+  long long a_subtiles, b_tiles, stages, a_bytes, b_bytes;
+  long long part_bytes, counter_bytes;   // split tail: one fp32 partial tile per CTA, arrival counters
+  long long total;                       // with the split-tail scratch
+  long long base;                        // without it
 };
+
 
 WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int tile_m, int tile_n) {
   WsPlan w{};
@@ -186,14 +196,22 @@ WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int 
   }
   w.a_bytes = (w.a_subtiles * w.stages * 512 + 1023) / 1024 * 1024;
   w.b_bytes = (w.b_tiles * w.stages * (tile_n / 128) * 512 + 1023) / 1024 * 1024;
-  w.total = w.a_bytes + w.b_bytes;
+  // one fp32 128 x tile_n partial per CTA; one counter per (tail tile, CTA
+  // of the pair, epilogue warp), fewer tail tiles than pairs
+  w.part_bytes = (long long)kMaxGridCtas * kBM * tile_n * 4;
+  w.counter_bytes = ((long long)kMaxGridCtas * 4 * 4 + 1023) / 1024 * 1024;
+  w.base = w.a_bytes + w.b_bytes;
+  w.total = w.base + w.part_bytes + w.counter_bytes;
   return w;
 }
 
-int64_t workspace_upper_bound(int mode, int64_t M, int64_t N, int64_t K, int64_t E) {
+int64_t workspace_upper_bound(int mode, int64_t M, int64_t N, int64_t K, int64_t E, bool with_split = true) {
   int64_t best = 0;
   for (int tm : {128, 256})
-    for (int tn : {128, 256}) best = std::max<int64_t>(best, plan_workspace(mode, M, N, K, E, tm, tn).total);
+    for (int tn : {128, 256}) {
+      const WsPlan w = plan_workspace(mode, M, N, K, E, tm, tn);
+      best = std::max<int64_t>(best, with_split ? w.total : w.base);
+    }
   return best;
 }
 
@@ -217,9 +235,11 @@ int pick_group_m(const TileChoice& c) {
   return c.tile_m == 128 ? 2 : 16;
 }
 
+// split_ok = 0: the caller's scratch only needs the packed scales and the
+// tail of the schedule is dealt as whole tiles.
 int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const void* b_scale,
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
-             void* workspace, int64_t workspace_bytes, void* stream_v) {
+             void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   const char* what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (out_dtype != MXGG_DTYPE_BF16 && out_dtype != MXGG_DTYPE_F16 && out_dtype != MXGG_DTYPE_F32)
@@ -259,11 +279,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   const int bn = tc.tile_n;
   const int pair = tc.tile_m / kBM;
   const WsPlan ws = plan_workspace(mode, M, N, K, E, tc.tile_m, bn);
-  if (!workspace || workspace_bytes < ws.total || !aligned(workspace, 256))
+  const long long need = split_ok ? ws.total : ws.base;
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(MXGG_ERR_INVALID, "%s: workspace of %lld bytes (256-byte aligned) required, got %lld at %p", what,
-                (long long)ws.total, (long long)workspace_bytes, workspace);
+                need, (long long)workspace_bytes, workspace);
   uint8_t* ws_a = static_cast<uint8_t*>(workspace);
   uint8_t* ws_b = ws_a + ws.a_bytes;
+  float* part_slots = reinterpret_cast<float*>(ws_b + ws.b_bytes);
+  int* part_counters = reinterpret_cast<int*>(ws_b + ws.b_bytes + ws.part_bytes);
+  const bool split_tail = split_ok && g_schedule != MXGG_SCHED_TILES;
 
   // 1) pack the row-major scales into the atoms the GEMM loads
   {
@@ -290,6 +314,10 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     pp.b_tiles = (int)ws.b_tiles;
     pp.a_out = ws_a;
     pp.b_out = ws_b;
+    if (split_tail) {
+      pp.zero = part_counters;
+      pp.zero_count = ws.counter_bytes / 4;
+    }
     const long long chunks = (ws.stages + 3) / 4;
     const long long warps = (ws.a_subtiles + ws.b_tiles * (bn / 128)) * chunks;
     const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
@@ -315,6 +343,10 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   const int es = out_esize(out_dtype);
   p.tma_store = aligned(out, 16) && ((out_cols * es) % 16 == 0);
   p.group_m = pick_group_m(tc);
+  p.split_tail = split_tail ? 1 : 0;
+  p.split_max = g_split_max;
+  p.part_slots = part_slots;
+  p.part_counters = part_counters;
   p.status = st->status;
 
   Maps maps;
@@ -391,8 +423,12 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
 int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
                             const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
                             void* out, int out_dtype, void* stream) {
+  bool split_ok = true;
   if (M >= 0 && N >= 0 && K >= 0 && E >= 1) {
-    const int64_t need = workspace_upper_bound(kFwd, M, N, K, E);
+    const int64_t need = workspace_upper_bound(kFwd, M, N, K, E, false);
+    // the split tail needs its partial tiles too; without room for them the
+    // last round is dealt as whole tiles
+    split_ok = workspace_upper_bound(kFwd, M, N, K, E, true) <= kNoAllocScratchBytes;
     if (need > kNoAllocScratchBytes)
       return fail(MXGG_ERR_UNSUPPORTED,
                   "mxgg_grouped_mm_noalloc: this problem needs %lld bytes of scratch, more than the %lld-byte "
@@ -414,7 +450,7 @@ int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, c
     ws = g_noalloc_ptr[dev];
   }
   return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, ws,
-                  kNoAllocScratchBytes, stream);
+                  kNoAllocScratchBytes, stream, split_ok);
 }
 
 int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
@@ -511,6 +547,17 @@ int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m) {
   g_tile_m = tile_m;
   g_tile_n = tile_n;
   g_group_m = group_m;
+  return MXGG_OK;
+}
+
+int mxgg_set_schedule(int32_t schedule, int32_t split_max) {
+  if (schedule != MXGG_SCHED_DEFAULT && schedule != MXGG_SCHED_TILES && schedule != MXGG_SCHED_SPLIT_TAIL)
+    return fail(MXGG_ERR_INVALID, "mxgg_set_schedule: unknown schedule %d", (int)schedule);
+  if (split_max < 0 || split_max == 1 || split_max > 64)
+    return fail(MXGG_ERR_INVALID, "mxgg_set_schedule: split_max must be 0 (automatic) or 2..64");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_schedule = schedule;
+  g_split_max = split_max;
   return MXGG_OK;
 }
 

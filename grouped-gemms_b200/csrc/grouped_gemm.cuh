@@ -71,6 +71,10 @@ struct GemmParams {
   int stages;                // 128-element contraction stages of the packed scales
   int tma_store;             // 1: output rows are 16-byte aligned for TMA stores
   int group_m;               // rasterisation band in row tiles (row tile fastest inside a band)
+  int split_tail;            // 1: split the tiles of the last, partial round along the contraction
+  int split_max;             // most pieces per split tile (0: about sqrt(stages))
+  float* part_slots;         // split tiles: one fp32 128 x BN partial per CTA of the grid
+  int* part_counters;        // split tiles: arrivals per (tail tile, CTA of the pair, epilogue warp), zeroed before the launch
   uint32_t* status;          // error word (device memory), 0 = ok
 };
 
@@ -86,12 +90,23 @@ struct Unit {
   int c_end;
   int a_sub;         // packed A-scale sub-tile of the tile's first 128 rows
   int b_tile;        // packed B-scale tile
+  // a stage range of a tail tile that other CTA pairs share
+  int split;         // 1: publish a partial; the last pair to arrive writes the tile
+  int tail;          // index of the tile in the tail round (its arrival counter)
+  int n_contrib;     // pairs contributing to the tile: p0 .. p0 + n_contrib - 1
+  int p0;
+  int me;            // this pair's place among the contributors
 };
 
 template <int BN, int STAGES, int PAIR, typename OutT>
 struct SmemLayout {
   static constexpr int kEpiCols = 64 / sizeof(OutT);   // 64-byte staging rows
   static constexpr int kBRows = BN / PAIR;              // B rows staged by this CTA
+  // A split tile's last pair sums the partials through the stage buffers,
+  // idle by then: a quarter per epilogue warp, two chunk buffers of kMaxWays
+  // fp32 partial chunks (32 rows x kEpiCols) each.
+  static constexpr int kRedWarpBytes = (STAGES * kBM * kBK + STAGES * kBRows * kBK) / 4;
+  static constexpr int kMaxWays = kRedWarpBytes / (2 * 32 * kEpiCols * 4);
   alignas(1024) uint8_t a[STAGES][kBM * kBK];
   alignas(1024) uint8_t b[STAGES][kBRows * kBK];
   alignas(1024) uint8_t epi[4][2][32 * 64];            // per epilogue warp, double buffered
@@ -110,6 +125,9 @@ struct SmemLayout {
   int g_end[kMaxGroups];
   int g_cum[kMaxGroups + 1];
   int g_order[kMaxGroups];   // wgrad: groups by decreasing token count
+
+  // a and b are one contiguous region (the split-tile reduction spans both)
+  static_assert(sizeof(a) % 1024 == 0, "stage buffers must be contiguous");
 };
 
 __device__ __forceinline__ int cdiv_i(int a, int b) { return (a + b - 1) / b; }
@@ -178,6 +196,11 @@ __device__ __forceinline__ int unit_at(int k, int i, int P) { return k * P + ((k
 template <int BN, int TILE_M, class S>
 __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, int t) {
   Unit u;
+  u.split = 0;
+  u.tail = 0;
+  u.n_contrib = 1;
+  u.p0 = 0;
+  u.me = 0;
   if (p.mode == kFwd) {
     const int NT = cdiv_i(p.N, BN);
     const int MT = sm->g_cum[p.E];
@@ -241,6 +264,61 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     u.b_tile = kt;
   }
   return u;
+}
+
+// Pieces a tail tile of C stages is split into when s pairs are free for it.
+// Measured on B200 (256 x 256 pair tiles): a stage takes ~0.55 us, publishing
+// a partial ~3.5 us and the last pair's reduction ~1.7 us per piece, so w
+// pieces cost ~0.55 C / w + 3.5 + 1.7 w: about sqrt(C / 3) pieces, and tiles
+// under 24 stages stay whole.
+__device__ __forceinline__ int split_ways(const GemmParams& p, int C, int s, int max_ways) {
+  if (C <= 1) return 1;
+  int cap = p.split_max;
+  if (cap <= 0) {
+    if (C < 24) return 1;
+    cap = 2;
+    while ((cap + 1) * (cap + 1) * 3 <= C) ++cap;
+  }
+  return max(1, min(min(min(s, C), cap), max_ways));
+}
+
+// The next unit of CTA pair `pair` of `P`, identical in every role.  Whole
+// tiles are dealt in snake-ordered rounds of P (units_at).  With split_tail,
+// the L < P tiles of the last, partial round are instead cut along the
+// contraction into pieces, one per otherwise idle pair: pair i takes piece
+// i % s of tail tile i / s (s = P / L).  `k` counts the pair's rounds.
+template <int BN, int TILE_M, class S>
+__device__ __forceinline__ bool next_unit(const S* sm, const GemmParams& p, int& k, int pair, int P, int num_units,
+                                          Unit& u) {
+  const int F = num_units / P;
+  const int L = num_units - F * P;
+  const int s = (p.split_tail && L > 0) ? P / L : 1;
+  if (s < 2 || k < F) {
+    const int t = unit_at(k, pair, P);
+    if (t >= num_units) return false;
+    ++k;
+    u = decode_unit<BN, TILE_M>(sm, p, t);
+    return true;
+  }
+  if (k > F) return false;
+  ++k;
+  const int ti = pair / s, j = pair - ti * s;
+  if (ti >= L) return false;
+  u = decode_unit<BN, TILE_M>(sm, p, F * P + ti);
+  const int C = u.st_count;
+  const int ways = split_ways(p, C, s, S::kMaxWays);
+  if (j >= ways) return false;
+  if (ways > 1) {
+    const int lo = C * j / ways, hi = C * (j + 1) / ways;
+    u.st_begin += lo;
+    u.st_count = hi - lo;
+    u.split = 1;
+    u.tail = ti;
+    u.n_contrib = ways;
+    u.p0 = ti * s;
+    u.me = j;
+  }
+  return true;
 }
 
 template <typename OutT>
@@ -371,10 +449,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int k = 0; ok; ++k) {
-        const int t = unit_at(k, unit0, unit_stride);
-        if (t >= num_units) break;
-        const Unit u = decode_unit<BN, kTileM>(sm, p, t);
+      int k = 0;
+      Unit u;
+      while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const int stage = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -426,10 +503,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t sfbdesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfb[0]));
       uint32_t it = 0, ai = 0;
       bool ok = true;
-      for (int k = 0; ok; ++k, ++ai) {
-        const int t = unit_at(k, unit0, unit_stride);
-        if (t >= num_units) break;
-        const Unit u = decode_unit<BN, kTileM>(sm, p, t);
+      int k = 0;
+      Unit u;
+      for (; ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
         const int acc = ai & 1;
         const uint32_t aph = (ai >> 1) & 1u;
         // this buffer fully drained (tile ai - 2) ...
@@ -509,10 +585,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     uint32_t ai = 0;
     int buf = 0;
-    for (int k = 0;; ++k, ++ai) {
-      const int t = unit_at(k, unit0, unit_stride);
-      if (t >= num_units) break;
-      const Unit u = decode_unit<BN, kTileM>(sm, p, t);
+    int k = 0;
+    Unit u;
+    for (; next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
       const int acc = ai & 1;
       const uint32_t aph = (ai >> 1) & 1u;
       if (!ptx::mbar_wait(ptx::smem_u32(&sm->tfull[acc]), aph, abort)) {
@@ -529,10 +604,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // chunk order: the columns shared with the other buffer first
       // (buffer 0: its last kOv columns, buffer 1: its first kOv columns)
       const int c_first = (acc == 0) ? (kChunks - kOvChunks) : 0;
-#pragma unroll 1
-      for (int ci = 0; ci < kChunks; ++ci) {
-        const int c = (acc == 0) ? (ci < kOvChunks ? c_first + ci : ci - kOvChunks) : ci;
-        uint32_t v[kEpiCols];
+      // chunk ci of the accumulator (in drain order) -> v, releasing the
+      // buffer's shared / whole columns to the MMA warp as they are read
+      auto load_chunk = [&](int ci, int c, uint32_t (&v)[kEpiCols]) {
         if (!zero) {
           if constexpr (kEpiCols == 32) {
             ptx::tmem_ld_32x32b_x32(t_row + c * kEpiCols, reinterpret_cast<uint32_t(&)[32]>(v));
@@ -556,9 +630,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) arrive_leader(&sm->tempty_all[acc]);
         }
-        if (rows_here == 0) continue;
+      };
+      // fp32 chunk c of this thread's row -> output (TMA store through the
+      // staging buffer, or predicated vector stores)
+      auto emit = [&](int c, const uint32_t (&v)[kEpiCols]) {
+        if (rows_here == 0) return;
         const int col0 = u.out_col + c * kEpiCols;
-        if (col0 >= p.out_cols) continue;
+        if (col0 >= p.out_cols) return;
         // 64 output bytes for this thread's row
         uint32_t w[16];
         if constexpr (sizeof(OutT) == 4) {
@@ -606,6 +684,115 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (j < ncols) d[j] = (uint16_t)(w[j >> 1] >> ((j & 1) * 16));
           }
         }
+      };
+      if (!u.split) {
+#pragma unroll 1
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int c = (acc == 0) ? (ci < kOvChunks ? c_first + ci : ci - kOvChunks) : ci;
+          uint32_t v[kEpiCols];
+          load_chunk(ci, c, v);
+          emit(c, v);
+        }
+        continue;
+      }
+      // Split tile.  Each contributing pair publishes its fp32 partial and
+      // counts its arrival; the pair that arrives last sums all partials in
+      // contributor order and writes the tile, so the result does not depend
+      // on timing.  A pair that finds every other partial already published
+      // skips its own and adds its accumulator in its place (same order, same
+      // sum).  Partial layout: per (pair, CTA, epilogue warp) a block of
+      // 32 rows, float4 i of chunk c of lane l at [(c * kV + i) * 32 + l]
+      // (coalesced stores, contiguous chunks for the reduction's copies).
+      constexpr int kV = kEpiCols / 4;
+      constexpr int kChunkF4 = kV * 32;                 // float4 per chunk of a warp block
+      auto part = [&](int pair_q) -> const float4* {
+        return reinterpret_cast<const float4*>(p.part_slots) +
+               (long long)((pair_q * PAIR + (int)rank) * 4 + q) * (kChunks * kChunkF4) + lane;
+      };
+      int* const ctr = p.part_counters + (u.tail * PAIR + (int)rank) * 4 + q;
+      int seen = 0;
+      if (lane == 0) seen = ptx::ld_acquire_gpu(ctr);
+      seen = __shfl_sync(0xffffffffu, seen, 0);
+      __syncwarp();
+      const bool fast = (seen == u.n_contrib - 1);
+      if (!fast) {
+        float4* mine = const_cast<float4*>(part(unit0));
+#pragma unroll 1
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int c = (acc == 0) ? (ci < kOvChunks ? c_first + ci : ci - kOvChunks) : ci;
+          uint32_t v[kEpiCols];
+          load_chunk(ci, c, v);
+#pragma unroll
+          for (int i = 0; i < kV; ++i)
+            __stcg(mine + c * kChunkF4 + i * 32,
+                   make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                               __uint_as_float(v[4 * i + 3])));
+        }
+        __threadfence();
+        __syncwarp();
+        int arrived = 0;
+        if (lane == 0) arrived = atomicAdd(ctr, 1);
+        arrived = __shfl_sync(0xffffffffu, arrived, 0);
+        if (arrived != u.n_contrib - 1) continue;
+        __threadfence();
+      }
+      // Sum chunk by chunk: cp.async streams the contributors' copies of the
+      // coming chunks into a ring in this warp's quarter of the (idle) stage
+      // buffers, `depth` chunks deep, while the current one is added.  Each
+      // lane copies and reads only its own 16-byte slots, so its own
+      // wait_group orders them; one group is committed per chunk (empty ones
+      // included) so that wait_group(depth - 1) always means "chunk ci landed".
+      const uint32_t red = ptx::smem_u32(sm->a) + q * S::kRedWarpBytes + lane * 16;
+      constexpr int kSlots = S::kRedWarpBytes / (kChunkF4 * 16);
+      const int depth = min(kSlots / u.n_contrib, 12);
+      auto chunk_of = [&](int ci) { return (acc == 0) ? (ci < kOvChunks ? c_first + ci : ci - kOvChunks) : ci; };
+      auto slot_addr = [&](int ci, int j) {
+        return red + (uint32_t)(((ci % depth) * u.n_contrib + j) * kChunkF4 * 16);
+      };
+      auto prefetch = [&](int ci) {
+        if (ci < kChunks) {
+          const int c = chunk_of(ci);
+          for (int j = 0; j < u.n_contrib; ++j) {
+            if (fast && j == u.me) continue;
+            const float4* src = part(u.p0 + j) + c * kChunkF4;
+            const uint32_t dst = slot_addr(ci, j);
+#pragma unroll
+            for (int i = 0; i < kV; ++i) ptx::cp_async_16(dst + i * 32 * 16, src + i * 32);
+          }
+        }
+        ptx::cp_async_commit();
+      };
+      for (int ci = 0; ci < depth - 1; ++ci) prefetch(ci);
+#pragma unroll 1
+      for (int ci = 0; ci < kChunks; ++ci) {
+        const int c = chunk_of(ci);
+        uint32_t v[kEpiCols];
+        if (fast) load_chunk(ci, c, v);
+        prefetch(ci + depth - 1);
+        ptx::cp_async_wait_group_dyn(depth - 1);
+        float sum[kEpiCols];
+#pragma unroll
+        for (int i = 0; i < kEpiCols; ++i) sum[i] = 0.0f;
+        for (int j = 0; j < u.n_contrib; ++j) {
+          const uint32_t src = slot_addr(ci, j);
+          if (fast && j == u.me) {
+#pragma unroll
+            for (int i = 0; i < kEpiCols; ++i) sum[i] += __uint_as_float(v[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < kV; ++i) {
+              float4 x;
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                           : "r"(src + i * 32 * 16)
+                           : "memory");
+              sum[4 * i] += x.x; sum[4 * i + 1] += x.y; sum[4 * i + 2] += x.z; sum[4 * i + 3] += x.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kEpiCols; ++i) v[i] = __float_as_uint(sum[i]);
+        emit(c, v);
       }
     }
     if (lane == 0) ptx::bulk_wait<0>();

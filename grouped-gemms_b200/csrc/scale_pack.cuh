@@ -40,6 +40,8 @@ struct PackParams {
   int b_tiles;           // B-side tiles
   uint8_t* a_out;
   uint8_t* b_out;
+  int* zero;             // stream-K arrival counters to clear (or null)
+  long long zero_count;
 };
 
 // Load the scale words of stages [q*4, q*4+4) for one row: word j = the four
@@ -109,6 +111,11 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
       if (lane == 0) s_cum[p.E] = carry_sum;
     }
     __syncthreads();
+  }
+  if (p.zero) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < p.zero_count;
+         i += (long long)gridDim.x * blockDim.x)
+      p.zero[i] = 0;
   }
   const int halves = p.tile_m / 128;
   const int bsub = p.tile_n / 128;

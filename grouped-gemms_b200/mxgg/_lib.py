@@ -15,6 +15,7 @@ MXGG_OK = 0
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 QUANT_ROWS, QUANT_COLS = 0, 1
 SCALE_ROW_MAJOR, SCALE_BLOCKED = 0, 1
+SCHED_DEFAULT, SCHED_TILES, SCHED_SPLIT_TAIL = 0, 1, 2
 
 # every symbol include/mxgg.h declares, with (restype, argtypes)
 _vp = ctypes.c_void_p
@@ -30,6 +31,7 @@ SIGNATURES = {
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
     "mxgg_set_tile_config": (_int, [_i32, _i32, _i32]),
+    "mxgg_set_schedule": (_int, [_i32, _i32]),
     "mxgg_device_status": (_int, [ctypes.POINTER(ctypes.c_uint32), _int, _vp]),
     "mxgg_last_error": (ctypes.c_char_p, []),
     "mxgg_version": (_i32, []),
@@ -80,3 +82,10 @@ def set_tile_config(tile_m: int = 0, tile_n: int = 0, group_m: int = 0) -> None:
     """Tile shape for later GEMM calls (0 = automatic): tile_m 128 (one CTA)
     or 256 (a CTA pair), tile_n 128 or 256, group_m the rasterisation band."""
     check(load().mxgg_set_tile_config(tile_m, tile_n, group_m), "mxgg_set_tile_config")
+
+
+def set_schedule(schedule: int = SCHED_DEFAULT, split_max: int = 0) -> None:
+    """Work schedule of later GEMM calls: SCHED_SPLIT_TAIL (default) cuts the
+    tiles of the last partial round along the contraction for idle CTA pairs,
+    SCHED_TILES deals whole tiles; split_max caps the pieces per tile."""
+    check(load().mxgg_set_schedule(schedule, split_max), "mxgg_set_schedule")

@@ -140,6 +140,17 @@ int mxgg_build_tile_map(const int32_t* group_end_offsets, int64_t E, int64_t M, 
  * tile_n in {128, 256}, group_m >= 1 rasterisation band in m-tiles. */
 int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m);
 
+/* Work schedule of later GEMM calls on this process.  Output tiles are
+ * dealt to the persistent CTA pairs in rounds; with SPLIT_TAIL (the default)
+ * the tiles of the last, partial round are cut along the contraction into
+ * pieces for the pairs that would otherwise idle, and the last piece to
+ * finish sums the fp32 partials in a fixed order (results do not depend on
+ * timing).  TILES deals every tile whole.  split_max caps the pieces per
+ * tile (0: about the square root of the tile's 128-element stages; else
+ * 2..64).  No counterpart in the reference. */
+enum { MXGG_SCHED_DEFAULT = 0, MXGG_SCHED_TILES = 1, MXGG_SCHED_SPLIT_TAIL = 2 };
+int mxgg_set_schedule(int32_t schedule, int32_t split_max);
+
 /* Error bits raised by device-side bounded waits since the last clear
  * (0 = none).  Synchronises `stream`.  clear != 0 resets the word. */
 int mxgg_device_status(uint32_t* status_out, int clear, void* stream);

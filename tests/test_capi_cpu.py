@@ -96,6 +96,28 @@ def test_tile_config_validation():
     assert lib.mxgg_set_tile_config(0, 0, 0) == 0
 
 
+def test_schedule_validation():
+    lib = _lib.load()
+    assert lib.mxgg_set_schedule(3, 0) == 1
+    assert lib.mxgg_set_schedule(-1, 0) == 1
+    assert lib.mxgg_set_schedule(0, 1) == 1
+    assert lib.mxgg_set_schedule(0, 65) == 1
+    for s in (_lib.SCHED_TILES, _lib.SCHED_SPLIT_TAIL, _lib.SCHED_DEFAULT):
+        assert lib.mxgg_set_schedule(s, 0) == 0
+    assert lib.mxgg_set_schedule(_lib.SCHED_DEFAULT, 4) == 0
+    assert lib.mxgg_set_schedule(_lib.SCHED_DEFAULT, 0) == 0
+
+
+def test_workspace_holds_split_tail_partials():
+    # one fp32 128 x 256 partial tile for each of up to 160 CTAs, on top of
+    # the packed scales, whatever the problem
+    lib = _lib.load()
+    for fn in (lib.mxgg_grouped_mm_workspace_size, lib.mxgg_wgrad_workspace_size):
+        assert fn(256, 256, 1024, 1) >= 160 * 128 * 256 * 4
+    f = lib.mxgg_grouped_mm_workspace_size
+    assert f(4096, 4096, 4096, 8) > f(4096, 4096, 4096, 1)     # B scales of every group
+
+
 def test_no_cpu_fallback():
     import torch
     import utils

@@ -228,3 +228,43 @@ def test_tile_map_matches_reference_layout(K_):
         np.testing.assert_array_equal(got[E:2 * E], raw)
         assert got[2 * E] == pad
         np.testing.assert_array_equal(got[2 * E + 1:], pmap)
+
+
+@pytest.mark.parametrize("sched,split_max", [(1, 0), (2, 0), (2, 64)])
+@pytest.mark.parametrize("tile_m", [128, 256])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("E,M,N,K,offs", [
+    # fewer tiles than pairs: every tile split along K
+    (1, 2048, 256, 4096, [2048]),
+    # a full round of tiles, then a partial one that is split
+    (2, 2048, 2560, 1024, [1000, 2048]),
+    # ragged groups, odd N (predicated stores), an empty group
+    (4, 1500, 200, 2048, [300, 300, 1100, 1500]),
+])
+def test_split_tail_schedule(K_, sched, split_max, tile_m, out_dtype, E, M, N, K, offs):
+    """Whole-tile and split-tail schedules against the oracle."""
+    import mxgg
+    _, _, a_s, a_q, b_s, b_q, o = _make(E, M, N, K, offs, seed=E + K)
+    mxgg.set_schedule(sched, split_max)
+    mxgg.set_tile_config(tile_m, 0, 0)
+    try:
+        out = K_.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, o, out_dtype=out_dtype)
+        torch.cuda.synchronize()
+    finally:
+        mxgg.set_schedule(0, 0)
+        mxgg.set_tile_config(0, 0, 0)
+    _check(out, _oracle(a_q, a_s, b_q, b_s, o), out_dtype)
+
+
+def test_split_tail_deterministic(K_):
+    import mxgg
+    E, M, N, K = 1, 2048, 512, 8192
+    _, _, a_s, a_q, b_s, b_q, o = _make(E, M, N, K, [M], seed=4)
+    mxgg.set_schedule(2, 64)
+    try:
+        outs = [K_.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, o, out_dtype=torch.float32) for _ in range(4)]
+        torch.cuda.synchronize()
+    finally:
+        mxgg.set_schedule(0, 0)
+    for x in outs[1:]:
+        assert torch.equal(x, outs[0])

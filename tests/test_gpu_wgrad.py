@@ -8,6 +8,7 @@ import pytest
 import torch
 
 from helpers import O, bf16_round, f32, gpu_status_clear, offsets, u8
+from mxgg import _lib
 
 pytestmark = pytest.mark.gpu
 
@@ -139,3 +140,57 @@ def test_full_size_sampled(K_, U):
         ref = GOd[:, prev:e] @ IAd[:, prev:e].T
         assert O.rel_l2(got_all[gi], bf16_round(ref)) <= 1e-3
         prev = e
+
+
+@pytest.fixture
+def schedule():
+    """Set the GEMM schedule for one test and restore the defaults after it."""
+    def set_(s, split_max=0):
+        _lib.set_schedule(s, split_max)
+    yield set_
+    _lib.set_schedule(_lib.SCHED_DEFAULT, 0)
+    _lib.set_tile_config(0, 0, 0)
+
+
+@pytest.mark.parametrize("sched,split_max", [(_lib.SCHED_TILES, 0), (_lib.SCHED_SPLIT_TAIL, 0),
+                                             (_lib.SCHED_SPLIT_TAIL, 64)])
+@pytest.mark.parametrize("tile_m", [128, 256])
+@pytest.mark.parametrize("E,M,N,K,offs", [
+    # one tile: split over as many pairs as it has stages (split_max 64)
+    (1, 8192, 256, 256, [8192]),
+    # a few tiles, many stages: every tile split across several pairs
+    (2, 16384, 256, 512, [9600, 16384]),
+    # jagged groups (empty, sub-stage, off-grid); the tail holds empty-group tiles
+    (5, 2048, 384, 256, [0, 32, 480, 480, 2048]),
+    # many tiles: a full round and a partial one
+    (8, 4096, 1024, 2560, None),
+])
+def test_schedules_vs_oracle(K_, schedule, sched, split_max, tile_m, E, M, N, K, offs):
+    schedule(sched, split_max)
+    _lib.set_tile_config(tile_m, 0, 0)
+    if offs is None:
+        offs = offsets(E, M, 32, seed=11)
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=E + 3)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref = _oracle(go_q, go_s, ia_q, ia_s, offs)
+    _check(out, ref, torch.float32)
+    prev = 0
+    for g, e in enumerate(offs):
+        if e == prev:
+            assert torch.count_nonzero(out[g]) == 0
+        prev = e
+
+
+def test_split_tail_deterministic(K_, schedule):
+    """Partials are summed in a fixed order: repeated calls are bit-identical."""
+    schedule(_lib.SCHED_SPLIT_TAIL, 64)
+    E, M, N, K = 3, 12288, 512, 512
+    offs = [4000, 4000, 12288]
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=9)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    outs = [K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=torch.float32) for _ in range(4)]
+    torch.cuda.synchronize()
+    for x in outs[1:]:
+        assert torch.equal(x, outs[0])
