@@ -145,8 +145,103 @@ def build_problems(device, shapes, passes, seed=123):
     return probs
 
 
+def build_ep_problems(device, shapes, passes, world, rank, seed=123):
+    """Expert-parallel sweep: the same 36 shapes with every rank holding its
+    own M = 16640 tokens (offsets drawn as the single-GPU sweep draws them,
+    seeded per rank) and the weights of the experts it hosts.  fwd and dgrad
+    run dispatch -> segment GEMM -> combine; wgrad runs on the hosting rank
+    over the tokens it received (expert-major, as the forward's dispatch left
+    them) and sums replicas' gradients with an all-reduce.  Per-rank FLOPs
+    are 2*rows*N*K over the rows that rank computes; every rank sends all M of
+    its rows, so the ranks' total is world * 2*M*N*K."""
+    import torch
+    import utils
+    from mxgg import ep
+
+    random.seed(seed + 1000 * rank)
+    gen = torch.Generator(device=device).manual_seed(seed + 1000 * rank)
+    probs = []
+    groups = {}
+    for (E, M, N, K) in shapes:
+        pl = ep.ExpertPlacement(world, E)
+        if E not in groups:
+            groups[E] = ep.replica_groups(pl)          # collective: same order on every rank
+        offs = utils.generate_jagged_offs(E, M, multiple_of=32, device="cpu").tolist()
+        counts = [b - a for a, b in zip([0] + offs[:-1], offs)]
+        plan = ep.plan_dispatch(pl, counts, device)
+        mine = pl.experts_of(rank)
+        gw = torch.Generator(device=device).manual_seed(seed + 77 * (mine[0] + 1))
+        Wl = torch.randn(len(mine), N, K, device=device, dtype=torch.bfloat16, generator=gw)
+        if "fwd" in passes:
+            A = torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=gen)
+            a_s, a_q = utils.to_mx(A)
+            w_s, w_q = utils.to_mx(Wl)
+            probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan,
+                              args=(a_q, a_s), weights=(w_q, w_s)))
+            del A
+        if "dgrad" in passes:
+            G = torch.randn(M, N, device=device, dtype=torch.bfloat16, generator=gen)
+            g_s, g_q = utils.to_mx(G)
+            wt = [utils.to_mx_dim1(Wl[e]) for e in range(len(mine))]
+            probs.append(dict(pass_="dgrad", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan,
+                              args=(g_q, g_s), weights=(torch.stack([q for _, q in wt]),
+                                                        torch.stack([s_ for s_, _ in wt]))))
+            del G
+        if "wgrad" in passes:
+            R = plan.rows_recv
+            loc = plan.expert_rows()
+            loffs = torch.tensor(loc, dtype=torch.int64).cumsum(0).to(torch.int32).to(device)
+            go = torch.randn(R, N, device=device, dtype=torch.bfloat16, generator=gen)
+            x = torch.randn(R, K, device=device, dtype=torch.bfloat16, generator=gen)
+            go_s, go_q = utils.to_mx_dim1(go)
+            ia_s, ia_q = utils.to_mx_dim1(x)
+            probs.append(dict(pass_="wgrad", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan,
+                              args=(go_q, go_s, ia_q, ia_s, loffs), groups=groups[E]))
+            del go, x
+        del Wl
+    torch.cuda.synchronize()
+    return probs
+
+
+def run_ep_problem(p, marks=None):
+    """One expert-parallel call; `marks` (3 events) split it into dispatch |
+    local GEMM | combine."""
+    import kernels
+    from mxgg import ep
+    from mxgg.ops import grouped_mm_segments_op
+    plan = p["plan"]
+    if p["pass_"] == "wgrad":
+        if marks:
+            marks[0].record()
+        out = kernels.triton_mxfp8_wgrad(*p["args"])
+        if marks:
+            marks[1].record()
+        ep.replica_allreduce(plan.placement, out, p.get("groups"))
+        if marks:
+            marks[2].record()
+        return out
+    recv_q, recv_s = ep.dispatch(plan, *p["args"])
+    if marks:
+        marks[0].record()
+    y = grouped_mm_segments_op(recv_q, p["weights"][0], recv_s, p["weights"][1], plan.seg_offs, plan.seg_expert,
+                               torch_bf16())
+    if marks:
+        marks[1].record()
+    out = ep.combine(plan, y)
+    if marks:
+        marks[2].record()
+    return out
+
+
+def torch_bf16():
+    import torch
+    return torch.bfloat16
+
+
 def run_problem(p):
     import kernels
+    if "plan" in p:
+        return run_ep_problem(p)
     if p["pass_"] == "wgrad":
         return kernels.triton_mxfp8_wgrad(*p["args"])
     return kernels.triton_mxfp8_grouped_mm(*p["args"])
@@ -345,6 +440,35 @@ def capture_graphs(probs):
     return graphs
 
 
+def time_ep_problems(probs, steps, warmup, world, flush):
+    """Expert-parallel sweep, eager (NCCL calls are not captured): per-problem
+    mean device time (s) and per-phase times (dispatch, GEMM, combine)."""
+    import torch
+    n = len(probs)
+    for _ in range(warmup):
+        for p in probs:
+            flush()
+            run_ep_problem(p)
+    barrier(world)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    rec = [[(ev(), ev(), ev(), ev(), ev()) for _ in range(n)] for _ in range(steps)]
+    step_s, step_e = ev(), ev()
+    step_s.record()
+    for s in range(steps):
+        for i, p in enumerate(probs):
+            flush()
+            e = rec[s][i]
+            e[0].record()
+            run_ep_problem(p, marks=e[1:4])
+            e[4].record()
+    step_e.record()
+    barrier(world)
+    per = [sum(rec[s][i][0].elapsed_time(rec[s][i][4]) for s in range(steps)) / steps * 1e-3 for i in range(n)]
+    phases = [[sum(rec[s][i][k].elapsed_time(rec[s][i][k + 1]) for s in range(steps)) / steps * 1e-3
+               for k in range(3)] for i in range(n)]
+    return per, phases, step_s.elapsed_time(step_e) / steps
+
+
 def time_problems(probs, steps, warmup, world, flush):
     """Per-problem mean device time (s) over `steps` timed steps."""
     import torch
@@ -448,7 +572,7 @@ def main():
     cfg = {"workload": "llama4-36-shapes x {" + ",".join(passes) + "}", "shapes": len(idx), "M": M_TOKENS,
            "tile": f"{args.tile_m or 'auto'}x{args.tile_n or 'auto'}",
            "E": [1, 2, 4, 8], "N": [2048, 5120, 8192], "K": [2048, 5120, 8192], "offs": "generate_jagged_offs(seed 123, multiple_of 32)",
-           "l2": "flushed (512 MiB memset) before every timed launch", "parallelism": f"replicas x{args.gpus}"}
+           "l2": "flushed (512 MiB memset) before every timed launch", "parallelism": "single GPU"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -480,18 +604,41 @@ def main():
     mxgg.set_schedule({"default": mxgg._lib.SCHED_DEFAULT, "tiles": mxgg._lib.SCHED_TILES,
                        "split_tail": mxgg._lib.SCHED_SPLIT_TAIL}[args.schedule], args.split_max)
 
-    probs = build_problems(dev, [shapes[i] for i in idx], passes)
+    ep_mode = world > 1
+    if ep_mode:
+        probs = build_ep_problems(dev, [shapes[i] for i in idx], passes, world, rank)
+        cfg["parallelism"] = f"ep{world} (expert parallel: NCCL all-to-all dispatch/combine)"
+        cfg["M"] = f"{M_TOKENS} tokens per rank"
+    else:
+        probs = build_problems(dev, [shapes[i] for i in idx], passes)
     utils.flush_l2(dev)
     flush = lambda: utils.flush_l2(dev)  # noqa: E731
 
+    phases = None
     with ClockSampler(gpu_smi_id(dev)) as clk:
         # a short untimed pre-run keeps the sampler's window on a loaded GPU
         for p_ in probs[: min(len(probs), 12)]:
             flush()
             run_problem(p_)
-        per, wall_ms = time_problems(probs, args.steps, args.warmup, world, flush)
+        if ep_mode:
+            per, phases, wall_ms = time_ep_problems(probs, args.steps, args.warmup, world, flush)
+        else:
+            per, wall_ms = time_problems(probs, args.steps, args.warmup, world, flush)
     per = allreduce_max(per, world)
     status = mxgg.device_status(clear=True)
+    ep_info = None
+    if ep_mode:
+        # rank 0's own GEMM work and phase split (max over ranks per phase)
+        ph = allreduce_max([x for row in phases for x in row], world)
+        phases = [ph[3 * i:3 * i + 3] for i in range(len(probs))]
+        local_flops = [2.0 * p["plan"].rows_recv * p["shape"][2] * p["shape"][3] for p in probs]
+        gemm_t = [x[1] for x in phases]
+        ep_info = {"phases_us_per_step": {
+                       "dispatch": round(1e6 * sum(x[0] for p, x in zip(probs, phases) if p["pass_"] != "wgrad"), 1),
+                       "gemm": round(1e6 * sum(gemm_t), 1),
+                       "combine_or_replica_allreduce": round(1e6 * sum(x[2] for x in phases), 1)},
+                   "rank0_gemm_tflops_geomean": round(geomean([f / t / 1e12 for f, t in zip(local_flops, gemm_t)]), 1),
+                   "placement": "experts sharded when E >= world, replicated (world/E copies) when E < world"}
 
     tf = [p["flops"] / t / 1e12 for p, t in zip(probs, per)]
     by_pass = {ps: round(geomean([x for x, p in zip(tf, probs) if p["pass_"] == ps]), 1) for ps in passes}
@@ -499,6 +646,9 @@ def main():
     total_flops = sum(p["flops"] for p in probs)
     total_time = sum(per)
     achieved = total_flops / total_time / 1e12
+    if ep_mode:
+        # the GEMM kernel's own rate on rank 0 (communication excluded)
+        achieved = sum(local_flops) / sum(gemm_t) / 1e12
 
     e2e = None
     if args.no_extras:
@@ -541,6 +691,8 @@ def main():
                 "roofline": roof, "quantize_roofline": quant, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": 2 * len(probs) * args.steps, "clocks": clk.summary(),
                 "device_status": status, "wall_ms_per_step": round(wall_ms, 3)}
+        if ep_info:
+            line["expert_parallel"] = ep_info
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier(world)

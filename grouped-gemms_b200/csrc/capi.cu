@@ -183,13 +183,15 @@ struct WsPlan {
 };
 
 
-WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int tile_m, int tile_n) {
+// fwd: E groups (segments) over n_experts slices of B; wgrad: n_experts unused
+WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int64_t n_experts, int tile_m,
+                      int tile_n) {
   WsPlan w{};
   const int64_t C = mode == kFwd ? K : M;
   w.stages = (C + kBK - 1) / kBK;
   if (mode == kFwd) {
     w.a_subtiles = ((M + tile_m - 1) / tile_m + (E - 1)) * (tile_m / kBM);
-    w.b_tiles = E * ((N + tile_n - 1) / tile_n);
+    w.b_tiles = n_experts * ((N + tile_n - 1) / tile_n);
   } else {
     w.a_subtiles = ((N + tile_m - 1) / tile_m) * (tile_m / kBM);
     w.b_tiles = (K + tile_n - 1) / tile_n;
@@ -205,11 +207,12 @@ WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int 
   return w;
 }
 
-int64_t workspace_upper_bound(int mode, int64_t M, int64_t N, int64_t K, int64_t E, bool with_split = true) {
+int64_t workspace_upper_bound(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int64_t n_experts,
+                              bool with_split = true) {
   int64_t best = 0;
   for (int tm : {128, 256})
     for (int tn : {128, 256}) {
-      const WsPlan w = plan_workspace(mode, M, N, K, E, tm, tn);
+      const WsPlan w = plan_workspace(mode, M, N, K, E, n_experts, tm, tn);
       best = std::max<int64_t>(best, with_split ? w.total : w.base);
     }
   return best;
@@ -237,21 +240,27 @@ int pick_group_m(const TileChoice& c) {
 
 // split_ok = 0: the caller's scratch only needs the packed scales and the
 // tail of the schedule is dealt as whole tiles.
+// Forward groups may be segments that share B slices: group g multiplies
+// B[group_expert[g]] (null: B[g], n_experts == E).
 int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const void* b_scale,
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
-             void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true) {
+             void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
+             const int32_t* group_expert = nullptr, int64_t n_experts = -1,
+             const char* what = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  const char* what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
+  if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
+  if (n_experts < 0) n_experts = E;
   if (out_dtype != MXGG_DTYPE_BF16 && out_dtype != MXGG_DTYPE_F16 && out_dtype != MXGG_DTYPE_F32)
     return fail(MXGG_ERR_INVALID, "%s: unknown out_dtype %d", what, out_dtype);
   if (M < 0 || N < 0 || K < 0 || E < 1)
     return fail(MXGG_ERR_INVALID, "%s: bad sizes M=%lld N=%lld K=%lld E=%lld", what, (long long)M, (long long)N,
                 (long long)K, (long long)E);
   if (E > kMaxGroups) return fail(MXGG_ERR_UNSUPPORTED, "%s: E=%lld exceeds %d groups", what, (long long)E, kMaxGroups);
+  if (n_experts < 1) return fail(MXGG_ERR_INVALID, "%s: n_experts=%lld", what, (long long)n_experts);
   // contraction length: fwd K, wgrad tokens M
   const int64_t C = mode == kFwd ? K : M;
   const int64_t rows_a = mode == kFwd ? M : N;
-  const int64_t rows_b = mode == kFwd ? E * N : K;
+  const int64_t rows_b = mode == kFwd ? n_experts * N : K;
   const int64_t out_cols = mode == kFwd ? N : K;
   const int64_t out_rows = mode == kFwd ? M : E * N;
   if (C % 32 != 0)
@@ -278,7 +287,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   const TileChoice tc = pick_tiles(out_cols);
   const int bn = tc.tile_n;
   const int pair = tc.tile_m / kBM;
-  const WsPlan ws = plan_workspace(mode, M, N, K, E, tc.tile_m, bn);
+  const WsPlan ws = plan_workspace(mode, M, N, K, E, n_experts, tc.tile_m, bn);
   const long long need = split_ok ? ws.total : ws.base;
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(MXGG_ERR_INVALID, "%s: workspace of %lld bytes (256-byte aligned) required, got %lld at %p", what,
@@ -335,6 +344,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.rows_b = (int)rows_b;
   p.contraction = (int)C;
   p.offs = offs;
+  p.group_expert = mode == kFwd ? group_expert : nullptr;
+  p.n_experts = (int)n_experts;
   p.stages = (int)ws.stages;
   p.out = out;
   p.out_ld = out_cols;
@@ -405,12 +416,12 @@ extern "C" {
 
 int64_t mxgg_grouped_mm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t E) {
   if (M < 0 || N < 0 || K < 0 || E < 1) return -1;
-  return workspace_upper_bound(kFwd, M, N, K, E);
+  return workspace_upper_bound(kFwd, M, N, K, E, E);
 }
 
 int64_t mxgg_wgrad_workspace_size(int64_t N, int64_t K, int64_t M, int64_t E) {
   if (M < 0 || N < 0 || K < 0 || E < 1) return -1;
-  return workspace_upper_bound(kWgrad, M, N, K, E);
+  return workspace_upper_bound(kWgrad, M, N, K, E, E);
 }
 
 int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
@@ -420,15 +431,30 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
                   workspace_bytes, stream);
 }
 
+int64_t mxgg_grouped_mm_segments_workspace_size(int64_t M, int64_t N, int64_t K, int64_t n_segments,
+                                                int64_t n_experts) {
+  if (M < 0 || N < 0 || K < 0 || n_segments < 1 || n_experts < 1) return -1;
+  return workspace_upper_bound(kFwd, M, N, K, n_segments, n_experts);
+}
+
+int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                             const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                             int64_t K, int64_t n_segments, int64_t n_experts, void* out, int out_dtype,
+                             void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!segment_expert && n_segments > 0) return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_segments: null segment_expert");
+  return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments");
+}
+
 int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
                             const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
                             void* out, int out_dtype, void* stream) {
   bool split_ok = true;
   if (M >= 0 && N >= 0 && K >= 0 && E >= 1) {
-    const int64_t need = workspace_upper_bound(kFwd, M, N, K, E, false);
+    const int64_t need = workspace_upper_bound(kFwd, M, N, K, E, E, false);
     // the split tail needs its partial tiles too; without room for them the
     // last round is dealt as whole tiles
-    split_ok = workspace_upper_bound(kFwd, M, N, K, E, true) <= kNoAllocScratchBytes;
+    split_ok = workspace_upper_bound(kFwd, M, N, K, E, E, true) <= kNoAllocScratchBytes;
     if (need > kNoAllocScratchBytes)
       return fail(MXGG_ERR_UNSUPPORTED,
                   "mxgg_grouped_mm_noalloc: this problem needs %lld bytes of scratch, more than the %lld-byte "

@@ -64,6 +64,8 @@ struct GemmParams {
   int rows_a, rows_b;        // rows of the A / B operand tensors (for clamping scale reads)
   int contraction;           // fwd: K, wgrad: M
   const int32_t* offs;       // (E,) cumulative group ends
+  const int32_t* group_expert;  // fwd: expert (B slice) of each group, or null for group g -> expert g
+  int n_experts;             // fwd: experts in B (E when group_expert is null)
   void* out;
   long long out_ld;          // elements per output row
   long long out_rows;        // rows of the output tensor
@@ -125,6 +127,7 @@ struct SmemLayout {
   int g_end[kMaxGroups];
   int g_cum[kMaxGroups + 1];
   int g_order[kMaxGroups];   // wgrad: groups by decreasing token count
+  int g_expert[kMaxGroups];  // fwd: B slice of each group
 
   // a and b are one contiguous region (the split-tile reduction spans both)
   static_assert(sizeof(a) % 1024 == 0, "stage buffers must be contiguous");
@@ -169,6 +172,10 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
     carry_sum += __shfl_sync(0xffffffffu, incl, 31);
   }
   if (lane == 0) sm->g_cum[p.E] = carry_sum;
+  // fwd: which B slice each group multiplies (clamped, so a bad index can
+  // never address memory outside B)
+  for (int i = lane; i < p.E; i += 32)
+    sm->g_expert[i] = p.group_expert ? min(max(__ldg(p.group_expert + i), 0), p.n_experts - 1) : i;
 }
 
 // wgrad work per tile is proportional to the group's token count: visit the
@@ -220,7 +227,8 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     const int g = lo;
     const int row0 = sm->g_start[g] + (m - sm->g_cum[g]) * TILE_M;
     u.a_row = row0;
-    u.b_row = g * p.N + n * BN;
+    const int ge = sm->g_expert[g];
+    u.b_row = ge * p.N + n * BN;
     u.out_row = row0;
     u.out_col = n * BN;
     u.valid_rows = min(TILE_M, sm->g_end[g] - row0);
@@ -229,7 +237,7 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     u.c_begin = 0;
     u.c_end = p.K;
     u.a_sub = m * (TILE_M / kBM);
-    u.b_tile = g * NT + n;
+    u.b_tile = ge * NT + n;
   } else {
     const int NT = cdiv_i(p.N, TILE_M);
     const int KT = cdiv_i(p.K, BN);

@@ -37,7 +37,7 @@ struct PackParams {
   long long sf_ld;       // bytes per scale row
   int vec;               // 4: 16-byte row loads are aligned, 1: 4-byte, 0: bytes
   int a_subtiles;        // A-side sub-tiles provisioned in the workspace
-  int b_tiles;           // B-side tiles
+  int b_tiles;           // B-side tiles (fwd: experts x n-tiles)
   uint8_t* a_out;
   uint8_t* b_out;
   int* zero;             // stream-K arrival counters to clear (or null)

@@ -27,6 +27,9 @@ SIGNATURES = {
     "mxgg_wgrad_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
     "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
+    "mxgg_grouped_mm_segments_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _int, _vp,
+                                        _i64, _vp]),
     "mxgg_grouped_mm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),

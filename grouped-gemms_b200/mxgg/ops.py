@@ -117,6 +117,40 @@ def _(a, b, a_scale, b_scale, offs, out_dtype):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
+# ------------------------------------------------------- grouped_mm_segments
+@torch.library.custom_op("mxgg::grouped_mm_segments", mutates_args=())
+def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
+                           seg_expert: Tensor, out_dtype: torch.dtype) -> Tensor:
+    """Rows of segment s times B[seg_expert[s]]: the layout an expert-parallel
+    all-to-all delivers (source-major, then expert)."""
+    _require_cuda(a, b, a_scale, b_scale, seg_offs, seg_expert, what="mxgg::grouped_mm_segments")
+    if out_dtype not in _OUT_DTYPES:
+        raise TypeError(f"mxgg::grouped_mm_segments: unsupported out_dtype {out_dtype}")
+    M, K = a.shape
+    E, N, _ = b.shape
+    S = seg_offs.shape[0]
+    a = a.contiguous()
+    b = b.contiguous()
+    a_scale = as_u8(a_scale).contiguous()
+    b_scale = as_u8(b_scale).contiguous()
+    seg_offs = seg_offs.to(torch.int32).contiguous()
+    seg_expert = seg_expert.to(torch.int32).contiguous()
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    lib = _lib.load()
+    ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), a.device)
+    with torch.cuda.device(a.device):
+        _lib.check(lib.mxgg_grouped_mm_segments(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
+                                                _ptr(seg_expert), M, N, K, S, E, _ptr(out), _OUT_DTYPES[out_dtype],
+                                                _ptr(ws), ws.numel(), _stream(a.device)),
+                   "mxgg_grouped_mm_segments")
+    return out
+
+
+@grouped_mm_segments_op.register_fake
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
+
+
 # --------------------------------------------------------------------- wgrad
 @torch.library.custom_op("mxgg::wgrad", mutates_args=())
 def wgrad_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,

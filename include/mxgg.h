@@ -97,6 +97,25 @@ int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, c
                             void* out, int out_dtype, void* stream);
 
 /*
+ * Forward grouped GEMM over segments that share experts: segment s (rows
+ * [segment_end_offsets[s-1], segment_end_offsets[s]) of A) is multiplied by
+ * B[segment_expert[s]].  This is the layout an expert-parallel all-to-all
+ * delivers (rows grouped by source rank, then by expert), so the GEMM reads
+ * the receive buffer as it lands.  No counterpart in the reference.
+ *   b        (n_experts, N, K) e4m3,   b_scale (n_experts, N, K/32)
+ *   segment_end_offsets (n_segments,) int32, device, cumulative
+ *   segment_expert      (n_segments,) int32, device, in [0, n_experts)
+ * Other arguments as mxgg_grouped_mm; the workspace is at least
+ * mxgg_grouped_mm_segments_workspace_size(M, N, K, n_segments, n_experts).
+ */
+int64_t mxgg_grouped_mm_segments_workspace_size(int64_t M, int64_t N, int64_t K, int64_t n_segments,
+                                                int64_t n_experts);
+int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                             const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                             int64_t K, int64_t n_segments, int64_t n_experts, void* out, int out_dtype,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Weight-gradient grouped GEMM: out[g] = GO_t[:, group g] @ X_t[:, group g]^T.
  * Replaces triton_mxfp8_wgrad (reference kernels/backward.py:217-305).
  *   go_t     (N, M) e4m3 (quantised along tokens)   go_scale (N, M/32)
