@@ -145,10 +145,11 @@ def build_problems(device, shapes, passes, seed=123):
     return probs
 
 
-def build_ep_problems(device, shapes, passes, world, rank, seed=123):
+def build_ep_problems(device, shapes, passes, world, rank, seed=123, impl="fused"):
     """Expert-parallel sweep: the same 36 shapes with every rank holding its
-    own M = 16640 tokens (offsets drawn as the single-GPU sweep draws them,
-    seeded per rank) and the weights of the experts it hosts.  fwd and dgrad
+    own M = 16640 tokens and the weights of the experts it hosts.  Group sizes
+    are the single-GPU sweep's (same seed and draw order), rotated by rank so
+    that every rank computes M rows.  fwd and dgrad
     run dispatch -> segment GEMM -> combine; wgrad runs on the hosting rank
     over the tokens it received (expert-major, as the forward's dispatch left
     them) and sums replicas' gradients with an all-reduce.  Per-rank FLOPs
@@ -158,7 +159,7 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123):
     import utils
     from mxgg import ep
 
-    random.seed(seed + 1000 * rank)
+    random.seed(seed)
     gen = torch.Generator(device=device).manual_seed(seed + 1000 * rank)
     probs = []
     groups = {}
@@ -167,7 +168,12 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123):
         if E not in groups:
             groups[E] = ep.replica_groups(pl)          # collective: same order on every rank
         offs = utils.generate_jagged_offs(E, M, multiple_of=32, device="cpu").tolist()
-        counts = [b - a for a, b in zip([0] + offs[:-1], offs)]
+        base = [b - a for a, b in zip([0] + offs[:-1], offs)]
+        # every rank routes the same jagged distribution, rotated so that every
+        # rank computes exactly M rows: the sweep measures dispatch, GEMM and
+        # combine, not a router's load imbalance
+        shift = (rank // pl.replicas) * pl.local
+        counts = [base[(e - shift) % E] for e in range(E)]
         plan = ep.plan_dispatch(pl, counts, device)
         mine = pl.experts_of(rank)
         gw = torch.Generator(device=device).manual_seed(seed + 77 * (mine[0] + 1))
@@ -176,14 +182,14 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123):
             A = torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=gen)
             a_s, a_q = utils.to_mx(A)
             w_s, w_q = utils.to_mx(Wl)
-            probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan,
+            probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan, counts=counts,
                               args=(a_q, a_s), weights=(w_q, w_s)))
             del A
         if "dgrad" in passes:
             G = torch.randn(M, N, device=device, dtype=torch.bfloat16, generator=gen)
             g_s, g_q = utils.to_mx(G)
             wt = [utils.to_mx_dim1(Wl[e]) for e in range(len(mine))]
-            probs.append(dict(pass_="dgrad", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan,
+            probs.append(dict(pass_="dgrad", shape=(E, M, N, K), flops=2.0 * M * N * K, plan=plan, counts=counts,
                               args=(g_q, g_s), weights=(torch.stack([q for _, q in wt]),
                                                         torch.stack([s_ for s_, _ in wt]))))
             del G
@@ -199,6 +205,16 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123):
                               args=(go_q, go_s, ia_q, ia_s, loffs), groups=groups[E]))
             del go, x
         del Wl
+    if impl == "fused" and any(p["pass_"] != "wgrad" for p in probs):
+        # one set of shared buffers sized for the whole sweep
+        import torch.distributed as dist
+        cap = torch.tensor([max(p["plan"].rows_recv for p in probs)], device=device)
+        dist.all_reduce(cap, op=dist.ReduceOp.MAX)
+        kmax = max(max(s[2], s[3]) for s in shapes)
+        fx = ep.FusedExpertParallel(ep.ExpertPlacement(world, world), int(cap.item()), M_TOKENS, kmax, kmax)
+        for p in probs:
+            if p["pass_"] != "wgrad":
+                p["fused"] = (fx, fx.plan(p["counts"], ep.ExpertPlacement(world, p["shape"][0])))
     torch.cuda.synchronize()
     return probs
 
@@ -218,6 +234,16 @@ def run_ep_problem(p, marks=None):
             marks[1].record()
         ep.replica_allreduce(plan.placement, out, p.get("groups"))
         if marks:
+            marks[2].record()
+        return out
+    if "fused" in p:
+        fx, fplan = p["fused"]
+        fx.dispatch(fplan, *p["args"])
+        if marks:
+            marks[0].record()
+        out = fx.compute(fplan, p["args"][0].shape[1], p["weights"][0], p["weights"][1], torch_bf16())
+        if marks:
+            marks[1].record()
             marks[2].record()
         return out
     recv_q, recv_s = ep.dispatch(plan, *p["args"])
@@ -562,6 +588,9 @@ def main():
                     help="GEMM work schedule: split the last partial round's tiles (split_tail, the default) "
                          "or deal whole tiles")
     ap.add_argument("--split-max", type=int, default=0, help="most pieces per split tile (0 = automatic)")
+    ap.add_argument("--ep-impl", default="fused", choices=["fused", "nccl"],
+                    help="N > 1: peer-memory dispatch with the combine fused into the GEMM (fused), "
+                         "or NCCL all-to-all dispatch/combine around the segment GEMM (nccl)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -606,8 +635,10 @@ def main():
 
     ep_mode = world > 1
     if ep_mode:
-        probs = build_ep_problems(dev, [shapes[i] for i in idx], passes, world, rank)
-        cfg["parallelism"] = f"ep{world} (expert parallel: NCCL all-to-all dispatch/combine)"
+        probs = build_ep_problems(dev, [shapes[i] for i in idx], passes, world, rank, impl=args.ep_impl)
+        cfg["parallelism"] = (f"ep{world} (expert parallel: peer-memory dispatch, combine fused into the GEMM "
+                              "epilogue over NVLink)" if args.ep_impl == "fused" else
+                              f"ep{world} (expert parallel: NCCL all-to-all dispatch/combine)")
         cfg["M"] = f"{M_TOKENS} tokens per rank"
     else:
         probs = build_problems(dev, [shapes[i] for i in idx], passes)
@@ -696,6 +727,8 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier(world)
+        for fx in {id(p["fused"][0]): p["fused"][0] for p in probs if "fused" in p}.values():
+            fx.close()
         import torch.distributed as dist
         dist.destroy_process_group()
     return 0

@@ -15,6 +15,7 @@
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
 #include "scale_pack.cuh"
+#include "peer.cuh"
 #include "tile_map.cuh"
 
 namespace mxgg {
@@ -127,7 +128,8 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
 constexpr int kMaxGridCtas = 160;
 
 struct Maps {
-  CUtensorMap a, b, sfa, sfb, out;
+  CUtensorMap a, b, sfa, sfb;
+  OutMaps out;
 };
 
 template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
@@ -238,6 +240,17 @@ int pick_group_m(const TileChoice& c) {
   return c.tile_m == 128 ? 2 : 16;
 }
 
+// Expert-parallel output routing of a forward call (see GemmParams).
+struct EpRoute {
+  const int32_t* group_dst = nullptr;
+  const int32_t* group_dst_row = nullptr;
+  int n_dst = 0;
+  int local_dst = 0;
+  void* out_dst[kMaxDst] = {};
+  int64_t rows_dst[kMaxDst] = {};
+  void* inbox_dst[kMaxDst] = {};   // all null: peers' rows are stored in place
+};
+
 // split_ok = 0: the caller's scratch only needs the packed scales and the
 // tail of the schedule is dealt as whole tiles.
 // Forward groups may be segments that share B slices: group g multiplies
@@ -246,7 +259,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
              void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
              const int32_t* group_expert = nullptr, int64_t n_experts = -1,
-             const char* what = nullptr) {
+             const char* what = nullptr, const EpRoute* route = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (n_experts < 0) n_experts = E;
@@ -262,11 +275,27 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   const int64_t rows_a = mode == kFwd ? M : N;
   const int64_t rows_b = mode == kFwd ? n_experts * N : K;
   const int64_t out_cols = mode == kFwd ? N : K;
-  const int64_t out_rows = mode == kFwd ? M : E * N;
+  int64_t out_rows = mode == kFwd ? M : E * N;
   if (C % 32 != 0)
     return fail(MXGG_ERR_INVALID, "%s: contraction length %lld must be a multiple of 32", what, (long long)C);
-  if (out_rows == 0 || out_cols == 0) return MXGG_OK;
-  if (!out) return fail(MXGG_ERR_INVALID, "%s: null output", what);
+  const int es_out = out_esize(out_dtype);
+  if (route) {
+    if (mode != kFwd || route->n_dst < 1 || route->n_dst > kMaxDst || route->local_dst < 0 ||
+        route->local_dst >= route->n_dst || !route->group_dst || !route->group_dst_row)
+      return fail(MXGG_ERR_INVALID, "%s: bad expert-parallel routing (n_dst %d, local %d)", what, route->n_dst,
+                  route->local_dst);
+    if (C == 0 || (out_cols * es_out) % 16 != 0)
+      return fail(MXGG_ERR_UNSUPPORTED, "%s: expert-parallel outputs need K > 0 and 16-byte output rows", what);
+    for (int i = 0; i < route->n_dst; ++i)
+      if (route->rows_dst[i] < 0 || (route->rows_dst[i] > 0 && (!route->out_dst[i] || !aligned(route->out_dst[i], 16))))
+        return fail(MXGG_ERR_INVALID, "%s: destination %d needs a 16-byte aligned output", what, i);
+    out = route->out_dst[route->local_dst];
+    out_rows = route->rows_dst[route->local_dst];
+    if (M == 0 || out_cols == 0) return MXGG_OK;
+  } else {
+    if (out_rows == 0 || out_cols == 0) return MXGG_OK;
+    if (!out) return fail(MXGG_ERR_INVALID, "%s: null output", what);
+  }
   const int64_t lim = (int64_t)1 << 31;
   if (rows_a >= lim || rows_b >= lim || out_rows >= lim || C >= lim || out_cols >= lim)
     return fail(MXGG_ERR_UNSUPPORTED, "%s: extents beyond 2^31", what);
@@ -352,7 +381,27 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.out_rows = out_rows;
   p.out_cols = (int)out_cols;
   const int es = out_esize(out_dtype);
-  p.tma_store = aligned(out, 16) && ((out_cols * es) % 16 == 0);
+  p.tma_store = out_rows > 0 && aligned(out, 16) && ((out_cols * es) % 16 == 0);
+  if (route) {
+    p.group_dst = route->group_dst;
+    p.group_dst_row = route->group_dst_row;
+    p.n_dst = route->n_dst;
+    p.local_dst = route->local_dst;
+    bool inbox = (out_cols * es) % 64 == 0;
+    for (int i = 0; i < route->n_dst; ++i) {
+      p.out_dst[i] = route->out_dst[i];
+      p.out_rows_dst[i] = route->rows_dst[i];
+      p.inbox_dst[i] = route->inbox_dst[i];
+      if (i != route->local_dst && route->rows_dst[i] > 0 && (!route->inbox_dst[i] || !aligned(route->inbox_dst[i], 16)))
+        inbox = false;
+    }
+    p.inbox_chunks = inbox ? (int)((out_cols * es) / 64) : 0;
+  } else {
+    p.n_dst = 1;
+    p.local_dst = 0;
+    p.out_dst[0] = out;
+    p.out_rows_dst[0] = out_rows;
+  }
   p.group_m = pick_group_m(tc);
   p.split_tail = split_tail ? 1 : 0;
   p.split_max = g_split_max;
@@ -374,12 +423,20 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                             (uint64_t)(ws.b_tiles * ws.stages * 4 * (bn / 128)), 128, 128, 128, 4 * (bn / 128),
                             CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
-  if (p.tma_store) {
-    if (int rc = make_tmap_2d(&maps.out, out, out_tmap_dtype(out_dtype), es, (uint64_t)out_rows, (uint64_t)out_cols,
-                              (uint64_t)out_cols, 64 / es, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+  std::memset(&maps.out, 0, sizeof(maps.out));
+  if (route) {
+    // one map per destination with rows (the peers' outputs take TMA stores too)
+    for (int i = 0; i < route->n_dst; ++i) {
+      if (route->rows_dst[i] <= 0) continue;
+      if (int rc = make_tmap_2d(&maps.out.m[i], route->out_dst[i], out_tmap_dtype(out_dtype), es,
+                                (uint64_t)route->rows_dst[i], (uint64_t)out_cols, (uint64_t)out_cols, 64 / es, 32,
+                                CU_TENSOR_MAP_SWIZZLE_64B))
+        return rc;
+    }
+  } else if (p.tma_store) {
+    if (int rc = make_tmap_2d(&maps.out.m[0], out, out_tmap_dtype(out_dtype), es, (uint64_t)out_rows,
+                              (uint64_t)out_cols, (uint64_t)out_cols, 64 / es, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return rc;
-  } else {
-    std::memset(&maps.out, 0, sizeof(maps.out));
   }
 
   long long max_units;
@@ -545,6 +602,107 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
   } else {
     return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown mode %d", mode);
   }
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                       const int32_t* segment_end_offsets, const int32_t* segment_expert, const int32_t* segment_dst,
+                       const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
+                       int64_t n_experts, void* const* dst_out, const int64_t* dst_rows, void* const* dst_inbox,
+                       int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace, int64_t workspace_bytes,
+                       void* stream) {
+  if (!segment_expert || !dst_out || !dst_rows)
+    return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: null segment or destination table");
+  if (n_dst < 1 || n_dst > kMaxDst)
+    return fail(MXGG_ERR_UNSUPPORTED, "mxgg_grouped_mm_ep: %d destinations (1..%d)", (int)n_dst, kMaxDst);
+  EpRoute r;
+  r.group_dst = segment_dst;
+  r.group_dst_row = segment_dst_row;
+  r.n_dst = n_dst;
+  r.local_dst = local_dst;
+  for (int i = 0; i < n_dst; ++i) {
+    r.out_dst[i] = dst_out[i];
+    r.rows_dst[i] = dst_rows[i];
+    r.inbox_dst[i] = dst_inbox ? dst_inbox[i] : nullptr;
+  }
+  return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, nullptr, out_dtype,
+                  workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r);
+}
+
+int mxgg_ipc_alloc(int64_t bytes, void** ptr, void* handle) {
+  if (bytes <= 0 || !ptr || !handle) return fail(MXGG_ERR_INVALID, "mxgg_ipc_alloc: bad arguments");
+  void* p = nullptr;
+  MXGG_CUDA_TRY(cudaMalloc(&p, (size_t)bytes));
+  if (cudaError_t e = cudaMemset(p, 0, (size_t)bytes)) {
+    cudaFree(p);
+    return fail(MXGG_ERR_CUDA, "mxgg_ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaError_t e = cudaIpcGetMemHandle(&h, p)) {
+    cudaFree(p);
+    return fail(MXGG_ERR_CUDA, "mxgg_ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return MXGG_OK;
+}
+
+int mxgg_ipc_free(void* ptr) {
+  MXGG_CUDA_TRY(cudaFree(ptr));
+  return MXGG_OK;
+}
+
+int mxgg_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(MXGG_ERR_INVALID, "mxgg_ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  MXGG_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MXGG_OK;
+}
+
+int mxgg_ipc_close(void* ptr) {
+  MXGG_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return MXGG_OK;
+}
+
+int mxgg_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes < 0) return fail(MXGG_ERR_INVALID, "mxgg_copy_async: negative size");
+  if (bytes == 0) return MXGG_OK;
+  MXGG_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+  return MXGG_OK;
+}
+
+int mxgg_peer_barrier(void* const* flags, int32_t world, int32_t rank, int32_t epoch, void* stream) {
+  if (!flags || world < 1 || world > kMaxDst || rank < 0 || rank >= world)
+    return fail(MXGG_ERR_INVALID, "mxgg_peer_barrier: bad arguments (world %d, rank %d)", (int)world, (int)rank);
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  PeerFlags f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i]) return fail(MXGG_ERR_INVALID, "mxgg_peer_barrier: null flag array of rank %d", i);
+    f.flags[i] = static_cast<int*>(flags[i]);
+  }
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch, st->status);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_inbox_unpack(const void* inbox, void* out, const int32_t* row_blocks, int64_t n_row_blocks,
+                      int64_t row_bytes, void* stream) {
+  if (n_row_blocks < 0 || row_bytes <= 0 || row_bytes % 64 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_inbox_unpack: row_bytes %lld must be a positive multiple of 64",
+                (long long)row_bytes);
+  if (n_row_blocks == 0) return MXGG_OK;
+  if (!inbox || !out || !row_blocks || !aligned(inbox, 16) || !aligned(out, 16))
+    return fail(MXGG_ERR_INVALID, "mxgg_inbox_unpack: null or unaligned pointer");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long warps = n_row_blocks * (row_bytes / 64);
+  const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
+  inbox_unpack_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(inbox), static_cast<uint8_t*>(out), row_blocks, (int)n_row_blocks,
+      (int)(row_bytes / 64), (long long)row_bytes);
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
 }

@@ -43,6 +43,7 @@ constexpr int kBM = 128;          // rows per CTA (MMA M per CTA)
 constexpr int kBK = 128;          // contraction elements per stage (= one 128 B swizzle row of e4m3)
 constexpr int kThreads = 256;
 constexpr int kMaxGroups = 256;   // groups handled by the in-kernel table
+constexpr int kMaxDst = 8;        // output destinations (ranks) of an expert-parallel forward
 constexpr int kTmemCols = 512;
 
 enum : int { kFwd = 0, kWgrad = 1 };
@@ -78,6 +79,30 @@ struct GemmParams {
   float* part_slots;         // split tiles: one fp32 128 x BN partial per CTA of the grid
   int* part_counters;        // split tiles: arrivals per (tail tile, CTA of the pair, epilogue warp), zeroed before the launch
   uint32_t* status;          // error word (device memory), 0 = ok
+  // Expert-parallel output routing (fwd): group g's rows are stored to
+  // destination group_dst[g] (an output buffer, possibly a peer GPU's) from
+  // row group_dst_row[g] on.  Null group_dst: every group writes `out` at its
+  // own rows.  The local destination uses the TMA store map; peers get plain
+  // 16-byte stores over NVLink.
+  const int32_t* group_dst;
+  const int32_t* group_dst_row;
+  int n_dst;
+  int local_dst;
+  void* out_dst[kMaxDst];
+  long long out_rows_dst[kMaxDst];
+  // Peer inboxes (optional): a peer's full 32-row x 64-byte output blocks go
+  // to its inbox as contiguous 2 KB bulk copies, block (row / 32, byte column
+  // / 64) at ((row / 32) * inbox_chunks + column / 64) * 2048, in the
+  // staging buffer's 64-byte swizzle; the owner unpacks them.  NVLink moves
+  // 2 KB runs at several times the rate of 64-byte row pieces.
+  void* inbox_dst[kMaxDst];
+  int inbox_chunks;          // 64-byte chunks per output row; 0: no inboxes
+};
+
+// Output tensor maps: [0] the output of a single-GPU call; for an
+// expert-parallel call, one per destination (index = destination).
+struct OutMaps {
+  CUtensorMap m[kMaxDst];
 };
 
 struct Unit {
@@ -92,6 +117,7 @@ struct Unit {
   int c_end;
   int a_sub;         // packed A-scale sub-tile of the tile's first 128 rows
   int b_tile;        // packed B-scale tile
+  int dst;           // output destination (0 unless expert-parallel routing)
   // a stage range of a tail tile that other CTA pairs share
   int split;         // 1: publish a partial; the last pair to arrive writes the tile
   int tail;          // index of the tile in the tail round (its arrival counter)
@@ -128,6 +154,8 @@ struct SmemLayout {
   int g_cum[kMaxGroups + 1];
   int g_order[kMaxGroups];   // wgrad: groups by decreasing token count
   int g_expert[kMaxGroups];  // fwd: B slice of each group
+  int g_dst[kMaxGroups];     // fwd, expert parallel: output destination of each group
+  int g_dst_row[kMaxGroups]; //   and its first row there
 
   // a and b are one contiguous region (the split-tile reduction spans both)
   static_assert(sizeof(a) % 1024 == 0, "stage buffers must be contiguous");
@@ -174,8 +202,16 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
   if (lane == 0) sm->g_cum[p.E] = carry_sum;
   // fwd: which B slice each group multiplies (clamped, so a bad index can
   // never address memory outside B)
-  for (int i = lane; i < p.E; i += 32)
+  for (int i = lane; i < p.E; i += 32) {
     sm->g_expert[i] = p.group_expert ? min(max(__ldg(p.group_expert + i), 0), p.n_experts - 1) : i;
+    if (p.group_dst) {
+      sm->g_dst[i] = min(max(__ldg(p.group_dst + i), 0), p.n_dst - 1);
+      sm->g_dst_row[i] = max(__ldg(p.group_dst_row + i), 0);
+    } else {
+      sm->g_dst[i] = 0;
+      sm->g_dst_row[i] = -1;
+    }
+  }
 }
 
 // wgrad work per tile is proportional to the group's token count: visit the
@@ -204,6 +240,7 @@ template <int BN, int TILE_M, class S>
 __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, int t) {
   Unit u;
   u.split = 0;
+  u.dst = 0;
   u.tail = 0;
   u.n_contrib = 1;
   u.p0 = 0;
@@ -229,7 +266,8 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     u.a_row = row0;
     const int ge = sm->g_expert[g];
     u.b_row = ge * p.N + n * BN;
-    u.out_row = row0;
+    u.dst = sm->g_dst[g];
+    u.out_row = (sm->g_dst_row[g] >= 0) ? (long long)sm->g_dst_row[g] + (row0 - sm->g_start[g]) : row0;
     u.out_col = n * BN;
     u.valid_rows = min(TILE_M, sm->g_end[g] - row0);
     u.st_begin = 0;
@@ -351,7 +389,7 @@ template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                        const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
+                        const __grid_constant__ OutMaps omaps, const GemmParams p) {
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
   static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
   static_assert(ACC == 2, "two accumulator buffers (overlapping when 2*BN does not fit)");
@@ -419,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmap_b);
     ptx::prefetch_tmap(&tmap_sfa);
     ptx::prefetch_tmap(&tmap_sfb);
-    ptx::prefetch_tmap(&tmap_out);
+    ptx::prefetch_tmap(&omaps.m[p.local_dst]);
   }
   if (warp == 1) {
     if constexpr (PAIR == 2) {
@@ -654,7 +692,67 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = pack2<OutT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
         }
-        if (use_tma) {
+        if (u.dst != p.local_dst && rows_here < 32) {
+          // A peer GPU's output, rows cut by the group edge: stage the warp's
+          // rows x 64 B, then store them with 4 lanes per row, so each row's
+          // 64 bytes cross NVLink as one contiguous run.  Output rows are
+          // 16-byte aligned (host check).  Full 32-row blocks go by TMA below.
+          uint8_t* stg = sm->epi[q][buf];
+          if (lane == 0) ptx::bulk_wait_read<1>();   // a TMA store may still read this buffer
+          __syncwarp();
+          const uint32_t stg_u = ptx::smem_u32(stg);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t chunk = (uint32_t)(j ^ ((lane >> 1) & 3));   // 64 B swizzle
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(stg_u + lane * 64 + chunk * 16),
+                         "r"(w[4 * j]), "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                         : "memory");
+          }
+          __syncwarp();
+          OutT* base = reinterpret_cast<OutT*>(p.out_dst[u.dst]);
+          const long long lim = p.out_rows_dst[u.dst];
+          const int ncols = min(kEpiCols, p.out_cols - col0);
+          constexpr int kPer16 = 16 / (int)sizeof(OutT);
+          const int j = lane & 3;
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) {
+            const int r = pp * 8 + (lane >> 2);
+            const long long orow = u.out_row + my_row0 + r;
+            uint4 val;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                         : "r"(stg_u + r * 64 + ((uint32_t)(j ^ ((r >> 1) & 3))) * 16)
+                         : "memory");
+            if (r < rows_here && orow < lim && (j + 1) * kPer16 <= ncols)
+              *reinterpret_cast<uint4*>(base + orow * p.out_ld + col0 + j * kPer16) = val;
+          }
+          __syncwarp();
+          buf ^= 1;
+          return;
+        }
+        if (u.dst != p.local_dst && p.inbox_chunks > 0) {
+          uint8_t* stg = sm->epi[q][buf];
+          if (lane == 0) ptx::bulk_wait_read<1>();   // the copy that last used this buffer has read it
+          __syncwarp();
+          const uint32_t row_base = ptx::smem_u32(stg) + lane * 64;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t chunk = (uint32_t)(j ^ ((lane >> 1) & 3));   // 64 B swizzle
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(row_base + chunk * 16),
+                         "r"(w[4 * j]), "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                         : "memory");
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const long long blk = ((u.out_row + my_row0) >> 5) * p.inbox_chunks + (col0 * (int)sizeof(OutT)) / 64;
+            ptx::bulk_store(static_cast<uint8_t*>(p.inbox_dst[u.dst]) + blk * 2048, ptx::smem_u32(stg), 2048);
+            ptx::bulk_commit();
+          }
+          buf ^= 1;
+          return;
+        }
+        if (use_tma || u.dst != p.local_dst) {
           uint8_t* stg = sm->epi[q][buf];
           if (lane == 0) ptx::bulk_wait_read<1>();   // the store that last used this buffer has read it
           __syncwarp();
@@ -669,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_2d(&tmap_out, ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
+            ptx::tma_store_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
             ptx::bulk_commit();
           }
           buf ^= 1;
@@ -805,6 +903,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) ptx::bulk_wait<0>();
     __syncwarp();
+    // expert parallel: peers read this GPU's stores after a system-scope flag
+    if (p.n_dst > 1) __threadfence_system();
   }
 
   // ------------------------------------------------------------ teardown

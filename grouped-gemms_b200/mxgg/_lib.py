@@ -30,6 +30,16 @@ SIGNATURES = {
     "mxgg_grouped_mm_segments_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _int, _vp,
                                         _i64, _vp]),
+    "mxgg_grouped_mm_ep": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                  ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_vp), _i32, _i32, _int,
+                                  _vp, _i64, _vp]),
+    "mxgg_inbox_unpack": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "mxgg_ipc_alloc": (_int, [_i64, ctypes.POINTER(_vp), ctypes.c_char_p]),
+    "mxgg_ipc_free": (_int, [_vp]),
+    "mxgg_ipc_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "mxgg_ipc_close": (_int, [_vp]),
+    "mxgg_copy_async": (_int, [_vp, _vp, _i64, _vp]),
+    "mxgg_peer_barrier": (_int, [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp]),
     "mxgg_grouped_mm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),

@@ -196,3 +196,226 @@ def replica_groups(placement: ExpertPlacement) -> dict:
         ranks = tuple(range(e * placement.replicas, (e + 1) * placement.replicas))
         out[ranks] = dist.new_group(list(ranks))
     return out
+
+
+# ----------------------------------------------------------------------------
+# Fused path: peer-memory dispatch, combine fused into the GEMM epilogue.
+# ----------------------------------------------------------------------------
+@dataclass
+class FusedPlan:
+    """Routing of one fused expert-parallel call, as seen by one rank."""
+
+    rows_local: int
+    rows_recv: int
+    copies: List[tuple]          # (dest rank, first row there, first local row, rows)
+    seg_offs: Tensor             # (world * L,) int32 cumulative ends of the received segments
+    seg_expert: Tensor           # (world * L,) local expert of each segment
+    seg_dst: Tensor              # (world * L,) rank that owns each segment's rows
+    seg_dst_row: Tensor          # (world * L,) first row of the segment in its owner's output
+    dst_rows: List[int]          # local rows of every rank (the output buffers' heights)
+    inbox_ok: bool               # every segment starts on a 32-row boundary: peers' blocks go by inbox
+    remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
+
+
+class FusedExpertParallel:
+    """Expert-parallel forward / dgrad over NVLink peer memory.
+
+    Collective to construct (it allocates and maps the shared buffers).  Per
+    call (`grouped_mm`):
+
+    1. each rank pushes its rows for rank d straight into d's receive buffer
+       (one copy-engine ``cudaMemcpyAsync`` per destination, destinations on
+       parallel streams), then a cross-GPU barrier;
+    2. ``mxgg_grouped_mm_ep`` multiplies the received segments and sends each
+       output block to the rank that owns its rows as the tile finishes (TMA
+       stores for its own rows; 2 KB bulk copies into the owner's inbox for
+       peers'), so the return trip overlaps the math tile by tile;
+    3. a second barrier, then each rank unpacks its inbox into its output.
+
+    The returned tensor is a view of this rank's shared output buffer: use it
+    before the next call.
+    """
+
+    def __init__(self, placement: ExpertPlacement, max_recv_rows: int, max_local_rows: int, max_k: int, max_n: int,
+                 group=None):
+        from .peer import PeerBuffer
+        dist = _dist()
+        self.placement = placement
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world != placement.world:
+            raise ValueError("placement and process group disagree on the world size")
+        if self.world > 8:
+            raise ValueError("the fused path reaches at most 8 ranks (one NVLink domain)")
+        self.max_recv_rows, self.max_local_rows = int(max_recv_rows), int(max_local_rows)
+        self.max_k, self.max_n = int(max_k), int(max_n)
+        self.recv_a = PeerBuffer(max(self.max_recv_rows * self.max_k, 256), group)
+        self.recv_s = PeerBuffer(max(self.max_recv_rows * self.max_k // 32, 256), group)
+        self.out = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
+        self.inbox = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
+        self.flags = PeerBuffer(256, group)
+        self.epoch = 0
+        self._streams = [torch.cuda.Stream() for _ in range(self.world)]
+        # every rank's capacities, so a plan that overflows any of them fails on all ranks alike
+        caps = [None] * self.world
+        dist.all_gather_object(caps, (self.max_recv_rows, self.max_local_rows), group=group)
+        self._caps = caps
+
+    def close(self) -> None:
+        for b in (self.recv_a, self.recv_s, self.out, self.inbox, self.flags):
+            b.close()
+
+    # -------------------------------------------------------------- planning
+    def plan(self, expert_counts: Sequence[int], placement: Optional[ExpertPlacement] = None) -> FusedPlan:
+        """Collective: all-gather every rank's per-expert counts and derive the
+        copies, segment tables and output heights.  The shared buffers do not
+        depend on the placement, so one instance serves several (`placement`
+        overrides the constructor's for this plan)."""
+        dist = _dist()
+        pl, world, rank = placement or self.placement, self.world, self.rank
+        if pl.world != world:
+            raise ValueError("placement and process group disagree on the world size")
+        E = pl.n_experts
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mine = torch.tensor([int(c) for c in expert_counts], dtype=torch.int64, device=dev)
+        if mine.numel() != E or bool((mine < 0).any()):
+            raise ValueError("expert_counts must hold E non-negative counts")
+        allc = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allc, mine, group=self.group)
+        C = [t.tolist() for t in allc]                       # C[s][e]
+        # rows rank s sends to rank d, and where they start in s's local order
+        send = [[0] * world for _ in range(world)]
+        start = [[None] * world for _ in range(world)]
+        for s in range(world):
+            row = 0
+            for e in range(E):
+                d = pl.dest(s, e)
+                if start[s][d] is None:
+                    start[s][d] = row
+                send[s][d] += C[s][e]
+                row += C[s][e]
+        # receive layout of rank d: source-major, then local expert
+        recv_off = [[sum(send[s2][d] for s2 in range(s)) for d in range(world)] for s in range(world)]
+        copies = [(d, recv_off[rank][d], start[rank][d] or 0, send[rank][d]) for d in range(world) if send[rank][d]]
+        offs, expert, dsts, dst_rows_first = [], [], [], []
+        total = 0
+        mine_e = pl.experts_of(rank)
+        for s in range(world):
+            for le, e in enumerate(mine_e):
+                rows = C[s][e] if pl.dest(s, e) == rank else 0
+                total += rows
+                offs.append(total)
+                expert.append(le)
+                dsts.append(s)
+                dst_rows_first.append(sum(C[s][:e]))
+        rows_local = sum(C[rank])
+        for d in range(world):
+            need_recv = sum(send[s][d] for s in range(world))
+            if need_recv > self._caps[d][0] or sum(C[d]) > self._caps[d][1]:
+                raise ValueError(f"fused EP buffers of rank {d} too small: {need_recv} received / {sum(C[d])} "
+                                 f"local rows for {self._caps[d][0]} / {self._caps[d][1]}")
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+        inbox_ok = all(c % 32 == 0 for row in C for c in row)
+        blocks, row = [], 0
+        for e in range(E):
+            if pl.dest(rank, e) != rank:
+                blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
+            row += C[rank][e]
+        return FusedPlan(rows_local=rows_local, rows_recv=total, copies=copies, seg_offs=i32(offs),
+                         seg_expert=i32(expert), seg_dst=i32(dsts), seg_dst_row=i32(dst_rows_first),
+                         dst_rows=[sum(C[d]) for d in range(world)], inbox_ok=inbox_ok,
+                         remote_blocks=i32(blocks if inbox_ok else []))
+
+    # ---------------------------------------------------------------- calls
+    def barrier(self) -> None:
+        """Cross-GPU barrier on the current stream (bounded wait on the device)."""
+        import ctypes
+        from . import _lib
+        self.epoch += 1
+        arr = (ctypes.c_void_p * self.world)(*self.flags.ptrs)
+        _lib.check(_lib.load().mxgg_peer_barrier(arr, self.world, self.rank, self.epoch,
+                                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                   "mxgg_peer_barrier")
+
+    def dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
+        """Push this rank's rows into the owners' receive buffers, then barrier."""
+        import ctypes
+        from . import _lib
+        lib = _lib.load()
+        K = a_q.shape[1]
+        if K > self.max_k:
+            raise ValueError(f"K={K} exceeds the buffers' {self.max_k}")
+        a_q = a_q.contiguous()
+        a_s = a_s.contiguous()
+        cur = torch.cuda.current_stream()
+        ready = cur.record_event()
+        done = []
+        for (d, dst_row, src_row, rows) in plan.copies:
+            st = self._streams[d]
+            st.wait_event(ready)
+            sp = ctypes.c_void_p(st.cuda_stream)
+            _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_a.ptrs[d] + dst_row * K),
+                                           ctypes.c_void_p(a_q.data_ptr() + src_row * K), rows * K, sp),
+                       "mxgg_copy_async")
+            _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_s.ptrs[d] + dst_row * (K // 32)),
+                                           ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)), rows * (K // 32),
+                                           sp), "mxgg_copy_async")
+            done.append(st.record_event())
+            # the caching allocator must not hand the sources out before the copies finish
+            a_q.record_stream(st)
+            a_s.record_stream(st)
+        for ev in done:
+            cur.wait_event(ev)
+        self.barrier()
+
+    def grouped_mm(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s: Tensor,
+                   out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """Fused forward / dgrad: returns (rows_local, N) in this rank's row order."""
+        import ctypes
+        from . import _lib
+        from .ops import _OUT_DTYPES, _workspace, as_u8
+        lib = _lib.load()
+        K = a_q.shape[1]
+        L, N, Kw = w_q.shape
+        if Kw != K:
+            raise AssertionError(f"K mismatch: activations {K}, weights {Kw}")
+        if N > self.max_n:
+            raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
+        self.dispatch(plan, a_q, a_s)
+        return self.compute(plan, K, w_q, w_s, out_dtype)
+
+    def compute(self, plan: FusedPlan, K: int, w_q: Tensor, w_s: Tensor,
+                out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """The GEMM over rows already dispatched (`dispatch`), its peer stores
+        and the closing barrier."""
+        import ctypes
+        from . import _lib
+        from .ops import _OUT_DTYPES, _workspace, as_u8
+        lib = _lib.load()
+        L, N, _ = w_q.shape
+        R = plan.rows_recv
+        recv_q = self.recv_a.view((R, K), torch.uint8)
+        recv_s = self.recv_s.view((R, K // 32), torch.uint8)
+        S = plan.seg_offs.numel()
+        ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(R, N, K, S, L), w_q.device)
+        outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
+        rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
+        inboxes = (ctypes.c_void_p * self.world)(*self.inbox.ptrs) if plan.inbox_ok else None
+        w_q = w_q.contiguous()
+        w_s = as_u8(w_s).contiguous()
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _lib.check(lib.mxgg_grouped_mm_ep(p(recv_q), p(w_q), p(recv_s), p(w_s), p(plan.seg_offs), p(plan.seg_expert),
+                                          p(plan.seg_dst), p(plan.seg_dst_row), R, N, K, S, L, outs, rows, inboxes,
+                                          self.world, self.rank, _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                   "mxgg_grouped_mm_ep")
+        self.barrier()
+        es = torch.empty((), dtype=out_dtype).element_size()
+        if plan.inbox_ok and plan.remote_blocks.numel() and (N * es) % 64 == 0:
+            _lib.check(lib.mxgg_inbox_unpack(ctypes.c_void_p(self.inbox.ptrs[self.rank]),
+                                             ctypes.c_void_p(self.out.ptrs[self.rank]), p(plan.remote_blocks),
+                                             plan.remote_blocks.numel(), N * es,
+                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                       "mxgg_inbox_unpack")
+        return self.out.view((plan.rows_local, N), out_dtype)

@@ -116,6 +116,60 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
                              void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Expert-parallel forward with the combine fused into the epilogue: as
+ * mxgg_grouped_mm_segments, but segment s's output rows are stored to
+ * destination segment_dst[s] from row segment_dst_row[s] on, where
+ * destination d is the (rows dst_rows[d], N) output buffer dst_out[d] --
+ * typically rank d's output, mapped into this process by mxgg_ipc_open.
+ * The local destination (local_dst) is written with TMA stores, the others
+ * over NVLink, so the return all-to-all overlaps the math tile by tile.
+ * With dst_inbox (a HOST array of n_dst buffers as large as the outputs, or
+ * null), a peer's full 32-row x 64-byte blocks travel as contiguous 2 KB
+ * bulk copies into its inbox, which its owner unpacks with
+ * mxgg_inbox_unpack; this needs every segment to start on a 32-row boundary
+ * of its destination and N * element size % 64 == 0 (otherwise, and for
+ * partial blocks, rows are stored in place with 16-byte stores).  dst_out
+ * and dst_rows are HOST arrays of n_dst <= 8 entries; segment_dst /
+ * segment_dst_row are device int32 arrays.  Output rows must be 16-byte
+ * aligned (N * element size % 16 == 0).  Peers may read their outputs (and
+ * unpack their inboxes) after a later mxgg_peer_barrier on every rank.  No
+ * counterpart in the reference (its path is single-GPU).
+ */
+int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                       const int32_t* segment_end_offsets, const int32_t* segment_expert, const int32_t* segment_dst,
+                       const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
+                       int64_t n_experts, void* const* dst_out, const int64_t* dst_rows, void* const* dst_inbox,
+                       int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace, int64_t workspace_bytes,
+                       void* stream);
+
+/* Copies the listed 32-row blocks (device int32 row-block indices) of an
+ * inbox filled by peers' mxgg_grouped_mm_ep into the row-major output whose
+ * rows are row_bytes long (a multiple of 64). */
+int mxgg_inbox_unpack(const void* inbox, void* out, const int32_t* row_blocks, int64_t n_row_blocks,
+                      int64_t row_bytes, void* stream);
+
+/* Device memory shared between the processes of one node (CUDA IPC).
+ * mxgg_ipc_alloc: cudaMalloc + zero-fill + a 64-byte handle another process
+ * can open with mxgg_ipc_open (peer access enabled on first use).  Close what
+ * you opened before the owner frees it. */
+int mxgg_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int mxgg_ipc_free(void* ptr);
+int mxgg_ipc_open(const void* handle, void** ptr);
+int mxgg_ipc_close(void* ptr);
+
+/* One cudaMemcpyAsync (peer copies travel over NVLink on a copy engine). */
+int mxgg_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
+/* Cross-GPU barrier on `stream`: writes `epoch` into slot `rank` of every
+ * rank's flag array (flags[r] = rank r's array of `world` int32, HOST array
+ * of device pointers), then waits until this rank's own array holds `epoch`
+ * (or later) in every slot.  Every rank calls it with the same epoch, which
+ * must grow from call to call (flag arrays start at 0).  Work earlier on the
+ * stream is visible to peers' work after their barrier.  The wait gives up
+ * after 1 s and sets bit 64 in the device status word. */
+int mxgg_peer_barrier(void* const* flags, int32_t world, int32_t rank, int32_t epoch, void* stream);
+
+/*
  * Weight-gradient grouped GEMM: out[g] = GO_t[:, group g] @ X_t[:, group g]^T.
  * Replaces triton_mxfp8_wgrad (reference kernels/backward.py:217-305).
  *   go_t     (N, M) e4m3 (quantised along tokens)   go_scale (N, M/32)

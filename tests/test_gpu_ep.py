@@ -1,4 +1,6 @@
-"""Expert-parallel grouped GEMM on 2 GPUs over NCCL (skipped with fewer).
+"""Expert-parallel grouped GEMM on 2 GPUs (skipped with fewer): NCCL
+all-to-all dispatch/combine, and the fused path (peer-memory dispatch,
+combine inside the GEMM epilogue).
 
 Each rank quantises its own tokens (sorted by expert, seeded per rank) and
 holds the full weights only to build the check: the expert-parallel result
@@ -21,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, E, port, q):
+def _worker(rank, world, E, impl, align, port, q):
     import datetime
     import torch.distributed as dist
     try:
@@ -43,7 +45,7 @@ def _worker(rank, world, E, port, q):
         W = torch.randn(E, N, K, generator=gw).to(torch.bfloat16).to(dev)
         w_s, w_q = utils.to_mx(W)
         g = torch.Generator().manual_seed(11 + rank)
-        counts = [int(c) * 32 for c in torch.randint(0, 9, (E,), generator=g)]
+        counts = [int(c) * align for c in torch.randint(0, 9, (E,), generator=g)]
         if rank == 1:
             counts[-1] = 0
         rows = sum(counts)
@@ -51,13 +53,27 @@ def _worker(rank, world, E, port, q):
         a_s, a_q = utils.to_mx(A)
         offs = torch.tensor(counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(dev)
         ref = kernels.triton_mxfp8_grouped_mm(a_q, w_q, a_s, w_s, offs, out_dtype=torch.float32)
-        plan = plan_dispatch(pl, counts, dev)
         mine = pl.experts_of(rank)
-        got = ep_grouped_mm(plan, a_q, a_s, w_q[mine].contiguous(), w_s[mine].contiguous(),
-                            out_dtype=torch.float32)
+        if impl == "nccl":
+            plan = plan_dispatch(pl, counts, dev)
+            got = ep_grouped_mm(plan, a_q, a_s, w_q[mine].contiguous(), w_s[mine].contiguous(),
+                                out_dtype=torch.float32)
+        else:
+            from mxgg.ep import FusedExpertParallel
+            cap = 8 * 32 * E                                  # most rows any rank can hold
+            fused = FusedExpertParallel(pl, max_recv_rows=world * cap, max_local_rows=cap, max_k=K, max_n=N)
+            plan = fused.plan(counts)
+            # twice: the second call reuses the buffers behind the first's barriers
+            got = None
+            for _ in range(2):
+                got = fused.grouped_mm(plan, a_q, a_s, w_q[mine].contiguous(), w_s[mine].contiguous(),
+                                       out_dtype=torch.float32).clone()
+            torch.cuda.synchronize()
         torch.cuda.synchronize()
         ok = got.shape == ref.shape and torch.equal(got, ref)
         st = mxgg.device_status(clear=True)
+        if impl != "nccl":
+            fused.close()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok" if ok and st == 0 else f"mismatch (status {st}): "
@@ -68,14 +84,17 @@ def _worker(rank, world, E, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("impl,align", [("nccl", 32), ("fused", 32), ("fused", 16)])
 @pytest.mark.parametrize("E", [4, 1])
-def test_ep_grouped_mm_two_ranks(E):
+def test_ep_grouped_mm_two_ranks(E, impl, align):
+    """align 32: peers' output blocks travel through inboxes; align 16: some
+    segments start off the 32-row grid and rows are stored in place."""
     import torch.multiprocessing as mp
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, E, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, E, impl, align, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
