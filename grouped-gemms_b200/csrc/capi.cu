@@ -259,7 +259,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
              void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
              const int32_t* group_expert = nullptr, int64_t n_experts = -1,
-             const char* what = nullptr, const EpRoute* route = nullptr) {
+             const char* what = nullptr, const EpRoute* route = nullptr, int b_format = MXGG_FMT_E4M3) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (n_experts < 0) n_experts = E;
@@ -270,6 +270,12 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                 (long long)K, (long long)E);
   if (E > kMaxGroups) return fail(MXGG_ERR_UNSUPPORTED, "%s: E=%lld exceeds %d groups", what, (long long)E, kMaxGroups);
   if (n_experts < 1) return fail(MXGG_ERR_INVALID, "%s: n_experts=%lld", what, (long long)n_experts);
+  if (b_format != MXGG_FMT_E4M3 && b_format != MXGG_FMT_E2M1)
+    return fail(MXGG_ERR_INVALID, "%s: unknown B format %d", what, b_format);
+  const bool b_fp4 = b_format == MXGG_FMT_E2M1;
+  if (b_fp4 && (mode != kFwd || K % 128 != 0 || !aligned(b, 32)))
+    return fail(MXGG_ERR_UNSUPPORTED, "%s: e2m1 weights need the forward pass, K %% 128 == 0 and a 32-byte "
+                "aligned B", what);
   // contraction length: fwd K, wgrad tokens M
   const int64_t C = mode == kFwd ? K : M;
   const int64_t rows_a = mode == kFwd ? M : N;
@@ -375,6 +381,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.offs = offs;
   p.group_expert = mode == kFwd ? group_expert : nullptr;
   p.n_experts = (int)n_experts;
+  p.b_fmt = b_fp4 ? 5 : 0;
   p.stages = (int)ws.stages;
   p.out = out;
   p.out_ld = out_cols;
@@ -413,8 +420,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (int rc = make_tmap_2d(&maps.a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
                             kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C, (uint64_t)C,
-                            kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
+  // e2m1 weights: packed two per byte in HBM; TMA's 16U4_ALIGN16B type
+  // spreads every 16 values (8 bytes) over a 16-byte slot, the 8-bit
+  // container layout kind::mxf8f6f4 reads, so the smem tile and its
+  // descriptors are the same as for e4m3.
+  if (int rc = b_fp4 ? make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 1, (uint64_t)rows_b,
+                                    (uint64_t)C, (uint64_t)(C / 2), kBK, (uint32_t)(bn / pair),
+                                    CU_TENSOR_MAP_SWIZZLE_128B)
+                     : make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C,
+                                    (uint64_t)C, kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   if (int rc = make_tmap_2d(&maps.sfa, ws_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
                             (uint64_t)(ws.a_subtiles * ws.stages * 4), 128, 128, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -496,11 +510,12 @@ int64_t mxgg_grouped_mm_segments_workspace_size(int64_t M, int64_t N, int64_t K,
 
 int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, const void* b_scale,
                              const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
-                             int64_t K, int64_t n_segments, int64_t n_experts, void* out, int out_dtype,
-                             void* workspace, int64_t workspace_bytes, void* stream) {
+                             int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out,
+                             int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!segment_expert && n_segments > 0) return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_segments: null segment_expert");
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
-                  workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments");
+                  workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments", nullptr,
+                  b_format);
 }
 
 int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
@@ -541,6 +556,45 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
                int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
                   workspace_bytes, stream);
+}
+
+int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
+                         int scale_layout, void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (rows < 0 || cols < 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: negative size");
+  if (rows == 0 || cols == 0) return MXGG_OK;
+  if (!x || !q || !scales) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: null pointer");
+  if (x_dtype != MXGG_DTYPE_BF16 && x_dtype != MXGG_DTYPE_F16 && x_dtype != MXGG_DTYPE_F32)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: unknown x_dtype %d", x_dtype);
+  if (scale_layout != MXGG_SCALE_ROW_MAJOR && scale_layout != MXGG_SCALE_BLOCKED)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: unknown scale layout %d", scale_layout);
+  if (cols % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: cols=%lld not a multiple of 32", (long long)cols);
+  if (!aligned(x, 16) || !aligned(q, 4))
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_fp4: x must be 16-byte and q 4-byte aligned");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const int nthreads = 256;
+  const long long work = rows * cols / 8;
+  const long long blocks =
+      std::max(1LL, std::min<long long>((work + nthreads - 1) / nthreads, (long long)st->num_sms * 8));
+  uint8_t* qq = static_cast<uint8_t*>(q);
+  uint8_t* ss = static_cast<uint8_t*>(scales);
+  switch (x_dtype) {
+    case MXGG_DTYPE_BF16:
+      quantize_rows_e4m3<__nv_bfloat16, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), rows, cols, qq, ss, scale_layout);
+      break;
+    case MXGG_DTYPE_F16:
+      quantize_rows_e4m3<__half, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const __half*>(x), rows, cols, qq, ss, scale_layout);
+      break;
+    default:
+      quantize_rows_e4m3<float, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const float*>(x), rows, cols, qq, ss, scale_layout);
+  }
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
 }
 
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales, int mode,
@@ -609,9 +663,9 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
 int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const void* b_scale,
                        const int32_t* segment_end_offsets, const int32_t* segment_expert, const int32_t* segment_dst,
                        const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
-                       int64_t n_experts, void* const* dst_out, const int64_t* dst_rows, void* const* dst_inbox,
-                       int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace, int64_t workspace_bytes,
-                       void* stream) {
+                       int64_t n_experts, int32_t b_format, void* const* dst_out, const int64_t* dst_rows,
+                       void* const* dst_inbox, int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
   if (!segment_expert || !dst_out || !dst_rows)
     return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: null segment or destination table");
   if (n_dst < 1 || n_dst > kMaxDst)
@@ -627,7 +681,8 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
     r.inbox_dst[i] = dst_inbox ? dst_inbox[i] : nullptr;
   }
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, nullptr, out_dtype,
-                  workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r);
+                  workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r,
+                  b_format);
 }
 
 int mxgg_ipc_alloc(int64_t bytes, void** ptr, void* handle) {

@@ -67,6 +67,7 @@ struct GemmParams {
   const int32_t* offs;       // (E,) cumulative group ends
   const int32_t* group_expert;  // fwd: expert (B slice) of each group, or null for group g -> expert g
   int n_experts;             // fwd: experts in B (E when group_expert is null)
+  int b_fmt;                 // B element type in the MMA's encoding: 0 e4m3, 5 e2m1 (TMA-unpacked to 8-bit slots)
   void* out;
   long long out_ld;          // elements per output row
   long long out_rows;        // rows of the output tensor
@@ -411,7 +412,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // epilogue chunk drained first for each buffer (the shared columns)
   constexpr int kOvChunks = kOv / kEpiCols;
   // bytes the leader's full barrier receives per stage (both CTAs' tiles and scale atoms)
-  constexpr uint32_t kStageBytes = PAIR * ((kBM + kBRows) * kBK + kBM * 4 + BN * 4);
+  // bytes one stage's loads deliver (the transaction count): e2m1 B tiles
+  // count their packed global bytes, half of the 8-bit-slot smem they fill
+  const uint32_t kStageBytes =
+      PAIR * (kBM * kBK + (p.b_fmt == 5 ? kBRows * kBK / 2 : kBRows * kBK) + kBM * 4 + BN * 4);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   S* sm = reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -540,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0 && leader) {
-      constexpr uint32_t kIdesc = ptx::idesc_mxf8(kTileM, BN, 0, 0);
+      const uint32_t kIdesc = ptx::idesc_mxf8(kTileM, BN, 0, (uint32_t)p.b_fmt);
       constexpr uint32_t kAStep = (kBM * kBK) >> 4;     // descriptor start-address step per stage
       constexpr uint32_t kBStep = (kBRows * kBK) >> 4;
       const uint64_t adesc0 = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->a[0]));

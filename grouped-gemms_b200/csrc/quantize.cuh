@@ -26,6 +26,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include <cstdint>
@@ -113,6 +114,21 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&f)[8], float mult, uint32_
   return make_uint2(lo, hi);
 }
 
+// Eight inputs of one 32-block -> eight e2m1 nibbles (one word, element 2k in
+// the low nibble of byte k, the layout the tensor cores and TMA's 4-bit types
+// read).  MXFP4 has no counterpart in the reference: FLOOR scaling is extended
+// with emax = 2, values saturate to +-6 and NaN becomes +6 (the hardware
+// conversion's rule; e2m1 has no NaN).
+__device__ __forceinline__ uint32_t e2m1x8(const float (&f)[8], float mult) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    w |= (uint32_t)__nv_cvt_float2_to_fp4x2(make_float2(f[2 * k] * mult, f[2 * k + 1] * mult), __NV_E2M1,
+                                            cudaRoundNearest)
+         << (8 * k);
+  return w;
+}
+
 // offset of scale (r, c) of a (R, C) scale matrix in the blocked atom layout
 __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c, long long C) {
   const long long cb = (C + 3) / 4;
@@ -124,7 +140,8 @@ __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c,
 // x: (R, C) contiguous, C % 32 == 0.  q: (R, C) e4m3.  s: scales.
 // Each thread handles kUnroll 8-element slots a grid-stride apart and issues
 // all their loads before converting, so kUnroll 16-byte loads are in flight.
-template <typename T>
+// kFp4: e2m1 output, packed two per byte (q holds R x C/2 bytes).
+template <typename T, bool kFp4 = false>
 __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ x, long long R, long long C,
                                                           uint8_t* __restrict__ q, uint8_t* __restrict__ s,
                                                           int scale_layout) {
@@ -162,9 +179,12 @@ __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ 
     for (int u = 0; u < kUnroll; ++u) {
       const long long i = base + u * stride;
       if (i >= total8) continue;
-      const uint32_t sc = floor_scale(m[u], 8);
+      const uint32_t sc = floor_scale(m[u], kFp4 ? 2 : 8);
       const float mult = __uint_as_float((254u - sc) << 23);    // 2^(127 - s)
-      *reinterpret_cast<uint2*>(q + i * 8) = e4m3x8(f[u], mult, m[u]);
+      if constexpr (kFp4)
+        *reinterpret_cast<uint32_t*>(q + i * 4) = e2m1x8(f[u], mult);
+      else
+        *reinterpret_cast<uint2*>(q + i * 8) = e4m3x8(f[u], mult, m[u]);
       if ((lane & 3) == 0) {
         const long long blk = i / 4;
         if (scale_layout == kScaleRowMajor) {

@@ -50,10 +50,20 @@ def triton_mxfp8_grouped_mm(
 
     Returns ``(M, N)`` of ``out_dtype``; rows at or past ``group_end_offsets[-1]``
     are left unwritten, like the reference (forward.py:583).
+
+    ``weight`` may also be MXFP4: ``(E, N, K//2)`` ``float4_e2m1fn_x2`` (two
+    e2m1 values per byte, from ``utils.to_mx(w, elem_dtype=torch.float4_e2m1fn_x2)``)
+    with the same ``(E, N, K//32)`` scales; the product runs on the same
+    block-scaled tensor-core path.  The reference has no MXFP4 path.
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
     M, K = input_act.shape
     E, N, K2 = weight.shape
+    if weight.dtype == torch.float4_e2m1fn_x2:
+        assert K == 2 * K2, f"K mismatch: A={K}, B={2 * K2} (e2m1 packed)"
+        experts = torch.arange(E, dtype=torch.int32, device=weight.device)
+        return mxgg.grouped_mm_segments_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets,
+                                           experts, out_dtype)
     assert K == K2, f"K mismatch: A={K}, B={K2}"
     return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)

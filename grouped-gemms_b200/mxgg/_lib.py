@@ -16,6 +16,7 @@ DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 QUANT_ROWS, QUANT_COLS = 0, 1
 SCALE_ROW_MAJOR, SCALE_BLOCKED = 0, 1
 SCHED_DEFAULT, SCHED_TILES, SCHED_SPLIT_TAIL = 0, 1, 2
+FMT_E4M3, FMT_E2M1 = 0, 1
 
 # every symbol include/mxgg.h declares, with (restype, argtypes)
 _vp = ctypes.c_void_p
@@ -28,9 +29,9 @@ SIGNATURES = {
     "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
     "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
     "mxgg_grouped_mm_segments_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
-    "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _int, _vp,
-                                        _i64, _vp]),
-    "mxgg_grouped_mm_ep": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+    "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int,
+                                        _vp, _i64, _vp]),
+    "mxgg_grouped_mm_ep": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                   ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_vp), _i32, _i32, _int,
                                   _vp, _i64, _vp]),
     "mxgg_inbox_unpack": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
@@ -42,6 +43,7 @@ SIGNATURES = {
     "mxgg_peer_barrier": (_int, [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp]),
     "mxgg_grouped_mm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
+    "mxgg_quantize_mx_fp4": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
     "mxgg_set_tile_config": (_int, [_i32, _i32, _i32]),
     "mxgg_set_schedule": (_int, [_i32, _i32]),

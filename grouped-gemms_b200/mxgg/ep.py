@@ -378,6 +378,8 @@ class FusedExpertParallel:
         lib = _lib.load()
         K = a_q.shape[1]
         L, N, Kw = w_q.shape
+        if w_q.dtype == torch.float4_e2m1fn_x2:
+            Kw *= 2
         if Kw != K:
             raise AssertionError(f"K mismatch: activations {K}, weights {Kw}")
         if N > self.max_n:
@@ -391,7 +393,7 @@ class FusedExpertParallel:
         and the closing barrier."""
         import ctypes
         from . import _lib
-        from .ops import _OUT_DTYPES, _workspace, as_u8
+        from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
         lib = _lib.load()
         L, N, _ = w_q.shape
         R = plan.rows_recv
@@ -406,7 +408,8 @@ class FusedExpertParallel:
         w_s = as_u8(w_s).contiguous()
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         _lib.check(lib.mxgg_grouped_mm_ep(p(recv_q), p(w_q), p(recv_s), p(w_s), p(plan.seg_offs), p(plan.seg_expert),
-                                          p(plan.seg_dst), p(plan.seg_dst_row), R, N, K, S, L, outs, rows, inboxes,
+                                          p(plan.seg_dst), p(plan.seg_dst_row), R, N, K, S, L, b_format_of(w_q),
+                                          outs, rows, inboxes,
                                           self.world, self.rank, _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_grouped_mm_ep")

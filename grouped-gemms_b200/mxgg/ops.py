@@ -42,6 +42,11 @@ def _workspace(nbytes: int, device: torch.device) -> Tensor:
     return buf[off:off + nbytes]
 
 
+def b_format_of(b: Tensor) -> int:
+    """MXGG_FMT_E2M1 for packed MXFP4 weights (float4_e2m1fn_x2), else e4m3."""
+    return _lib.FMT_E2M1 if b.dtype == torch.float4_e2m1fn_x2 else _lib.FMT_E4M3
+
+
 def as_u8(t: Tensor) -> Tensor:
     """Scales may be uint8 or float8_e8m0fnu (reference forward.py:534-535)."""
     return t if t.dtype == torch.uint8 else t.view(torch.uint8)
@@ -88,6 +93,36 @@ def _(x, mode, scale_layout):
     return s, q
 
 
+@torch.library.custom_op("mxgg::to_mx_fp4", mutates_args=())
+def to_mx_fp4_op(x: Tensor, scale_layout: int) -> Tuple[Tensor, Tensor]:
+    """MXFP4 along the last dim: (scales (R, C/32) u8, q (R, C/2) float4_e2m1fn_x2)."""
+    _require_cuda(x, what="mxgg::to_mx_fp4")
+    if x.dtype not in _IN_DTYPES:
+        raise TypeError(f"mxgg::to_mx_fp4: unsupported input dtype {x.dtype}")
+    x = x.contiguous()
+    R, C = x.shape
+    with torch.cuda.device(x.device):
+        q = torch.empty((R, C // 2), dtype=torch.uint8, device=x.device)
+        if scale_layout == _lib.SCALE_BLOCKED:
+            s = torch.zeros(((R + 127) // 128 * 128) * ((C // 32 + 3) // 4 * 4), dtype=torch.uint8, device=x.device)
+        else:
+            s = torch.empty((R, C // 32), dtype=torch.uint8, device=x.device)
+        _lib.check(_lib.load().mxgg_quantize_mx_fp4(_ptr(x), _IN_DTYPES[x.dtype], R, C, _ptr(q), _ptr(s),
+                                                    scale_layout, _stream(x.device)), "mxgg_quantize_mx_fp4")
+    return s, q.view(torch.float4_e2m1fn_x2)
+
+
+@to_mx_fp4_op.register_fake
+def _(x, scale_layout):
+    R, C = x.shape
+    q = x.new_empty((R, C // 2), dtype=torch.float4_e2m1fn_x2)
+    if scale_layout == _lib.SCALE_BLOCKED:
+        s = x.new_empty(((R + 127) // 128 * 128) * ((C // 32 + 3) // 4 * 4), dtype=torch.uint8)
+    else:
+        s = x.new_empty((R, C // 32), dtype=torch.uint8)
+    return s, q
+
+
 # ---------------------------------------------------------------- grouped_mm
 @torch.library.custom_op("mxgg::grouped_mm", mutates_args=())
 def grouped_mm_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
@@ -128,6 +163,7 @@ def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tenso
         raise TypeError(f"mxgg::grouped_mm_segments: unsupported out_dtype {out_dtype}")
     M, K = a.shape
     E, N, _ = b.shape
+    b_format = b_format_of(b)
     S = seg_offs.shape[0]
     a = a.contiguous()
     b = b.contiguous()
@@ -140,8 +176,8 @@ def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tenso
     ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), a.device)
     with torch.cuda.device(a.device):
         _lib.check(lib.mxgg_grouped_mm_segments(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
-                                                _ptr(seg_expert), M, N, K, S, E, _ptr(out), _OUT_DTYPES[out_dtype],
-                                                _ptr(ws), ws.numel(), _stream(a.device)),
+                                                _ptr(seg_expert), M, N, K, S, E, b_format, _ptr(out),
+                                                _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(), _stream(a.device)),
                    "mxgg_grouped_mm_segments")
     return out
 

@@ -19,7 +19,7 @@ from mxgg import _lib
 
 
 def _check_to_mx_args(data: torch.Tensor, elem_dtype, block_size: int) -> None:
-    assert elem_dtype is torch.float8_e4m3fn, "only e4m3fn supported here"
+    assert elem_dtype in (torch.float8_e4m3fn, torch.float4_e2m1fn_x2), "only e4m3fn (and e2m1 weights) supported here"
     assert data.shape[-1] % block_size == 0, (
         f"last dim {data.shape[-1]} must be divisible by block_size {block_size}"
     )
@@ -37,9 +37,16 @@ def to_mx(data: torch.Tensor, elem_dtype=torch.float8_e4m3fn, block_size: int = 
     _check_to_mx_args(data, elem_dtype, block_size)
     orig_shape = data.shape
     x2 = data.reshape(-1, orig_shape[-1])
-    s, q = mxgg.to_mx_op(x2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
     scale_shape = list(orig_shape)
     scale_shape[-1] = orig_shape[-1] // block_size
+    if elem_dtype is torch.float4_e2m1fn_x2:
+        # MXFP4 (no reference counterpart): FLOOR scaling with emax 2, two
+        # e2m1 values per byte, element 2i in the low nibble
+        s, q = mxgg.to_mx_fp4_op(x2, _lib.SCALE_ROW_MAJOR)
+        q_shape = list(orig_shape)
+        q_shape[-1] = orig_shape[-1] // 2
+        return s.reshape(scale_shape), q.reshape(q_shape)
+    s, q = mxgg.to_mx_op(x2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
     return s.reshape(scale_shape), q.reshape(orig_shape)
 
 

@@ -45,6 +45,10 @@ extern "C" {
 #define MXGG_SCALE_ROW_MAJOR 0 /* (rows, cols/32), the reference layout */
 #define MXGG_SCALE_BLOCKED 1   /* 128x4 atoms (rows padded to 128, cols/32 to 4) */
 
+/* element formats of a GEMM operand */
+#define MXGG_FMT_E4M3 0 /* MXFP8: one e4m3 byte per element */
+#define MXGG_FMT_E2M1 1 /* MXFP4: two e2m1 values per byte, element 2i in the low nibble */
+
 /*
  * Scratch ("workspace") for one grouped-GEMM call: the row-major scales are
  * re-laid into the 128x4 atoms the tensor cores read, one atom per 128-row
@@ -105,6 +109,12 @@ int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, c
  *   b        (n_experts, N, K) e4m3,   b_scale (n_experts, N, K/32)
  *   segment_end_offsets (n_segments,) int32, device, cumulative
  *   segment_expert      (n_segments,) int32, device, in [0, n_experts)
+ *   b_format  MXGG_FMT_E4M3, or MXGG_FMT_E2M1 for MXFP4 weights: b holds
+ *             (n_experts, N, K/2) bytes, two e2m1 values per byte (element
+ *             2i in the low nibble), 32-byte aligned, K % 128 == 0; the
+ *             scales are still one e8m0 per 32 elements.  MXFP4 x MXFP8 runs
+ *             on the same kind::mxf8f6f4 tensor-core path (no reference
+ *             counterpart: its kernels are MXFP8 only).
  * Other arguments as mxgg_grouped_mm; the workspace is at least
  * mxgg_grouped_mm_segments_workspace_size(M, N, K, n_segments, n_experts).
  */
@@ -112,8 +122,8 @@ int64_t mxgg_grouped_mm_segments_workspace_size(int64_t M, int64_t N, int64_t K,
                                                 int64_t n_experts);
 int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, const void* b_scale,
                              const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
-                             int64_t K, int64_t n_segments, int64_t n_experts, void* out, int out_dtype,
-                             void* workspace, int64_t workspace_bytes, void* stream);
+                             int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out,
+                             int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Expert-parallel forward with the combine fused into the epilogue: as
@@ -138,9 +148,9 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
 int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const void* b_scale,
                        const int32_t* segment_end_offsets, const int32_t* segment_expert, const int32_t* segment_dst,
                        const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
-                       int64_t n_experts, void* const* dst_out, const int64_t* dst_rows, void* const* dst_inbox,
-                       int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace, int64_t workspace_bytes,
-                       void* stream);
+                       int64_t n_experts, int32_t b_format, void* const* dst_out, const int64_t* dst_rows,
+                       void* const* dst_inbox, int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace,
+                       int64_t workspace_bytes, void* stream);
 
 /* Copies the listed 32-row blocks (device int32 row-block indices) of an
  * inbox filled by peers' mxgg_grouped_mm_ep into the row-major output whose
@@ -196,6 +206,13 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
  *   scale_layout MXGG_SCALE_ROW_MAJOR or MXGG_SCALE_BLOCKED (the caller
  *              zero-fills the padding of a blocked buffer).
  */
+/* MXFP4 quantiser (rows mode): FLOOR scaling with emax 2, e2m1 elements
+ * packed two per byte (element 2i in the low nibble) into q (rows, cols/2),
+ * scales (rows, cols/32) e8m0.  Values saturate to +-6; NaN becomes +6 (e2m1
+ * has no NaN).  No counterpart in the reference (its to_mx is e4m3 only). */
+int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
+                         int scale_layout, void* stream);
+
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
                      int mode, int scale_layout, void* stream);
 

@@ -127,8 +127,13 @@ _E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float
 
 
 def e2m1_encode(v: np.ndarray) -> np.ndarray:
-    """float32 (already clamped to [-6, 6]) -> e2m1 nibbles, RNE on the grid."""
+    """float32 (already clamped to [-6, 6]) -> e2m1 nibbles, RNE on the grid.
+
+    e2m1 has no NaN: NaN becomes +6 (code 0b0111), the rule of the hardware
+    conversion the GPU quantiser uses.  (MXFP4 has no reference
+    implementation; this defines it.)"""
     v = np.asarray(v, dtype=np.float32)
+    nan = np.isnan(v)
     sign = (v.view(np.uint32) >> 31).astype(np.uint8)
     a = np.abs(v.astype(np.float64))
     # grid points 0,.5,1,1.5,2,3,4,6 ; ties go to the even mantissa code
@@ -142,7 +147,23 @@ def e2m1_encode(v: np.ndarray) -> np.ndarray:
         else:
             up = a >= mid
         codes = np.where(up, c, codes).astype(np.uint8)
-    return codes | (sign << 3)
+    out = codes | (sign << 3)
+    return np.where(nan, np.uint8(7), out).astype(np.uint8)
+
+
+def pack_e2m1(nibbles: np.ndarray) -> np.ndarray:
+    """(..., 2n) nibbles -> (..., n) bytes, element 2i in the low nibble."""
+    n = np.asarray(nibbles, dtype=np.uint8)
+    return (n[..., 0::2] & 0xF) | ((n[..., 1::2] & 0xF) << 4)
+
+
+def unpack_e2m1(packed: np.ndarray) -> np.ndarray:
+    """(..., n) bytes -> (..., 2n) nibbles (inverse of pack_e2m1)."""
+    p = np.asarray(packed, dtype=np.uint8)
+    out = np.empty(p.shape[:-1] + (2 * p.shape[-1],), dtype=np.uint8)
+    out[..., 0::2] = p & 0xF
+    out[..., 1::2] = p >> 4
+    return out
 
 
 def e2m1_decode(n: np.ndarray) -> np.ndarray:

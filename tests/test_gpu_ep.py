@@ -43,7 +43,8 @@ def _worker(rank, world, E, impl, align, port, q):
         pl = ExpertPlacement(world, E)
         gw = torch.Generator().manual_seed(7)
         W = torch.randn(E, N, K, generator=gw).to(torch.bfloat16).to(dev)
-        w_s, w_q = utils.to_mx(W)
+        fp4 = impl.endswith("fp4")
+        w_s, w_q = utils.to_mx(W, elem_dtype=torch.float4_e2m1fn_x2 if fp4 else torch.float8_e4m3fn)
         g = torch.Generator().manual_seed(11 + rank)
         counts = [int(c) * align for c in torch.randint(0, 9, (E,), generator=g)]
         if rank == 1:
@@ -54,9 +55,11 @@ def _worker(rank, world, E, impl, align, port, q):
         offs = torch.tensor(counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(dev)
         ref = kernels.triton_mxfp8_grouped_mm(a_q, w_q, a_s, w_s, offs, out_dtype=torch.float32)
         mine = pl.experts_of(rank)
-        if impl == "nccl":
+        wq_mine = w_q.view(torch.uint8)[mine].contiguous().view(w_q.dtype)   # (no index kernels for 4-bit dtypes)
+        ws_mine = w_s[mine].contiguous()
+        if impl.startswith("nccl"):
             plan = plan_dispatch(pl, counts, dev)
-            got = ep_grouped_mm(plan, a_q, a_s, w_q[mine].contiguous(), w_s[mine].contiguous(),
+            got = ep_grouped_mm(plan, a_q, a_s, wq_mine, ws_mine,
                                 out_dtype=torch.float32)
         else:
             from mxgg.ep import FusedExpertParallel
@@ -66,13 +69,13 @@ def _worker(rank, world, E, impl, align, port, q):
             # twice: the second call reuses the buffers behind the first's barriers
             got = None
             for _ in range(2):
-                got = fused.grouped_mm(plan, a_q, a_s, w_q[mine].contiguous(), w_s[mine].contiguous(),
+                got = fused.grouped_mm(plan, a_q, a_s, wq_mine, ws_mine,
                                        out_dtype=torch.float32).clone()
             torch.cuda.synchronize()
         torch.cuda.synchronize()
         ok = got.shape == ref.shape and torch.equal(got, ref)
         st = mxgg.device_status(clear=True)
-        if impl != "nccl":
+        if not impl.startswith("nccl"):
             fused.close()
         dist.barrier()
         dist.destroy_process_group()
@@ -84,7 +87,7 @@ def _worker(rank, world, E, impl, align, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("impl,align", [("nccl", 32), ("fused", 32), ("fused", 16)])
+@pytest.mark.parametrize("impl,align", [("nccl", 32), ("fused", 32), ("fused", 16), ("fused-fp4", 32)])
 @pytest.mark.parametrize("E", [4, 1])
 def test_ep_grouped_mm_two_ranks(E, impl, align):
     """align 32: peers' output blocks travel through inboxes; align 16: some
