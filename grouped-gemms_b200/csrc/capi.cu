@@ -558,6 +558,41 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
                   workspace_bytes, stream);
 }
 
+int mxgg_quantize_mx_gather(const void* x, int x_dtype, int64_t in_rows, const int32_t* row_index, int64_t n_rows,
+                            int64_t cols, void* q, void* scales, void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (in_rows < 0 || n_rows < 0 || cols < 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_gather: negative size");
+  if (n_rows == 0 || cols == 0) return MXGG_OK;
+  if (!x || !row_index || !q || !scales) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_gather: null pointer");
+  if (x_dtype != MXGG_DTYPE_BF16 && x_dtype != MXGG_DTYPE_F16 && x_dtype != MXGG_DTYPE_F32)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_gather: unknown x_dtype %d", x_dtype);
+  if (cols % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_gather: cols=%lld not a multiple of 32", (long long)cols);
+  if (!aligned(x, 16) || !aligned(q, 8))
+    return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx_gather: x must be 16-byte and q 8-byte aligned");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long work = n_rows * cols / 8;
+  const long long blocks = std::max(1LL, std::min<long long>((work + 255) / 256, (long long)st->num_sms * 16));
+  uint8_t* qq = static_cast<uint8_t*>(q);
+  uint8_t* ss = static_cast<uint8_t*>(scales);
+  switch (x_dtype) {
+    case MXGG_DTYPE_BF16:
+      quantize_rows_gather_e4m3<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), in_rows, row_index, n_rows, cols, qq, ss);
+      break;
+    case MXGG_DTYPE_F16:
+      quantize_rows_gather_e4m3<__half><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const __half*>(x),
+                                                                              in_rows, row_index, n_rows, cols, qq, ss);
+      break;
+    default:
+      quantize_rows_gather_e4m3<float><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const float*>(x), in_rows,
+                                                                             row_index, n_rows, cols, qq, ss);
+  }
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
 int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
                          int scale_layout, void* stream_v) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);

@@ -198,6 +198,54 @@ __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ 
   }
 }
 
+// ------------------------------------------------------ gathered row mode
+// Quantise-on-dispatch: output row i is input row row_index[i] (or zeros
+// when row_index[i] is negative -- the padding of a routed group -- or out of
+// range), so routing's gather
+// and to_mx are one HBM pass.  x (R_in, C) contiguous, C % 32 == 0;
+// q (n_rows, C) e4m3; s (n_rows, C/32) row-major.  One thread per 8
+// elements, four lanes per 32-block, as quantize_rows_e4m3.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_gather_e4m3(const T* __restrict__ x,
+                                                                 long long in_rows,
+                                                                 const int32_t* __restrict__ row_index,
+                                                                 long long n_rows, long long C,
+                                                                 uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
+  const long long per_row = C / 8;
+  const long long total8 = n_rows * per_row;
+  const long long total8_w = (total8 + 31) / 32 * 32;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total8_w; i += stride) {
+    float f[8];
+    bool live = false;
+    long long r = 0, c8 = 0;
+    if (i < total8) {
+      r = i / per_row;
+      c8 = i - r * per_row;
+      const int src = __ldg(row_index + r);
+      live = src >= 0 && src < in_rows;   // out-of-range indices read as padding
+      if (live) {
+        load8<T>(x + (long long)src * C + c8 * 8, f);
+      }
+    }
+    if (!live) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = 0.0f;
+    }
+    uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = max(m, abs_bits(f[k]));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (i >= total8) continue;
+    const uint32_t sc = floor_scale(m, 8);
+    const float mult = __uint_as_float((254u - sc) << 23);
+    *reinterpret_cast<uint2*>(q + i * 8) = e4m3x8(f, mult, m);
+    if ((lane & 3) == 0) s[i / 4] = (uint8_t)sc;
+  }
+}
+
 // -------------------------------------------------------------- col mode
 // x: (R, C) contiguous, R % 32 == 0.  Quantises along R and writes the
 // transposed result: qt (C, R) e4m3, scales (C, R/32).

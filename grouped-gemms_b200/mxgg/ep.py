@@ -387,18 +387,31 @@ class FusedExpertParallel:
         self.dispatch(plan, a_q, a_s)
         return self.compute(plan, K, w_q, w_s, out_dtype)
 
+    def received(self, plan: FusedPlan, K: int):
+        """The dispatched rows as (rows_recv, K) e4m3 and (rows_recv, K/32) scale views."""
+        R = plan.rows_recv
+        return (self.recv_a.view((R, K), torch.uint8).view(torch.float8_e4m3fn),
+                self.recv_s.view((R, K // 32), torch.uint8))
+
     def compute(self, plan: FusedPlan, K: int, w_q: Tensor, w_s: Tensor,
-                out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+                out_dtype: torch.dtype = torch.bfloat16, a: Optional[tuple] = None) -> Tensor:
         """The GEMM over rows already dispatched (`dispatch`), its peer stores
-        and the closing barrier."""
+        and the closing barrier.  `a` = (a_q, a_s) replaces the receive
+        buffers with local rows in the same segment layout (for example the
+        quantised output of an earlier GEMM over the received rows)."""
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
         lib = _lib.load()
         L, N, _ = w_q.shape
         R = plan.rows_recv
-        recv_q = self.recv_a.view((R, K), torch.uint8)
-        recv_s = self.recv_s.view((R, K // 32), torch.uint8)
+        if a is None:
+            recv_q = self.recv_a.view((R, K), torch.uint8)
+            recv_s = self.recv_s.view((R, K // 32), torch.uint8)
+        else:
+            recv_q, recv_s = a[0].contiguous(), as_u8(a[1]).contiguous()
+            if recv_q.shape != (R, K) or recv_s.shape != (R, K // 32):
+                raise ValueError(f"local rows {tuple(recv_q.shape)} do not match the plan's ({R}, {K})")
         S = plan.seg_offs.numel()
         ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(R, N, K, S, L), w_q.device)
         outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)

@@ -206,6 +206,14 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
  *   scale_layout MXGG_SCALE_ROW_MAJOR or MXGG_SCALE_BLOCKED (the caller
  *              zero-fills the padding of a blocked buffer).
  */
+/* Quantise-on-dispatch: MXFP8 rows mode of the gathered rows
+ * x[row_index[i]] (zeros where row_index[i] is negative -- padding -- or
+ * not below in_rows), so the routing gather and to_mx are one pass.  q (n_rows, cols) e4m3, scales (n_rows, cols/32) row-major.
+ * Bit-exact with to_mx of the gathered rows.  No counterpart in the
+ * reference. */
+int mxgg_quantize_mx_gather(const void* x, int x_dtype, int64_t in_rows, const int32_t* row_index, int64_t n_rows,
+                            int64_t cols, void* q, void* scales, void* stream);
+
 /* MXFP4 quantiser (rows mode): FLOOR scaling with emax 2, e2m1 elements
  * packed two per byte (element 2i in the low nibble) into q (rows, cols/2),
  * scales (rows, cols/32) e8m0.  Values saturate to +-6; NaN becomes +6 (e2m1
