@@ -128,6 +128,11 @@ def build_problems(device, shapes, passes, seed=123):
             b_s, b_q = utils.to_mx(W)
             probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K,
                               args=(a_q, b_q, a_s, b_s, offs)))
+        if "fwd4" in passes:
+            a_s, a_q = utils.to_mx(A)
+            w4_s, w4_q = utils.to_mx(W, elem_dtype=torch.float4_e2m1fn_x2)
+            probs.append(dict(pass_="fwd4", shape=(E, M, N, K), flops=2.0 * M * N * K,
+                              args=(a_q, w4_q, a_s, w4_s, offs)))
         if "dgrad" in passes:
             g_s, g_q = utils.to_mx(G)                                  # along N
             wt = [utils.to_mx_dim1(W[e]) for e in range(E)]            # W[e]^T (K, N), along N
@@ -219,6 +224,61 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123, impl="fused
     return probs
 
 
+MOE_TOKENS_PER_RANK = 16384
+MOE_EXPERTS_PER_RANK = 8
+MOE_D_MODEL, MOE_D_FF = 5120, 8192
+
+
+def bench_moe(device, world, rank, steps, warmup):
+    """BASELINE config 5, weak-scaled: 8 experts and 16384 tokens per rank
+    (E = 64 and 131072 tokens at 8 GPUs), top-2 routing from seeded N(0,1)
+    logits, up 5120 -> 8192 and down 8192 -> 5120, MXFP8 weights and MXFP4
+    weights x MXFP8 activations.  One step = one layer forward over this
+    rank's tokens (routing, quantise-on-dispatch, dispatch, both GEMMs,
+    combine); TFLOPS counts the useful 2 * 2T * d_model * d_ff * 2 FLOPs of
+    all ranks over the slowest rank's time."""
+    import torch
+    from mxgg import ep as ep_mod
+    from mxgg.moe import MoELayer
+    E = MOE_EXPERTS_PER_RANK * world
+    T = MOE_TOKENS_PER_RANK
+    g = torch.Generator(device=device).manual_seed(5 + rank)
+    x = torch.randn(T, MOE_D_MODEL, device=device, dtype=torch.bfloat16, generator=g)
+    logits = torch.randn(T, E, device=device, generator=g)
+    placement = ep_mod.ExpertPlacement(world, E) if world > 1 else None
+    fx = None
+    if world > 1:
+        cap = int(1.5 * 2 * T) + 32 * E
+        fx = ep_mod.FusedExpertParallel(placement, max_recv_rows=cap, max_local_rows=2 * T + 32 * E,
+                                        max_k=MOE_D_FF, max_n=MOE_D_FF)
+    out = {"config": {"experts": E, "experts_per_gpu": MOE_EXPERTS_PER_RANK, "tokens": T * world,
+                      "tokens_per_gpu": T, "top_k": 2, "d_model": MOE_D_MODEL, "d_ff": MOE_D_FF,
+                      "routing": "softmax of seeded N(0,1) logits, top-2, renormalised; groups padded to 32"}}
+    for name, fp4 in (("mxfp8", False), ("mxfp4_weights", True)):
+        gw = torch.Generator(device=device).manual_seed(1000 + rank)
+        up = torch.randn(MOE_EXPERTS_PER_RANK, MOE_D_FF, MOE_D_MODEL, device=device, dtype=torch.bfloat16,
+                         generator=gw) * MOE_D_MODEL ** -0.5
+        down = torch.randn(MOE_EXPERTS_PER_RANK, MOE_D_MODEL, MOE_D_FF, device=device, dtype=torch.bfloat16,
+                           generator=gw) * MOE_D_FF ** -0.5
+        layer = MoELayer(up, down, E, weights_fp4=fp4, placement=placement, ep=fx)
+        del up, down
+        for _ in range(warmup):
+            layer.forward(x, logits)
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            layer.forward(x, logits)
+        e.record()
+        barrier(world)
+        t = allreduce_max([s.elapsed_time(e) / steps * 1e-3], world)[0]
+        out[name] = {"tflops": round(world * layer.flops(T) / t / 1e12, 1), "ms_per_step": round(t * 1e3, 3)}
+        del layer
+    if fx is not None:
+        fx.close()
+    return out
+
+
 def run_ep_problem(p, marks=None):
     """One expert-parallel call; `marks` (3 events) split it into dispatch |
     local GEMM | combine."""
@@ -237,13 +297,21 @@ def run_ep_problem(p, marks=None):
             marks[2].record()
         return out
     if "fused" in p:
+        # dispatch | self-rows GEMM (overlapping the copies) | received-rows GEMM + barrier + inbox unpack
         fx, fplan = p["fused"]
-        fx.dispatch(fplan, *p["args"])
+        a_q, a_s = p["args"]
+        K = a_q.shape[1]
+        w_q, w_s = p["weights"]
+        fx.start_dispatch(fplan, a_q, a_s)
+        fx.gemm(fplan, "self", K, w_q, w_s, torch_bf16(), a=fx.self_rows(fplan, a_q, a_s))
+        fx.finish_dispatch()
         if marks:
             marks[0].record()
-        out = fx.compute(fplan, p["args"][0].shape[1], p["weights"][0], p["weights"][1], torch_bf16())
+        fx.gemm(fplan, "remote", K, w_q, w_s, torch_bf16())
         if marks:
             marks[1].record()
+        out = fx.finish(fplan, w_q.shape[1], torch_bf16())
+        if marks:
             marks[2].record()
         return out
     recv_q, recv_s = ep.dispatch(plan, *p["args"])
@@ -662,12 +730,15 @@ def main():
         # rank 0's own GEMM work and phase split (max over ranks per phase)
         ph = allreduce_max([x for row in phases for x in row], world)
         phases = [ph[3 * i:3 * i + 3] for i in range(len(probs))]
-        local_flops = [2.0 * p["plan"].rows_recv * p["shape"][2] * p["shape"][3] for p in probs]
+        # rows each timed GEMM phase multiplies: the received rows (fused: peers' rows only)
+        local_flops = [2.0 * (p["fused"][1].rows_recv if "fused" in p else p["plan"].rows_recv)
+                       * p["shape"][2] * p["shape"][3] for p in probs]
         gemm_t = [x[1] for x in phases]
         ep_info = {"phases_us_per_step": {
-                       "dispatch": round(1e6 * sum(x[0] for p, x in zip(probs, phases) if p["pass_"] != "wgrad"), 1),
-                       "gemm": round(1e6 * sum(gemm_t), 1),
-                       "combine_or_replica_allreduce": round(1e6 * sum(x[2] for x in phases), 1)},
+                       "dispatch_with_self_gemm": round(1e6 * sum(x[0] for p, x in zip(probs, phases)
+                                                                  if p["pass_"] != "wgrad"), 1),
+                       "remote_gemm_or_wgrad": round(1e6 * sum(gemm_t), 1),
+                       "finish_or_replica_allreduce": round(1e6 * sum(x[2] for x in phases), 1)},
                    "rank0_gemm_tflops_geomean": round(geomean([f / t / 1e12 for f, t in zip(local_flops, gemm_t)]), 1),
                    "placement": "experts sharded when E >= world, replicated (world/E copies) when E < world"}
 
@@ -704,6 +775,19 @@ def main():
         cpu = {"value": round(ref.run(), 4), "unit": "TFLOPS", "cores": cpu_cores(), "kind": "port",
                "sample": ref.describe()}
     quant = quantize_bandwidth(dev, peaks.get("hbm_gbs", 6650.0)) if rank == 0 and not args.no_extras else None
+    n_main = len(probs)
+    moe = None if args.no_extras else bench_moe(dev, world, rank, max(2, min(args.steps, 5)), 2)
+    fp4 = None
+    if world == 1 and not args.no_extras:
+        # MXFP4 weights x MXFP8 activations, the same 36 forward shapes
+        n_main = len(probs)
+        del probs
+        probs = []
+        p4 = build_problems(dev, [shapes[i] for i in idx], ["fwd4"])
+        per4, _ = time_problems(p4, max(1, min(args.steps, 3)), 1, world, flush)
+        fp4 = {"fwd_geomean_tflops": round(geomean([p["flops"] / t / 1e12 for p, t in zip(p4, per4)]), 1),
+               "note": "e2m1 weights (two per byte, TMA-unpacked) x e4m3 activations on kind::mxf8f6f4"}
+        del p4
 
     if rank == 0:
         peak = ceiling["tflops"] if ceiling and ceiling["tflops"] else 2.0 * peaks.get("bf16_tflops", 1590.0)
@@ -720,10 +804,14 @@ def main():
                 "per_pass_geomean": by_pass, "pct_of_nominal_peak": round(100 * gm / NOMINAL_MXFP8_TFLOPS, 2),
                 "pct_of_measured_mxfp8": round(100 * gm / peak, 2),
                 "roofline": roof, "quantize_roofline": quant, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": 2 * len(probs) * args.steps, "clocks": clk.summary(),
+                "gpu_launches": 2 * n_main * args.steps, "clocks": clk.summary(),
                 "device_status": status, "wall_ms_per_step": round(wall_ms, 3)}
         if ep_info:
             line["expert_parallel"] = ep_info
+        if moe:
+            line["moe_layer"] = moe
+        if fp4:
+            line["mxfp4_weights"] = fp4
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier(world)

@@ -202,16 +202,29 @@ def replica_groups(placement: ExpertPlacement) -> dict:
 # Fused path: peer-memory dispatch, combine fused into the GEMM epilogue.
 # ----------------------------------------------------------------------------
 @dataclass
+class _Segments:
+    offs: Tensor                 # int32 cumulative ends of the segments (rows of the A operand)
+    expert: Tensor               # local expert of each segment
+    dst: Tensor                  # rank that owns each segment's rows
+    dst_row: Tensor              # first row of the segment in its owner's output
+
+
+@dataclass
 class FusedPlan:
-    """Routing of one fused expert-parallel call, as seen by one rank."""
+    """Routing of one fused expert-parallel call, as seen by one rank.
+
+    The rows a rank routes to its own experts never move: the "self" GEMM
+    reads them from the caller's tensor (rows [self_row, self_row +
+    self_rows)) while the other ranks' rows are in flight.  The receive
+    buffer holds only peers' rows, source-major, then local expert."""
 
     rows_local: int
-    rows_recv: int
-    copies: List[tuple]          # (dest rank, first row there, first local row, rows)
-    seg_offs: Tensor             # (world * L,) int32 cumulative ends of the received segments
-    seg_expert: Tensor           # (world * L,) local expert of each segment
-    seg_dst: Tensor              # (world * L,) rank that owns each segment's rows
-    seg_dst_row: Tensor          # (world * L,) first row of the segment in its owner's output
+    rows_recv: int               # rows received from peers
+    copies: List[tuple]          # (dest rank, first row there, first local row, rows), dest != this rank
+    self_row: int
+    self_rows: int
+    self_seg: _Segments          # L segments over the self rows
+    remote_seg: _Segments        # world * L segments over the receive buffer (own source: empty)
     dst_rows: List[int]          # local rows of every rank (the output buffers' heights)
     inbox_ok: bool               # every segment starts on a 32-row boundary: peers' blocks go by inbox
     remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
@@ -223,13 +236,15 @@ class FusedExpertParallel:
     Collective to construct (it allocates and maps the shared buffers).  Per
     call (`grouped_mm`):
 
-    1. each rank pushes its rows for rank d straight into d's receive buffer
-       (one copy-engine ``cudaMemcpyAsync`` per destination, destinations on
-       parallel streams), then a cross-GPU barrier;
-    2. ``mxgg_grouped_mm_ep`` multiplies the received segments and sends each
-       output block to the rank that owns its rows as the tile finishes (TMA
-       stores for its own rows; 2 KB bulk copies into the owner's inbox for
-       peers'), so the return trip overlaps the math tile by tile;
+    1. each rank starts pushing its rows for rank d straight into d's receive
+       buffer (one copy-engine ``cudaMemcpyAsync`` per peer, on parallel
+       streams) and, meanwhile, multiplies the rows it routed to its own
+       experts where they lie;
+    2. a cross-GPU barrier, then ``mxgg_grouped_mm_ep`` multiplies the
+       received segments and sends each output block to the rank that owns
+       its rows as the tile finishes (TMA stores for its own rows; 2 KB bulk
+       copies into the owner's inbox for peers'), so the return trip overlaps
+       the math tile by tile;
     3. a second barrier, then each rank unpacks its inbox into its output.
 
     The returned tensor is a view of this rank's shared output buffer: use it
@@ -257,6 +272,7 @@ class FusedExpertParallel:
         self.flags = PeerBuffer(256, group)
         self.epoch = 0
         self._streams = [torch.cuda.Stream() for _ in range(self.world)]
+        self._pending = []
         # every rank's capacities, so a plan that overflows any of them fails on all ranks alike
         caps = [None] * self.world
         dist.all_gather_object(caps, (self.max_recv_rows, self.max_local_rows), group=group)
@@ -281,49 +297,56 @@ class FusedExpertParallel:
         mine = torch.tensor([int(c) for c in expert_counts], dtype=torch.int64, device=dev)
         if mine.numel() != E or bool((mine < 0).any()):
             raise ValueError("expert_counts must hold E non-negative counts")
-        allc = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(allc, mine, group=self.group)
-        C = [t.tolist() for t in allc]                       # C[s][e]
+        allc = torch.empty(world, E, dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(allc, mine, group=self.group)
+        C = allc.tolist()                                     # C[s][e], one device sync
         # rows rank s sends to rank d, and where they start in s's local order
         send = [[0] * world for _ in range(world)]
-        start = [[None] * world for _ in range(world)]
+        start = [[0] * world for _ in range(world)]
+        seen = [[False] * world for _ in range(world)]
         for s in range(world):
             row = 0
             for e in range(E):
                 d = pl.dest(s, e)
-                if start[s][d] is None:
-                    start[s][d] = row
+                if not seen[s][d]:
+                    start[s][d], seen[s][d] = row, True
                 send[s][d] += C[s][e]
                 row += C[s][e]
-        # receive layout of rank d: source-major, then local expert
-        recv_off = [[sum(send[s2][d] for s2 in range(s)) for d in range(world)] for s in range(world)]
-        copies = [(d, recv_off[rank][d], start[rank][d] or 0, send[rank][d]) for d in range(world) if send[rank][d]]
-        offs, expert, dsts, dst_rows_first = [], [], [], []
-        total = 0
+        # receive layout of rank d: peers only, source-major, then local expert
+        recv_off = [[sum(send[s2][d] for s2 in range(s) if s2 != d) for d in range(world)] for s in range(world)]
+        copies = [(d, recv_off[rank][d], start[rank][d], send[rank][d])
+                  for d in range(world) if d != rank and send[rank][d]]
         mine_e = pl.experts_of(rank)
-        for s in range(world):
-            for le, e in enumerate(mine_e):
-                rows = C[s][e] if pl.dest(s, e) == rank else 0
-                total += rows
-                offs.append(total)
-                expert.append(le)
-                dsts.append(s)
-                dst_rows_first.append(sum(C[s][:e]))
-        rows_local = sum(C[rank])
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+
+        def segments(sources):
+            offs, expert, dsts, first = [], [], [], []
+            total = 0
+            for s in range(world):
+                for le, e in enumerate(mine_e):
+                    rows = C[s][e] if (s in sources and pl.dest(s, e) == rank) else 0
+                    total += rows
+                    offs.append(total)
+                    expert.append(le)
+                    dsts.append(s)
+                    first.append(sum(C[s][:e]))
+            return total, _Segments(i32(offs), i32(expert), i32(dsts), i32(first))
+
+        rows_recv, remote_seg = segments([s for s in range(world) if s != rank])
+        self_rows, self_seg = segments([rank])
         for d in range(world):
-            need_recv = sum(send[s][d] for s in range(world))
+            need_recv = sum(send[s][d] for s in range(world) if s != d)
             if need_recv > self._caps[d][0] or sum(C[d]) > self._caps[d][1]:
                 raise ValueError(f"fused EP buffers of rank {d} too small: {need_recv} received / {sum(C[d])} "
                                  f"local rows for {self._caps[d][0]} / {self._caps[d][1]}")
-        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
         inbox_ok = all(c % 32 == 0 for row in C for c in row)
         blocks, row = [], 0
         for e in range(E):
             if pl.dest(rank, e) != rank:
                 blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
             row += C[rank][e]
-        return FusedPlan(rows_local=rows_local, rows_recv=total, copies=copies, seg_offs=i32(offs),
-                         seg_expert=i32(expert), seg_dst=i32(dsts), seg_dst_row=i32(dst_rows_first),
+        return FusedPlan(rows_local=sum(C[rank]), rows_recv=rows_recv, copies=copies, self_row=start[rank][rank],
+                         self_rows=self_rows, self_seg=self_seg, remote_seg=remote_seg,
                          dst_rows=[sum(C[d]) for d in range(world)], inbox_ok=inbox_ok,
                          remote_blocks=i32(blocks if inbox_ok else []))
 
@@ -338,8 +361,9 @@ class FusedExpertParallel:
                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_peer_barrier")
 
-    def dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
-        """Push this rank's rows into the owners' receive buffers, then barrier."""
+    def start_dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
+        """Start pushing this rank's rows into their hosts' receive buffers
+        (copy engines, one stream per peer); `finish_dispatch` joins them."""
         import ctypes
         from . import _lib
         lib = _lib.load()
@@ -350,7 +374,7 @@ class FusedExpertParallel:
         a_s = a_s.contiguous()
         cur = torch.cuda.current_stream()
         ready = cur.record_event()
-        done = []
+        self._pending = []
         for (d, dst_row, src_row, rows) in plan.copies:
             st = self._streams[d]
             st.wait_event(ready)
@@ -361,58 +385,61 @@ class FusedExpertParallel:
             _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_s.ptrs[d] + dst_row * (K // 32)),
                                            ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)), rows * (K // 32),
                                            sp), "mxgg_copy_async")
-            done.append(st.record_event())
+            self._pending.append(st.record_event())
             # the caching allocator must not hand the sources out before the copies finish
             a_q.record_stream(st)
             a_s.record_stream(st)
-        for ev in done:
+
+    def finish_dispatch(self) -> None:
+        """The current stream waits for this rank's copies, then for every
+        rank's (cross-GPU barrier): the receive buffers are complete."""
+        cur = torch.cuda.current_stream()
+        for ev in self._pending:
             cur.wait_event(ev)
+        self._pending = []
         self.barrier()
 
-    def grouped_mm(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s: Tensor,
-                   out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
-        """Fused forward / dgrad: returns (rows_local, N) in this rank's row order."""
-        import ctypes
-        from . import _lib
-        from .ops import _OUT_DTYPES, _workspace, as_u8
-        lib = _lib.load()
-        K = a_q.shape[1]
-        L, N, Kw = w_q.shape
-        if w_q.dtype == torch.float4_e2m1fn_x2:
-            Kw *= 2
-        if Kw != K:
-            raise AssertionError(f"K mismatch: activations {K}, weights {Kw}")
-        if N > self.max_n:
-            raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
-        self.dispatch(plan, a_q, a_s)
-        return self.compute(plan, K, w_q, w_s, out_dtype)
+    def dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
+        self.start_dispatch(plan, a_q, a_s)
+        self.finish_dispatch()
+
+    def self_rows(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor):
+        """The rows this rank routed to its own experts (views, no copy)."""
+        r0, n = plan.self_row, plan.self_rows
+        return a_q[r0:r0 + n], a_s[r0:r0 + n]
 
     def received(self, plan: FusedPlan, K: int):
-        """The dispatched rows as (rows_recv, K) e4m3 and (rows_recv, K/32) scale views."""
+        """The peers' dispatched rows as (rows_recv, K) e4m3 and (rows_recv, K/32) scale views."""
         R = plan.rows_recv
         return (self.recv_a.view((R, K), torch.uint8).view(torch.float8_e4m3fn),
                 self.recv_s.view((R, K // 32), torch.uint8))
 
-    def compute(self, plan: FusedPlan, K: int, w_q: Tensor, w_s: Tensor,
-                out_dtype: torch.dtype = torch.bfloat16, a: Optional[tuple] = None) -> Tensor:
-        """The GEMM over rows already dispatched (`dispatch`), its peer stores
-        and the closing barrier.  `a` = (a_q, a_s) replaces the receive
-        buffers with local rows in the same segment layout (for example the
-        quantised output of an earlier GEMM over the received rows)."""
+    def gemm(self, plan: FusedPlan, part: str, K: int, w_q: Tensor, w_s: Tensor,
+             out_dtype: torch.dtype = torch.bfloat16, a: Optional[tuple] = None) -> None:
+        """One part of the expert GEMM with its outputs sent to their owners.
+
+        part "self": the rows this rank routed to itself (`a` = their
+        (a_q, a_s), from `self_rows`, or an earlier GEMM's output over them);
+        part "remote": the received rows (`a` defaults to the receive buffers)."""
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
         lib = _lib.load()
         L, N, _ = w_q.shape
-        R = plan.rows_recv
+        if N > self.max_n:
+            raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
+        seg = plan.self_seg if part == "self" else plan.remote_seg
+        R = plan.self_rows if part == "self" else plan.rows_recv
         if a is None:
-            recv_q = self.recv_a.view((R, K), torch.uint8)
-            recv_s = self.recv_s.view((R, K // 32), torch.uint8)
-        else:
-            recv_q, recv_s = a[0].contiguous(), as_u8(a[1]).contiguous()
-            if recv_q.shape != (R, K) or recv_s.shape != (R, K // 32):
-                raise ValueError(f"local rows {tuple(recv_q.shape)} do not match the plan's ({R}, {K})")
-        S = plan.seg_offs.numel()
+            if part == "self":
+                raise ValueError("the self part needs its rows")
+            a = self.received(plan, K)
+        a_q, a_s = a[0].contiguous(), as_u8(a[1]).contiguous()
+        if a_q.shape[0] != R or a_s.shape != (R, K // 32):
+            raise ValueError(f"rows {tuple(a_q.shape)} do not match the plan's ({R}, {K})")
+        if R == 0:
+            return
+        S = seg.offs.numel()
         ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(R, N, K, S, L), w_q.device)
         outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
         rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
@@ -420,18 +447,37 @@ class FusedExpertParallel:
         w_q = w_q.contiguous()
         w_s = as_u8(w_s).contiguous()
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        _lib.check(lib.mxgg_grouped_mm_ep(p(recv_q), p(w_q), p(recv_s), p(w_s), p(plan.seg_offs), p(plan.seg_expert),
-                                          p(plan.seg_dst), p(plan.seg_dst_row), R, N, K, S, L, b_format_of(w_q),
-                                          outs, rows, inboxes,
-                                          self.world, self.rank, _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
-                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+        _lib.check(lib.mxgg_grouped_mm_ep(p(a_q), p(w_q), p(a_s), p(w_s), p(seg.offs), p(seg.expert),
+                                          p(seg.dst), p(seg.dst_row), R, N, K, S, L, b_format_of(w_q),
+                                          outs, rows, inboxes, self.world, self.rank, _OUT_DTYPES[out_dtype],
+                                          p(ws), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_grouped_mm_ep")
+
+    def finish(self, plan: FusedPlan, N: int, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """Barrier (every rank's stores are in), unpack this rank's inbox;
+        returns its (rows_local, N) output view."""
+        import ctypes
+        from . import _lib
         self.barrier()
         es = torch.empty((), dtype=out_dtype).element_size()
         if plan.inbox_ok and plan.remote_blocks.numel() and (N * es) % 64 == 0:
-            _lib.check(lib.mxgg_inbox_unpack(ctypes.c_void_p(self.inbox.ptrs[self.rank]),
-                                             ctypes.c_void_p(self.out.ptrs[self.rank]), p(plan.remote_blocks),
-                                             plan.remote_blocks.numel(), N * es,
-                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+            _lib.check(_lib.load().mxgg_inbox_unpack(ctypes.c_void_p(self.inbox.ptrs[self.rank]),
+                                                     ctypes.c_void_p(self.out.ptrs[self.rank]),
+                                                     ctypes.c_void_p(plan.remote_blocks.data_ptr()),
+                                                     plan.remote_blocks.numel(), N * es,
+                                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                        "mxgg_inbox_unpack")
         return self.out.view((plan.rows_local, N), out_dtype)
+
+    def grouped_mm(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s: Tensor,
+                   out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """Fused forward / dgrad: returns (rows_local, N) in this rank's row order."""
+        K = a_q.shape[1]
+        Kw = w_q.shape[2] * (2 if w_q.dtype == torch.float4_e2m1fn_x2 else 1)
+        if Kw != K:
+            raise AssertionError(f"K mismatch: activations {K}, weights {Kw}")
+        self.start_dispatch(plan, a_q, a_s)
+        self.gemm(plan, "self", K, w_q, w_s, out_dtype, a=self.self_rows(plan, a_q, a_s))
+        self.finish_dispatch()
+        self.gemm(plan, "remote", K, w_q, w_s, out_dtype)
+        return self.finish(plan, w_q.shape[1], out_dtype)

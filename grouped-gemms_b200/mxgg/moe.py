@@ -116,14 +116,24 @@ class MoELayer:
             h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
             y = grouped_mm_segments_op(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
         else:
+            # rows routed to this rank's own experts start while peers' rows are in flight
             ep = self.ep
             plan = ep.plan(layout.counts, self.placement)
-            ep.dispatch(plan, a_q, a_s)
-            r_q, r_s = ep.received(plan, self.d_model)
-            h = grouped_mm_segments_op(r_q, self.up_q, r_s, self.up_s, plan.seg_offs, plan.seg_expert, torch.bfloat16)
-            h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
-            y = ep.compute(plan, self.d_ff, self.down_q, self.down_s, torch.bfloat16, a=(h_q, h_s))
+            ep.start_dispatch(plan, a_q, a_s)
+            sq, ss = ep.self_rows(plan, a_q, a_s)
+            hs_s, hs_q = self._up(sq, ss, plan.self_seg)
+            ep.gemm(plan, "self", self.d_ff, self.down_q, self.down_s, torch.bfloat16, a=(hs_q, hs_s))
+            ep.finish_dispatch()
+            rq, rs = ep.received(plan, self.d_model)
+            hr_s, hr_q = self._up(rq, rs, plan.remote_seg)
+            ep.gemm(plan, "remote", self.d_ff, self.down_q, self.down_s, torch.bfloat16, a=(hr_q, hr_s))
+            y = ep.finish(plan, self.d_model, torch.bfloat16)
         return combine_top2(y, layout, weights)
+
+    def _up(self, a_q, a_s, seg):
+        """Up projection over one part's segments, then to_mx of its output."""
+        h = grouped_mm_segments_op(a_q, self.up_q, a_s, self.up_s, seg.offs, seg.expert, torch.bfloat16)
+        return to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
 
     def flops(self, tokens: int) -> float:
         """Useful FLOPs of one forward over `tokens` tokens (padding excluded)."""
