@@ -249,6 +249,9 @@ struct EpRoute {
   void* out_dst[kMaxDst] = {};
   int64_t rows_dst[kMaxDst] = {};
   void* inbox_dst[kMaxDst] = {};   // all null: peers' rows are stored in place
+  const void* a_atoms = nullptr;   // A scale atoms packed by the senders (null: pack here)
+  const int32_t* src_flags = nullptr;
+  int32_t src_epoch = 0;
 };
 
 // split_ok = 0: the caller's scratch only needs the packed scales and the
@@ -354,7 +357,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     if (ld % 16 == 0 && aligned(a_scale, 16) && aligned(b_scale, 16)) pp.vec = 4;
     else if (ld % 4 == 0 && aligned(a_scale, 4) && aligned(b_scale, 4)) pp.vec = 1;
     else pp.vec = 0;
-    pp.a_subtiles = (int)ws.a_subtiles;
+    // A atoms the senders packed already: pack only B here
+    pp.a_subtiles = (route && route->a_atoms) ? 0 : (int)ws.a_subtiles;
     pp.b_tiles = (int)ws.b_tiles;
     pp.a_out = ws_a;
     pp.b_out = ws_b;
@@ -363,7 +367,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
       pp.zero_count = ws.counter_bytes / 4;
     }
     const long long chunks = (ws.stages + 3) / 4;
-    const long long warps = (ws.a_subtiles + ws.b_tiles * (bn / 128)) * chunks;
+    const long long warps = ((long long)pp.a_subtiles + ws.b_tiles * (bn / 128)) * chunks;
     const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
     pack_scales_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pp);
     MXGG_CUDA_TRY(cudaGetLastError());
@@ -403,6 +407,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
         inbox = false;
     }
     p.inbox_chunks = inbox ? (int)((out_cols * es) / 64) : 0;
+    p.src_flags = route->src_flags;
+    p.src_epoch = route->src_epoch;
   } else {
     p.n_dst = 1;
     p.local_dst = 0;
@@ -430,7 +436,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                      : make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C,
                                     (uint64_t)C, kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = make_tmap_2d(&maps.sfa, ws_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+  if (int rc = make_tmap_2d(&maps.sfa, (route && route->a_atoms) ? route->a_atoms : ws_a,
+                            CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
                             (uint64_t)(ws.a_subtiles * ws.stages * 4), 128, 128, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   if (int rc = make_tmap_2d(&maps.sfb, ws_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
@@ -699,7 +706,8 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                        const int32_t* segment_end_offsets, const int32_t* segment_expert, const int32_t* segment_dst,
                        const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
                        int64_t n_experts, int32_t b_format, void* const* dst_out, const int64_t* dst_rows,
-                       void* const* dst_inbox, int32_t n_dst, int32_t local_dst, int out_dtype, void* workspace,
+                       void* const* dst_inbox, int32_t n_dst, int32_t local_dst, const void* a_atoms,
+                       const int32_t* src_flags, int32_t src_epoch, int out_dtype, void* workspace,
                        int64_t workspace_bytes, void* stream) {
   if (!segment_expert || !dst_out || !dst_rows)
     return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: null segment or destination table");
@@ -715,9 +723,68 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
     r.rows_dst[i] = dst_rows[i];
     r.inbox_dst[i] = dst_inbox ? dst_inbox[i] : nullptr;
   }
+  if (a_atoms && !aligned(a_atoms, 256)) return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: a_atoms not 256-byte aligned");
+  r.a_atoms = a_atoms;
+  r.src_flags = src_flags;
+  r.src_epoch = src_epoch;
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, nullptr, out_dtype,
                   workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r,
                   b_format);
+}
+
+int32_t mxgg_query_tile_m(void) { return pick_tiles(256).tile_m; }
+
+int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments) {
+  if (M < 0 || K < 0 || n_segments < 1) return -1;
+  int64_t best = 0;
+  for (int tm : {128, 256}) best = std::max<int64_t>(best, plan_workspace(kFwd, M, 128, K, n_segments, 1, tm, 128).a_bytes);
+  return best;
+}
+
+int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
+                      int64_t n_segments, int32_t tile_m, void* out, void* stream) {
+  if (rows < 0 || K <= 0 || K % 32 != 0 || n_segments < 1 || n_segments > kMaxGroups ||
+      (tile_m != 128 && tile_m != 256))
+    return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: bad sizes (rows %lld, K %lld, segments %lld, tile_m %d)",
+                (long long)rows, (long long)K, (long long)n_segments, (int)tile_m);
+  if (rows == 0) return MXGG_OK;
+  if (!a_scale || !segment_end_offsets || !out) return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: null pointer");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  PackParams pp{};
+  pp.mode = kFwd;
+  pp.E = (int)n_segments;
+  pp.M = (int)rows;
+  pp.N = 128;
+  pp.K = (int)K;
+  pp.tile_m = tile_m;
+  pp.tile_n = 128;
+  pp.stages = (int)((K + kBK - 1) / kBK);
+  pp.offs = segment_end_offsets;
+  pp.sfa = static_cast<const uint8_t*>(a_scale);
+  pp.sfb = static_cast<const uint8_t*>(a_scale);
+  pp.rows_a = (int)rows;
+  pp.rows_b = 1;
+  pp.sf_ld = K / 32;
+  const int64_t ld = K / 32;
+  pp.vec = (ld % 16 == 0 && aligned(a_scale, 16)) ? 4 : ((ld % 4 == 0 && aligned(a_scale, 4)) ? 1 : 0);
+  pp.a_subtiles = (int)(((rows + tile_m - 1) / tile_m + (n_segments - 1)) * (tile_m / kBM));
+  pp.b_tiles = 0;
+  pp.a_out = static_cast<uint8_t*>(out);
+  pp.b_out = nullptr;
+  const long long chunks = (pp.stages + 3) / 4;
+  const long long warps = (long long)pp.a_subtiles * chunks;
+  const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
+  pack_scales_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pp);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_peer_signal(void* slot, int32_t epoch, void* stream) {
+  if (!slot || !aligned(slot, 4)) return fail(MXGG_ERR_INVALID, "mxgg_peer_signal: bad slot");
+  peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int*>(slot), epoch);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
 }
 
 int mxgg_ipc_alloc(int64_t bytes, void** ptr, void* handle) {

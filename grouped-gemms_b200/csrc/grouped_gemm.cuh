@@ -56,6 +56,8 @@ enum : uint32_t {
   kErrAccWait = 8u,
   kErrEpilogueWait = 16u,
   kErrDrain = 32u,
+  // 64 is the cross-GPU barrier's (peer.cuh)
+  kErrSourceWait = 128u,     // expert parallel: a source's rows never arrived
 };
 
 struct GemmParams {
@@ -98,6 +100,11 @@ struct GemmParams {
   // 2 KB runs at several times the rate of 64-byte row pieces.
   void* inbox_dst[kMaxDst];
   int inbox_chunks;          // 64-byte chunks per output row; 0: no inboxes
+  // Streaming dispatch: the rows of group g come from rank group_dst[g]; the
+  // producer loads a tile only once that rank's slot of src_flags has reached
+  // src_epoch (written, after its copies, by the sender).  Null: no waits.
+  const int* src_flags;
+  int src_epoch;
 };
 
 // Output tensor maps: [0] the output of a single-GPU call; for an
@@ -386,6 +393,22 @@ __device__ __forceinline__ void raise_error(const GemmParams& p, volatile int* a
   *abort = 1;
 }
 
+// Bounded wait (1 s of %globaltimer, or an abort) for source `src`'s rows;
+// then orders them before this thread's TMA (async-proxy) reads.
+__device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volatile int* abort) {
+  const int* flag = p.src_flags + src;
+  const uint64_t t0 = ptx::globaltimer();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v - p.src_epoch >= 0) break;
+    if (*abort || ptx::globaltimer() - t0 > 1000000000ull) return false;
+    __nanosleep(64);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -501,7 +524,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int k = 0;
       Unit u;
+      uint32_t ready = 0;   // sources whose rows have arrived (streaming dispatch)
       while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
+        if (p.src_flags && u.st_count > 0 && !((ready >> u.dst) & 1u)) {
+          if (!wait_source(p, u.dst, abort)) {
+            raise_error(p, abort, kErrSourceWait);
+            ok = false;
+            break;
+          }
+          ready |= 1u << u.dst;
+        }
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const int stage = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;

@@ -205,7 +205,7 @@ def replica_groups(placement: ExpertPlacement) -> dict:
 class _Segments:
     offs: Tensor                 # int32 cumulative ends of the segments (rows of the A operand)
     expert: Tensor               # local expert of each segment
-    dst: Tensor                  # rank that owns each segment's rows
+    dst: Tensor                  # rank that owns each segment's rows (its source)
     dst_row: Tensor              # first row of the segment in its owner's output
 
 
@@ -213,39 +213,41 @@ class _Segments:
 class FusedPlan:
     """Routing of one fused expert-parallel call, as seen by one rank.
 
-    The rows a rank routes to its own experts never move: the "self" GEMM
-    reads them from the caller's tensor (rows [self_row, self_row +
-    self_rows)) while the other ranks' rows are in flight.  The receive
-    buffer holds only peers' rows, source-major, then local expert."""
+    Receive layout of rank d (its A operand): sources in arrival order d,
+    d-1, d-2, ... (its own rows first, copied locally), each source's rows
+    grouped by local expert.  Rank s sends to s, s+1, s+2, ... in turn, so
+    every receiver gets its sources one after another in that order."""
 
     rows_local: int
-    rows_recv: int               # rows received from peers
-    copies: List[tuple]          # (dest rank, first row there, first local row, rows), dest != this rank
-    self_row: int
-    self_rows: int
-    self_seg: _Segments          # L segments over the self rows
-    remote_seg: _Segments        # world * L segments over the receive buffer (own source: empty)
+    rows_recv: int               # all rows this rank multiplies (its own included)
+    copies: List[tuple]          # (dest rank, first row there, first local row, rows), in sending order
+    pack: List[tuple]            # (dest rank, cumulative segment ends (device), first m-tile there)
+    seg: _Segments               # world * L segments over the receive buffer
+    local_seg: _Segments         # the same segments with every row kept here, in receive order
     dst_rows: List[int]          # local rows of every rank (the output buffers' heights)
+    tile_m: int
     inbox_ok: bool               # every segment starts on a 32-row boundary: peers' blocks go by inbox
     remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
 
 
 class FusedExpertParallel:
-    """Expert-parallel forward / dgrad over NVLink peer memory.
+    """Expert-parallel forward / dgrad over NVLink peer memory, with the
+    dispatch streamed into the GEMM and the combine fused into its epilogue.
 
     Collective to construct (it allocates and maps the shared buffers).  Per
     call (`grouped_mm`):
 
-    1. each rank starts pushing its rows for rank d straight into d's receive
-       buffer (one copy-engine ``cudaMemcpyAsync`` per peer, on parallel
-       streams) and, meanwhile, multiplies the rows it routed to its own
-       experts where they lie;
-    2. a cross-GPU barrier, then ``mxgg_grouped_mm_ep`` multiplies the
-       received segments and sends each output block to the rank that owns
-       its rows as the tile finishes (TMA stores for its own rows; 2 KB bulk
-       copies into the owner's inbox for peers'), so the return trip overlaps
-       the math tile by tile;
-    3. a second barrier, then each rank unpacks its inbox into its output.
+    1. each rank packs the scale atoms of its rows straight into every
+       destination's atom buffer (in the destination's tile numbering), then,
+       on a side stream, copies its rows into the destinations' receive
+       buffers one destination after another (copy engine; its own rows first)
+       and after each copy raises that destination's flag for it;
+    2. meanwhile the GEMM runs over the whole receive buffer: its producer
+       loads a segment's tiles as soon as the segment's source has raised its
+       flag (a bounded wait), and its epilogue sends every output block to the
+       rank that owns the rows (TMA stores for its own rows; 2 KB bulk copies
+       into the owner's inbox for peers'), so both transfers overlap the math;
+    3. a cross-GPU barrier, then each rank unpacks its inbox into its output.
 
     The returned tensor is a view of this rank's shared output buffer: use it
     before the next call.
@@ -253,6 +255,7 @@ class FusedExpertParallel:
 
     def __init__(self, placement: ExpertPlacement, max_recv_rows: int, max_local_rows: int, max_k: int, max_n: int,
                  group=None):
+        from . import _lib
         from .peer import PeerBuffer
         dist = _dist()
         self.placement = placement
@@ -265,29 +268,33 @@ class FusedExpertParallel:
             raise ValueError("the fused path reaches at most 8 ranks (one NVLink domain)")
         self.max_recv_rows, self.max_local_rows = int(max_recv_rows), int(max_local_rows)
         self.max_k, self.max_n = int(max_k), int(max_n)
+        lib = _lib.load()
         self.recv_a = PeerBuffer(max(self.max_recv_rows * self.max_k, 256), group)
-        self.recv_s = PeerBuffer(max(self.max_recv_rows * self.max_k // 32, 256), group)
+        self.atoms = PeerBuffer(max(lib.mxgg_ep_atom_bytes(self.max_recv_rows, self.max_k, 256), 256), group)
         self.out = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
         self.inbox = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
-        self.flags = PeerBuffer(256, group)
+        self.flags = PeerBuffer(256, group)          # barrier slots
+        self.src_flags = PeerBuffer(256, group)      # streaming-dispatch slots, one per source
         self.epoch = 0
-        self._streams = [torch.cuda.Stream() for _ in range(self.world)]
-        self._pending = []
+        self.src_epoch = 0
+        self._side = torch.cuda.Stream()
+        self._side_pending = False
         # every rank's capacities, so a plan that overflows any of them fails on all ranks alike
         caps = [None] * self.world
         dist.all_gather_object(caps, (self.max_recv_rows, self.max_local_rows), group=group)
         self._caps = caps
 
     def close(self) -> None:
-        for b in (self.recv_a, self.recv_s, self.out, self.inbox, self.flags):
+        for b in (self.recv_a, self.atoms, self.out, self.inbox, self.flags, self.src_flags):
             b.close()
 
     # -------------------------------------------------------------- planning
     def plan(self, expert_counts: Sequence[int], placement: Optional[ExpertPlacement] = None) -> FusedPlan:
         """Collective: all-gather every rank's per-expert counts and derive the
-        copies, segment tables and output heights.  The shared buffers do not
-        depend on the placement, so one instance serves several (`placement`
-        overrides the constructor's for this plan)."""
+        copies, atom packing, segment tables and output heights.  The shared
+        buffers do not depend on the placement, so one instance serves several
+        (`placement` overrides the constructor's for this plan)."""
+        from . import _lib
         dist = _dist()
         pl, world, rank = placement or self.placement, self.world, self.rank
         if pl.world != world:
@@ -300,6 +307,7 @@ class FusedExpertParallel:
         allc = torch.empty(world, E, dtype=torch.int64, device=dev)
         dist.all_gather_into_tensor(allc, mine, group=self.group)
         C = allc.tolist()                                     # C[s][e], one device sync
+        tile_m = int(_lib.load().mxgg_query_tile_m())
         # rows rank s sends to rank d, and where they start in s's local order
         send = [[0] * world for _ in range(world)]
         start = [[0] * world for _ in range(world)]
@@ -312,30 +320,40 @@ class FusedExpertParallel:
                     start[s][d], seen[s][d] = row, True
                 send[s][d] += C[s][e]
                 row += C[s][e]
-        # receive layout of rank d: peers only, source-major, then local expert
-        recv_off = [[sum(send[s2][d] for s2 in range(s) if s2 != d) for d in range(world)] for s in range(world)]
-        copies = [(d, recv_off[rank][d], start[rank][d], send[rank][d])
-                  for d in range(world) if d != rank and send[rank][d]]
-        mine_e = pl.experts_of(rank)
-        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+        order = lambda d: [(d - j) % world for j in range(world)]   # noqa: E731  (sources, arrival order)
 
-        def segments(sources):
-            offs, expert, dsts, first = [], [], [], []
-            total = 0
-            for s in range(world):
-                for le, e in enumerate(mine_e):
-                    rows = C[s][e] if (s in sources and pl.dest(s, e) == rank) else 0
-                    total += rows
-                    offs.append(total)
-                    expert.append(le)
-                    dsts.append(s)
-                    first.append(sum(C[s][:e]))
-            return total, _Segments(i32(offs), i32(expert), i32(dsts), i32(first))
+        def seg_rows(s, d):
+            return [C[s][e] if pl.dest(s, e) == d else 0 for e in pl.experts_of(d)]
 
-        rows_recv, remote_seg = segments([s for s in range(world) if s != rank])
-        self_rows, self_seg = segments([rank])
+        # where each source's rows and atoms start at each receiver
+        recv_off = [[0] * world for _ in range(world)]
+        m0 = [[0] * world for _ in range(world)]
         for d in range(world):
-            need_recv = sum(send[s][d] for s in range(world) if s != d)
+            r = m = 0
+            for s in order(d):
+                recv_off[s][d], m0[s][d] = r, m
+                r += send[s][d]
+                m += sum((c + tile_m - 1) // tile_m for c in seg_rows(s, d))
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+        copies, pack = [], []
+        for j in range(world):
+            d = (rank + j) % world
+            if send[rank][d]:
+                copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
+                cum = torch.tensor(seg_rows(rank, d), dtype=torch.int64).cumsum(0).to(torch.int32)
+                pack.append((d, cum.to(dev), m0[rank][d]))
+        offs, expert, dsts, first, lfirst = [], [], [], [], []
+        total = 0
+        for s in order(rank):
+            for le, (e, rows) in enumerate(zip(pl.experts_of(rank), seg_rows(s, rank))):
+                lfirst.append(total)
+                total += rows
+                offs.append(total)
+                expert.append(le)
+                dsts.append(s)
+                first.append(sum(C[s][:e]))
+        for d in range(world):
+            need_recv = sum(send[s][d] for s in range(world))
             if need_recv > self._caps[d][0] or sum(C[d]) > self._caps[d][1]:
                 raise ValueError(f"fused EP buffers of rank {d} too small: {need_recv} received / {sum(C[d])} "
                                  f"local rows for {self._caps[d][0]} / {self._caps[d][1]}")
@@ -345,9 +363,11 @@ class FusedExpertParallel:
             if pl.dest(rank, e) != rank:
                 blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
             row += C[rank][e]
-        return FusedPlan(rows_local=sum(C[rank]), rows_recv=rows_recv, copies=copies, self_row=start[rank][rank],
-                         self_rows=self_rows, self_seg=self_seg, remote_seg=remote_seg,
-                         dst_rows=[sum(C[d]) for d in range(world)], inbox_ok=inbox_ok,
+        o, x = i32(offs), i32(expert)
+        return FusedPlan(rows_local=sum(C[rank]), rows_recv=total, copies=copies, pack=pack,
+                         seg=_Segments(o, x, i32(dsts), i32(first)),
+                         local_seg=_Segments(o, x, i32([rank] * len(offs)), i32(lfirst)),
+                         dst_rows=[sum(C[d]) for d in range(world)], tile_m=tile_m, inbox_ok=inbox_ok,
                          remote_blocks=i32(blocks if inbox_ok else []))
 
     # ---------------------------------------------------------------- calls
@@ -361,9 +381,10 @@ class FusedExpertParallel:
                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_peer_barrier")
 
-    def start_dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
-        """Start pushing this rank's rows into their hosts' receive buffers
-        (copy engines, one stream per peer); `finish_dispatch` joins them."""
+    def dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
+        """Start the streamed dispatch of this rank's rows (sorted by expert):
+        scale atoms into every destination's atom buffer (on the current
+        stream), then row copies and per-destination flags (side stream)."""
         import ctypes
         from . import _lib
         lib = _lib.load()
@@ -372,92 +393,107 @@ class FusedExpertParallel:
             raise ValueError(f"K={K} exceeds the buffers' {self.max_k}")
         a_q = a_q.contiguous()
         a_s = a_s.contiguous()
+        self.src_epoch += 1
         cur = torch.cuda.current_stream()
-        ready = cur.record_event()
-        self._pending = []
+        sp = ctypes.c_void_p(cur.cuda_stream)
+        stages = (K + 127) // 128
+        atom_bytes_per_mtile = (plan.tile_m // 128) * stages * 512
+        for (d, cum, m0), (_, _, src_row, rows) in zip(plan.pack, plan.copies):
+            _lib.check(lib.mxgg_pack_a_atoms(ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)),
+                                             ctypes.c_void_p(cum.data_ptr()), rows, K, cum.numel(), plan.tile_m,
+                                             ctypes.c_void_p(self.atoms.ptrs[d] + m0 * atom_bytes_per_mtile), sp),
+                       "mxgg_pack_a_atoms")
+        side = self._side
+        side.wait_stream(cur)
+        ssp = ctypes.c_void_p(side.cuda_stream)
         for (d, dst_row, src_row, rows) in plan.copies:
-            st = self._streams[d]
-            st.wait_event(ready)
-            sp = ctypes.c_void_p(st.cuda_stream)
             _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_a.ptrs[d] + dst_row * K),
-                                           ctypes.c_void_p(a_q.data_ptr() + src_row * K), rows * K, sp),
+                                           ctypes.c_void_p(a_q.data_ptr() + src_row * K), rows * K, ssp),
                        "mxgg_copy_async")
-            _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_s.ptrs[d] + dst_row * (K // 32)),
-                                           ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)), rows * (K // 32),
-                                           sp), "mxgg_copy_async")
-            self._pending.append(st.record_event())
-            # the caching allocator must not hand the sources out before the copies finish
-            a_q.record_stream(st)
-            a_s.record_stream(st)
+            _lib.check(lib.mxgg_peer_signal(ctypes.c_void_p(self.src_flags.ptrs[d] + 4 * self.rank),
+                                            self.src_epoch, ssp), "mxgg_peer_signal")
+        # (a destination this rank sends no rows to never waits for it: its segments are empty)
+        a_q.record_stream(side)
+        a_s.record_stream(side)
+        self._side_pending = True
 
-    def finish_dispatch(self) -> None:
-        """The current stream waits for this rank's copies, then for every
-        rank's (cross-GPU barrier): the receive buffers are complete."""
-        cur = torch.cuda.current_stream()
-        for ev in self._pending:
-            cur.wait_event(ev)
-        self._pending = []
-        self.barrier()
+    def received(self, plan: FusedPlan, K: int) -> Tensor:
+        """The receive buffer as (rows_recv, K) e4m3 (complete after `finish`)."""
+        return self.recv_a.view((plan.rows_recv, K), torch.uint8).view(torch.float8_e4m3fn)
 
-    def dispatch(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor) -> None:
-        self.start_dispatch(plan, a_q, a_s)
-        self.finish_dispatch()
-
-    def self_rows(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor):
-        """The rows this rank routed to its own experts (views, no copy)."""
-        r0, n = plan.self_row, plan.self_rows
-        return a_q[r0:r0 + n], a_s[r0:r0 + n]
-
-    def received(self, plan: FusedPlan, K: int):
-        """The peers' dispatched rows as (rows_recv, K) e4m3 and (rows_recv, K/32) scale views."""
-        R = plan.rows_recv
-        return (self.recv_a.view((R, K), torch.uint8).view(torch.float8_e4m3fn),
-                self.recv_s.view((R, K // 32), torch.uint8))
-
-    def gemm(self, plan: FusedPlan, part: str, K: int, w_q: Tensor, w_s: Tensor,
-             out_dtype: torch.dtype = torch.bfloat16, a: Optional[tuple] = None) -> None:
-        """One part of the expert GEMM with its outputs sent to their owners.
-
-        part "self": the rows this rank routed to itself (`a` = their
-        (a_q, a_s), from `self_rows`, or an earlier GEMM's output over them);
-        part "remote": the received rows (`a` defaults to the receive buffers)."""
+    def _ep_gemm(self, plan, seg, a_q, K, w_q, w_s, out_dtype, outs, rows, inboxes, a_atoms, src_flags, a_s=None):
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
         lib = _lib.load()
         L, N, _ = w_q.shape
-        if N > self.max_n:
-            raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
-        seg = plan.self_seg if part == "self" else plan.remote_seg
-        R = plan.self_rows if part == "self" else plan.rows_recv
-        if a is None:
-            if part == "self":
-                raise ValueError("the self part needs its rows")
-            a = self.received(plan, K)
-        a_q, a_s = a[0].contiguous(), as_u8(a[1]).contiguous()
-        if a_q.shape[0] != R or a_s.shape != (R, K // 32):
-            raise ValueError(f"rows {tuple(a_q.shape)} do not match the plan's ({R}, {K})")
+        R = a_q.shape[0]
         if R == 0:
             return
         S = seg.offs.numel()
         ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(R, N, K, S, L), w_q.device)
-        outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
-        rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
-        inboxes = (ctypes.c_void_p * self.world)(*self.inbox.ptrs) if plan.inbox_ok else None
         w_q = w_q.contiguous()
         w_s = as_u8(w_s).contiguous()
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        _lib.check(lib.mxgg_grouped_mm_ep(p(a_q), p(w_q), p(a_s), p(w_s), p(seg.offs), p(seg.expert),
-                                          p(seg.dst), p(seg.dst_row), R, N, K, S, L, b_format_of(w_q),
-                                          outs, rows, inboxes, self.world, self.rank, _OUT_DTYPES[out_dtype],
-                                          p(ws), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+        scale = p(as_u8(a_s).contiguous()) if a_s is not None else ctypes.c_void_p(a_atoms)
+        _lib.check(lib.mxgg_grouped_mm_ep(p(a_q), p(w_q), scale, p(w_s), p(seg.offs), p(seg.expert), p(seg.dst),
+                                          p(seg.dst_row), R, N, K, S, L, b_format_of(w_q), outs, rows, inboxes,
+                                          self.world, self.rank,
+                                          ctypes.c_void_p(a_atoms) if a_atoms else None,
+                                          ctypes.c_void_p(src_flags) if src_flags else None, self.src_epoch,
+                                          _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_grouped_mm_ep")
 
+    def gemm_received(self, plan: FusedPlan, K: int, w_q: Tensor, w_s: Tensor,
+                      out_dtype: torch.dtype = torch.bfloat16, local_out: Optional[Tensor] = None) -> None:
+        """GEMM over the receive buffer as it fills (after `dispatch`).  Output
+        rows go to their owners, or, with `local_out` ((rows_recv, N)), stay
+        here in receive order."""
+        import ctypes
+        L, N, _ = w_q.shape
+        if N > self.max_n:
+            raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
+        a = self.recv_a.view((plan.rows_recv, K), torch.uint8)
+        if local_out is not None:
+            if local_out.shape != (plan.rows_recv, N) or not local_out.is_contiguous():
+                raise ValueError("local_out must be a contiguous (rows_recv, N) tensor")
+            outs = (ctypes.c_void_p * self.world)(*[local_out.data_ptr() if r == self.rank else 0
+                                                    for r in range(self.world)])
+            rows = (ctypes.c_int64 * self.world)(*[plan.rows_recv if r == self.rank else 0
+                                                   for r in range(self.world)])
+            self._ep_gemm(plan, plan.local_seg, a, K, w_q, w_s, out_dtype, outs, rows, None,
+                          self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank])
+            return
+        outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
+        rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
+        inboxes = (ctypes.c_void_p * self.world)(*self.inbox.ptrs) if plan.inbox_ok else None
+        self._ep_gemm(plan, plan.seg, a, K, w_q, w_s, out_dtype, outs, rows, inboxes,
+                      self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank])
+
+    def gemm_local(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s: Tensor,
+                   out_dtype: torch.dtype = torch.bfloat16) -> None:
+        """GEMM over local rows laid out like the receive buffer (for example
+        the quantised output of `gemm_received(local_out=...)`), output rows
+        to their owners."""
+        import ctypes
+        K = a_q.shape[1]
+        if a_q.shape[0] != plan.rows_recv:
+            raise ValueError("local rows must match the plan's receive layout")
+        outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
+        rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
+        inboxes = (ctypes.c_void_p * self.world)(*self.inbox.ptrs) if plan.inbox_ok else None
+        self._ep_gemm(plan, plan.seg, a_q.contiguous(), K, w_q, w_s, out_dtype, outs, rows, inboxes, None, None,
+                      a_s=a_s)
+
     def finish(self, plan: FusedPlan, N: int, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
-        """Barrier (every rank's stores are in), unpack this rank's inbox;
-        returns its (rows_local, N) output view."""
+        """Join the copies, barrier (every rank's stores are in), unpack this
+        rank's inbox; returns its (rows_local, N) output view."""
         import ctypes
         from . import _lib
+        if self._side_pending:
+            torch.cuda.current_stream().wait_stream(self._side)
+            self._side_pending = False
         self.barrier()
         es = torch.empty((), dtype=out_dtype).element_size()
         if plan.inbox_ok and plan.remote_blocks.numel() and (N * es) % 64 == 0:
@@ -476,8 +512,6 @@ class FusedExpertParallel:
         Kw = w_q.shape[2] * (2 if w_q.dtype == torch.float4_e2m1fn_x2 else 1)
         if Kw != K:
             raise AssertionError(f"K mismatch: activations {K}, weights {Kw}")
-        self.start_dispatch(plan, a_q, a_s)
-        self.gemm(plan, "self", K, w_q, w_s, out_dtype, a=self.self_rows(plan, a_q, a_s))
-        self.finish_dispatch()
-        self.gemm(plan, "remote", K, w_q, w_s, out_dtype)
+        self.dispatch(plan, a_q, a_s)
+        self.gemm_received(plan, K, w_q, w_s, out_dtype)
         return self.finish(plan, w_q.shape[1], out_dtype)

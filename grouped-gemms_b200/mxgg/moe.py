@@ -116,24 +116,17 @@ class MoELayer:
             h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
             y = grouped_mm_segments_op(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
         else:
-            # rows routed to this rank's own experts start while peers' rows are in flight
+            # rows stream into the hosts' receive buffers while the up projection
+            # consumes them; the down projection sends its rows to their owners
             ep = self.ep
             plan = ep.plan(layout.counts, self.placement)
-            ep.start_dispatch(plan, a_q, a_s)
-            sq, ss = ep.self_rows(plan, a_q, a_s)
-            hs_s, hs_q = self._up(sq, ss, plan.self_seg)
-            ep.gemm(plan, "self", self.d_ff, self.down_q, self.down_s, torch.bfloat16, a=(hs_q, hs_s))
-            ep.finish_dispatch()
-            rq, rs = ep.received(plan, self.d_model)
-            hr_s, hr_q = self._up(rq, rs, plan.remote_seg)
-            ep.gemm(plan, "remote", self.d_ff, self.down_q, self.down_s, torch.bfloat16, a=(hr_q, hr_s))
+            ep.dispatch(plan, a_q, a_s)
+            h = torch.empty((plan.rows_recv, self.d_ff), dtype=torch.bfloat16, device=x.device)
+            ep.gemm_received(plan, self.d_model, self.up_q, self.up_s, torch.bfloat16, local_out=h)
+            h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
+            ep.gemm_local(plan, h_q, h_s, self.down_q, self.down_s, torch.bfloat16)
             y = ep.finish(plan, self.d_model, torch.bfloat16)
         return combine_top2(y, layout, weights)
-
-    def _up(self, a_q, a_s, seg):
-        """Up projection over one part's segments, then to_mx of its output."""
-        h = grouped_mm_segments_op(a_q, self.up_q, a_s, self.up_s, seg.offs, seg.expert, torch.bfloat16)
-        return to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
 
     def flops(self, tokens: int) -> float:
         """Useful FLOPs of one forward over `tokens` tokens (padding excluded)."""
