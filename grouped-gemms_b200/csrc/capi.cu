@@ -62,6 +62,8 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
+using WriteValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+WriteValueFn g_write_value = nullptr;
 
 int get_device_state(DeviceState** out) {
   int dev = 0;
@@ -87,6 +89,12 @@ int get_device_state(DeviceState** out) {
       if (q != cudaDriverEntryPointSuccess || !fn)
         return fail(MXGG_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
       g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    if (!g_write_value) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      MXGG_CUDA_TRY(cudaGetDriverEntryPoint("cuStreamWriteValue32", &fn, cudaEnableDefault, &q));
+      if (q == cudaDriverEntryPointSuccess && fn) g_write_value = reinterpret_cast<WriteValueFn>(fn);
     }
     st.init = true;
   }
@@ -128,7 +136,7 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
 constexpr int kMaxGridCtas = 160;
 
 struct Maps {
-  CUtensorMap a, b, sfa, sfb;
+  CUtensorMap a, a_self, b, sfa, sfb;
   OutMaps out;
 };
 
@@ -160,7 +168,7 @@ int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, lon
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.sfa, m.sfb, m.out, p));
+  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.a_self, m.b, m.sfa, m.sfb, m.out, p));
   return MXGG_OK;
 }
 
@@ -252,6 +260,11 @@ struct EpRoute {
   const void* a_atoms = nullptr;   // A scale atoms packed by the senders (null: pack here)
   const int32_t* src_flags = nullptr;
   int32_t src_epoch = 0;
+  const int32_t* group_src = nullptr;
+  const void* a_self = nullptr;    // rows of source self_src, read in place
+  int64_t a_self_rows = 0;
+  int32_t self_src = -1;
+  int64_t self_row_base = 0;
 };
 
 // split_ok = 0: the caller's scratch only needs the packed scales and the
@@ -409,11 +422,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     p.inbox_chunks = inbox ? (int)((out_cols * es) / 64) : 0;
     p.src_flags = route->src_flags;
     p.src_epoch = route->src_epoch;
+    p.group_src = route->group_src;
+    p.self_src = route->a_self ? route->self_src : -1;
+    p.self_row_base = (int)route->self_row_base;
   } else {
     p.n_dst = 1;
     p.local_dst = 0;
     p.out_dst[0] = out;
     p.out_rows_dst[0] = out_rows;
+    p.self_src = -1;
   }
   p.group_m = pick_group_m(tc);
   p.split_tail = split_tail ? 1 : 0;
@@ -426,6 +443,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (int rc = make_tmap_2d(&maps.a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
                             kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
+  if (route && route->a_self && route->a_self_rows > 0) {
+    if (!aligned(route->a_self, 16)) return fail(MXGG_ERR_INVALID, "%s: in-place rows must be 16-byte aligned", what);
+    if (int rc = make_tmap_2d(&maps.a_self, route->a_self, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                              (uint64_t)route->a_self_rows, (uint64_t)C, (uint64_t)C, kBK, kBM,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {
+    maps.a_self = maps.a;
+  }
   // e2m1 weights: packed two per byte in HBM; TMA's 16U4_ALIGN16B type
   // spreads every 16 values (8 bytes) over a 16-byte slot, the 8-bit
   // container layout kind::mxf8f6f4 reads, so the smem tile and its
@@ -707,8 +733,9 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                        const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
                        int64_t n_experts, int32_t b_format, void* const* dst_out, const int64_t* dst_rows,
                        void* const* dst_inbox, int32_t n_dst, int32_t local_dst, const void* a_atoms,
-                       const int32_t* src_flags, int32_t src_epoch, int out_dtype, void* workspace,
-                       int64_t workspace_bytes, void* stream) {
+                       const int32_t* src_flags, int32_t src_epoch, const int32_t* segment_src,
+                       const void* a_self, int64_t a_self_rows, int32_t self_src, int64_t self_row_base,
+                       int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!segment_expert || !dst_out || !dst_rows)
     return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: null segment or destination table");
   if (n_dst < 1 || n_dst > kMaxDst)
@@ -727,6 +754,13 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
   r.a_atoms = a_atoms;
   r.src_flags = src_flags;
   r.src_epoch = src_epoch;
+  r.group_src = segment_src;
+  if (a_self && (self_src < 0 || self_src >= n_dst || self_row_base < 0))
+    return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: bad in-place source %d", (int)self_src);
+  r.a_self = a_self;
+  r.a_self_rows = a_self_rows;
+  r.self_src = self_src;
+  r.self_row_base = self_row_base;
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, nullptr, out_dtype,
                   workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r,
                   b_format);
@@ -780,10 +814,17 @@ int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, i
   return MXGG_OK;
 }
 
+// A stream memory operation, not a kernel: it needs no SM, so it cannot be
+// held back by a GEMM that fills the GPU while waiting for the very flags
+// such signals raise on its peers.
 int mxgg_peer_signal(void* slot, int32_t epoch, void* stream) {
   if (!slot || !aligned(slot, 4)) return fail(MXGG_ERR_INVALID, "mxgg_peer_signal: bad slot");
-  peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int*>(slot), epoch);
-  MXGG_CUDA_TRY(cudaGetLastError());
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  if (!g_write_value) return fail(MXGG_ERR_UNSUPPORTED, "mxgg_peer_signal: cuStreamWriteValue32 is not available");
+  CUresult r = g_write_value(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(slot), (cuuint32_t)epoch,
+                             CU_STREAM_WRITE_VALUE_DEFAULT);
+  if (r != CUDA_SUCCESS) return fail(MXGG_ERR_CUDA, "mxgg_peer_signal: cuStreamWriteValue32 failed (%d)", (int)r);
   return MXGG_OK;
 }
 

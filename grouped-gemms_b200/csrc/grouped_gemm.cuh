@@ -105,6 +105,11 @@ struct GemmParams {
   // src_epoch (written, after its copies, by the sender).  Null: no waits.
   const int* src_flags;
   int src_epoch;
+  const int32_t* group_src;  // source rank of each group's rows (null: group_dst, the rows' owner)
+  // Rows of source self_src are read in place through the second A map
+  // (row + self_row_base) instead of from the receive buffer; they never wait.
+  int self_src;              // -1: none
+  int self_row_base;
 };
 
 // Output tensor maps: [0] the output of a single-GPU call; for an
@@ -126,6 +131,7 @@ struct Unit {
   int a_sub;         // packed A-scale sub-tile of the tile's first 128 rows
   int b_tile;        // packed B-scale tile
   int dst;           // output destination (0 unless expert-parallel routing)
+  int src;           // rank the rows come from (streaming dispatch)
   // a stage range of a tail tile that other CTA pairs share
   int split;         // 1: publish a partial; the last pair to arrive writes the tile
   int tail;          // index of the tile in the tail round (its arrival counter)
@@ -164,6 +170,7 @@ struct SmemLayout {
   int g_expert[kMaxGroups];  // fwd: B slice of each group
   int g_dst[kMaxGroups];     // fwd, expert parallel: output destination of each group
   int g_dst_row[kMaxGroups]; //   and its first row there
+  int g_src[kMaxGroups];     // fwd, streaming dispatch: source rank of each group's rows
 
   // a and b are one contiguous region (the split-tile reduction spans both)
   static_assert(sizeof(a) % 1024 == 0, "stage buffers must be contiguous");
@@ -215,9 +222,11 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
     if (p.group_dst) {
       sm->g_dst[i] = min(max(__ldg(p.group_dst + i), 0), p.n_dst - 1);
       sm->g_dst_row[i] = max(__ldg(p.group_dst_row + i), 0);
+      sm->g_src[i] = p.group_src ? min(max(__ldg(p.group_src + i), 0), p.n_dst - 1) : sm->g_dst[i];
     } else {
       sm->g_dst[i] = 0;
       sm->g_dst_row[i] = -1;
+      sm->g_src[i] = 0;
     }
   }
 }
@@ -249,6 +258,7 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
   Unit u;
   u.split = 0;
   u.dst = 0;
+  u.src = 0;
   u.tail = 0;
   u.n_contrib = 1;
   u.p0 = 0;
@@ -275,6 +285,7 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     const int ge = sm->g_expert[g];
     u.b_row = ge * p.N + n * BN;
     u.dst = sm->g_dst[g];
+    u.src = sm->g_src[g];
     u.out_row = (sm->g_dst_row[g] >= 0) ? (long long)sm->g_dst_row[g] + (row0 - sm->g_start[g]) : row0;
     u.out_col = n * BN;
     u.valid_rows = min(TILE_M, sm->g_end[g] - row0);
@@ -411,7 +422,8 @@ __device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volati
 
 template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_self,
+                        const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                         const __grid_constant__ OutMaps omaps, const GemmParams p) {
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
@@ -524,15 +536,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int k = 0;
       Unit u;
-      uint32_t ready = 0;   // sources whose rows have arrived (streaming dispatch)
+      // sources whose rows have arrived (streaming dispatch); rows read in place are always there
+      uint32_t ready = (p.self_src >= 0) ? (1u << p.self_src) : 0u;
       while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
-        if (p.src_flags && u.st_count > 0 && !((ready >> u.dst) & 1u)) {
-          if (!wait_source(p, u.dst, abort)) {
+        if (p.src_flags && u.st_count > 0 && !((ready >> u.src) & 1u)) {
+          if (!wait_source(p, u.src, abort)) {
             raise_error(p, abort, kErrSourceWait);
             ok = false;
             break;
           }
-          ready |= 1u << u.dst;
+          ready |= 1u << u.src;
         }
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const int stage = it % STAGES;
@@ -550,14 +563,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (PAIR == 2) {
             const uint32_t fb = leader_bar(&sm->full[stage]);
             if (leader) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&sm->full[stage]), kStageBytes);
-            ptx::tma_load_2d_pair(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row + kBM * (int)rank);
+            if (u.src == p.self_src)
+              ptx::tma_load_2d_pair(ptx::smem_u32(sm->a[stage]), &tmap_a_self, fb, x,
+                                    u.a_row + p.self_row_base + kBM * (int)rank);
+            else
+              ptx::tma_load_2d_pair(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row + kBM * (int)rank);
             ptx::tma_load_2d_pair(ptx::smem_u32(sm->b[stage]), &tmap_b, fb, x, u.b_row + kBRows * (int)rank);
             ptx::tma_load_2d_pair(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, fb, 0, ya);
             ptx::tma_load_2d_pair(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, fb, 0, yb);
           } else {
             const uint32_t fb = ptx::smem_u32(&sm->full[stage]);
             ptx::mbar_arrive_expect_tx(fb, kStageBytes);
-            ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row);
+            if (u.src == p.self_src)
+              ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a_self, fb, x, u.a_row + p.self_row_base);
+            else
+              ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row);
             ptx::tma_load_2d(ptx::smem_u32(sm->b[stage]), &tmap_b, fb, x, u.b_row);
             ptx::tma_load_2d(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, fb, 0, ya);
             ptx::tma_load_2d(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, fb, 0, yb);

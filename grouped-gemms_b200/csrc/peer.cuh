@@ -50,15 +50,6 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerFlags f, int
   __threadfence_system();
 }
 
-// Streaming dispatch: after this stream's copies to a peer, publish them by
-// writing `epoch` into the peer's slot for this rank (system-scope release).
-__global__ void __launch_bounds__(32) peer_signal_kernel(int* slot, int epoch) {
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(slot), "r"(epoch) : "memory");
-  }
-}
-
 // Unpacks this rank's inbox: for each listed 32-row block and each 64-byte
 // column chunk, the 2 KB block (rows in the 64-byte swizzle of the GEMM's
 // staging buffer: row r's chunk j at r * 64 + (j ^ ((r >> 1) & 3)) * 16)

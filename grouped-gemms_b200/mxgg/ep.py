@@ -205,8 +205,9 @@ def replica_groups(placement: ExpertPlacement) -> dict:
 class _Segments:
     offs: Tensor                 # int32 cumulative ends of the segments (rows of the A operand)
     expert: Tensor               # local expert of each segment
-    dst: Tensor                  # rank that owns each segment's rows (its source)
-    dst_row: Tensor              # first row of the segment in its owner's output
+    dst: Tensor                  # output destination of each segment's rows
+    dst_row: Tensor              # first row of the segment there
+    src: Tensor                  # rank each segment's rows come from
 
 
 @dataclass
@@ -214,14 +215,17 @@ class FusedPlan:
     """Routing of one fused expert-parallel call, as seen by one rank.
 
     Receive layout of rank d (its A operand): sources in arrival order d,
-    d-1, d-2, ... (its own rows first, copied locally), each source's rows
-    grouped by local expert.  Rank s sends to s, s+1, s+2, ... in turn, so
-    every receiver gets its sources one after another in that order."""
+    d-1, d-2, ..., each source's rows grouped by local expert.  Its own rows
+    keep their slot but are read in place from the caller's tensor.  Rank s
+    sends to s+1, s+2, ... in turn, so every receiver gets its sources one
+    after another in that order."""
 
     rows_local: int
     rows_recv: int               # all rows this rank multiplies (its own included)
-    copies: List[tuple]          # (dest rank, first row there, first local row, rows), in sending order
-    pack: List[tuple]            # (dest rank, cumulative segment ends (device), first m-tile there)
+    copies: List[tuple]          # (dest rank, first row there, first local row, rows) to peers, in sending order
+    pack: List[tuple]            # (dest rank, cumulative segment ends (device), first m-tile there,
+                                 #  first local row, rows), this rank included
+    self_base: int               # local row of the first row this rank routes to itself
     seg: _Segments               # world * L segments over the receive buffer
     local_seg: _Segments         # the same segments with every row kept here, in receive order
     dst_rows: List[int]          # local rows of every rank (the output buffers' heights)
@@ -279,6 +283,7 @@ class FusedExpertParallel:
         self.src_epoch = 0
         self._side = torch.cuda.Stream()
         self._side_pending = False
+        self._a_self = None
         # every rank's capacities, so a plan that overflows any of them fails on all ranks alike
         caps = [None] * self.world
         dist.all_gather_object(caps, (self.max_recv_rows, self.max_local_rows), group=group)
@@ -339,9 +344,10 @@ class FusedExpertParallel:
         for j in range(world):
             d = (rank + j) % world
             if send[rank][d]:
-                copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
+                if d != rank:
+                    copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
                 cum = torch.tensor(seg_rows(rank, d), dtype=torch.int64).cumsum(0).to(torch.int32)
-                pack.append((d, cum.to(dev), m0[rank][d]))
+                pack.append((d, cum.to(dev), m0[rank][d], start[rank][d], send[rank][d]))
         offs, expert, dsts, first, lfirst = [], [], [], [], []
         total = 0
         for s in order(rank):
@@ -363,10 +369,11 @@ class FusedExpertParallel:
             if pl.dest(rank, e) != rank:
                 blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
             row += C[rank][e]
-        o, x = i32(offs), i32(expert)
+        o, x, sr = i32(offs), i32(expert), i32(dsts)
         return FusedPlan(rows_local=sum(C[rank]), rows_recv=total, copies=copies, pack=pack,
-                         seg=_Segments(o, x, i32(dsts), i32(first)),
-                         local_seg=_Segments(o, x, i32([rank] * len(offs)), i32(lfirst)),
+                         self_base=start[rank][rank] - recv_off[rank][rank],
+                         seg=_Segments(o, x, sr, i32(first), sr),
+                         local_seg=_Segments(o, x, i32([rank] * len(offs)), i32(lfirst), sr),
                          dst_rows=[sum(C[d]) for d in range(world)], tile_m=tile_m, inbox_ok=inbox_ok,
                          remote_blocks=i32(blocks if inbox_ok else []))
 
@@ -398,7 +405,7 @@ class FusedExpertParallel:
         sp = ctypes.c_void_p(cur.cuda_stream)
         stages = (K + 127) // 128
         atom_bytes_per_mtile = (plan.tile_m // 128) * stages * 512
-        for (d, cum, m0), (_, _, src_row, rows) in zip(plan.pack, plan.copies):
+        for (d, cum, m0, src_row, rows) in plan.pack:
             _lib.check(lib.mxgg_pack_a_atoms(ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)),
                                              ctypes.c_void_p(cum.data_ptr()), rows, K, cum.numel(), plan.tile_m,
                                              ctypes.c_void_p(self.atoms.ptrs[d] + m0 * atom_bytes_per_mtile), sp),
@@ -416,12 +423,14 @@ class FusedExpertParallel:
         a_q.record_stream(side)
         a_s.record_stream(side)
         self._side_pending = True
+        self._a_self = (a_q, plan.self_base)     # this rank's own rows, read in place by gemm_received
 
     def received(self, plan: FusedPlan, K: int) -> Tensor:
         """The receive buffer as (rows_recv, K) e4m3 (complete after `finish`)."""
         return self.recv_a.view((plan.rows_recv, K), torch.uint8).view(torch.float8_e4m3fn)
 
-    def _ep_gemm(self, plan, seg, a_q, K, w_q, w_s, out_dtype, outs, rows, inboxes, a_atoms, src_flags, a_s=None):
+    def _ep_gemm(self, plan, seg, a_q, K, w_q, w_s, out_dtype, outs, rows, inboxes, a_atoms, src_flags, a_s=None,
+                 a_self=None):
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
@@ -441,6 +450,8 @@ class FusedExpertParallel:
                                           self.world, self.rank,
                                           ctypes.c_void_p(a_atoms) if a_atoms else None,
                                           ctypes.c_void_p(src_flags) if src_flags else None, self.src_epoch,
+                                          p(seg.src), p(a_self[0]) if a_self else None, a_self[0].shape[0] if a_self else 0,
+                                          self.rank, a_self[1] if a_self else 0,
                                           _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_grouped_mm_ep")
@@ -463,13 +474,13 @@ class FusedExpertParallel:
             rows = (ctypes.c_int64 * self.world)(*[plan.rows_recv if r == self.rank else 0
                                                    for r in range(self.world)])
             self._ep_gemm(plan, plan.local_seg, a, K, w_q, w_s, out_dtype, outs, rows, None,
-                          self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank])
+                          self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank], a_self=self._a_self)
             return
         outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
         rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)
         inboxes = (ctypes.c_void_p * self.world)(*self.inbox.ptrs) if plan.inbox_ok else None
         self._ep_gemm(plan, plan.seg, a, K, w_q, w_s, out_dtype, outs, rows, inboxes,
-                      self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank])
+                      self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank], a_self=self._a_self)
 
     def gemm_local(self, plan: FusedPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s: Tensor,
                    out_dtype: torch.dtype = torch.bfloat16) -> None:

@@ -150,17 +150,24 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                        const int32_t* segment_dst_row, int64_t M, int64_t N, int64_t K, int64_t n_segments,
                        int64_t n_experts, int32_t b_format, void* const* dst_out, const int64_t* dst_rows,
                        void* const* dst_inbox, int32_t n_dst, int32_t local_dst, const void* a_atoms,
-                       const int32_t* src_flags, int32_t src_epoch, int out_dtype, void* workspace,
-                       int64_t workspace_bytes, void* stream);
+                       const int32_t* src_flags, int32_t src_epoch, const int32_t* segment_src,
+                       const void* a_self, int64_t a_self_rows, int32_t self_src, int64_t self_row_base,
+                       int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Streaming dispatch for mxgg_grouped_mm_ep.  a_atoms (or null): the A
  * scales already packed into the GEMM's 128x4 atoms by the senders
  * (mxgg_pack_a_atoms, at least mxgg_ep_atom_bytes(M, K, n_segments) bytes,
  * 256-byte aligned); src_flags (or null): a device int32 array indexed by
  * source rank; the GEMM loads a segment's rows only after
- * src_flags[segment_dst[s]] has reached src_epoch (a bounded wait, status
+ * src_flags[source of s] has reached src_epoch (a bounded wait, status
  * bit 128 on timeout).  Senders publish with mxgg_peer_signal after their
- * copies, so segments start as their rows land instead of after a barrier. */
+ * copies, so segments start as their rows land instead of after a barrier.
+ * segment_src (device int32, or null when every segment's source is its
+ * destination segment_dst): the rank each segment's rows come from.
+ * a_self (or null): an (a_self_rows, K) e4m3 tensor holding the rows of
+ * source self_src, read in place -- segment rows of that source at receive
+ * row r are a_self row r + self_row_base -- so a rank's own rows need no copy
+ * and no wait. */
 int32_t mxgg_query_tile_m(void);
 int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments);
 /* Packs the scales of `rows` rows (a_scale (rows, K/32) row-major) grouped
@@ -170,8 +177,11 @@ int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments);
  * segments start in the receiver's order). */
 int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
                       int64_t n_segments, int32_t tile_m, void* out, void* stream);
-/* Writes `epoch` into `slot` (usually a peer's flag array) with system-scope
- * release, after everything earlier on `stream`. */
+/* Writes `epoch` into `slot` (usually a peer's flag array) once everything
+ * earlier on `stream` is done, as a stream memory operation
+ * (cuStreamWriteValue32, with its memory barrier): no kernel, so no SM is
+ * needed, and a GEMM filling the GPU while it waits for such flags from its
+ * peers cannot hold it back. */
 int mxgg_peer_signal(void* slot, int32_t epoch, void* stream);
 
 /* Copies the listed 32-row blocks (device int32 row-block indices) of an

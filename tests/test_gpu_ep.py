@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, E, impl, align, port, q):
+def _worker(rank, world, E, impl, align, port, q, big=False):
     import datetime
     import torch.distributed as dist
     try:
@@ -39,14 +39,14 @@ def _worker(rank, world, E, impl, align, port, q):
         from mxgg.ep import ExpertPlacement, ep_grouped_mm, plan_dispatch
         mxgg.set_schedule(mxgg._lib.SCHED_TILES, 0)
         dev = torch.device("cuda", rank)
-        N, K = 384, 512
+        N, K = (1024, 1024) if big else (384, 512)
         pl = ExpertPlacement(world, E)
         gw = torch.Generator().manual_seed(7)
         W = torch.randn(E, N, K, generator=gw).to(torch.bfloat16).to(dev)
         fp4 = impl.endswith("fp4")
         w_s, w_q = utils.to_mx(W, elem_dtype=torch.float4_e2m1fn_x2 if fp4 else torch.float8_e4m3fn)
         g = torch.Generator().manual_seed(11 + rank)
-        counts = [int(c) * align for c in torch.randint(0, 9, (E,), generator=g)]
+        counts = [int(c) * align * (16 if big else 1) for c in torch.randint(0, 9, (E,), generator=g)]
         if rank == 1:
             counts[-1] = 0
         rows = sum(counts)
@@ -63,15 +63,19 @@ def _worker(rank, world, E, impl, align, port, q):
                                 out_dtype=torch.float32)
         else:
             from mxgg.ep import FusedExpertParallel
-            cap = 8 * 32 * E                                  # most rows any rank can hold
+            cap = 8 * 32 * E * (16 if big else 1)             # most rows any rank can hold
             fused = FusedExpertParallel(pl, max_recv_rows=world * cap, max_local_rows=cap, max_k=K, max_n=N)
             plan = fused.plan(counts)
-            # twice: the second call reuses the buffers behind the first's barriers
-            got = None
-            for _ in range(2):
-                got = fused.grouped_mm(plan, a_q, a_s, wq_mine, ws_mine,
-                                       out_dtype=torch.float32).clone()
+            # a first call on other rows, then the checked one: stale rows left
+            # in the shared buffers by the first call cannot pass for fresh ones
+            A0 = torch.randn(rows, K, generator=g).to(torch.bfloat16).to(dev)
+            a0_s, a0_q = utils.to_mx(A0)
+            first = fused.grouped_mm(plan, a0_q, a0_s, wq_mine, ws_mine, out_dtype=torch.float32).clone()
+            ref0 = kernels.triton_mxfp8_grouped_mm(a0_q, w_q, a0_s, w_s, offs, out_dtype=torch.float32)
+            got = fused.grouped_mm(plan, a_q, a_s, wq_mine, ws_mine, out_dtype=torch.float32).clone()
             torch.cuda.synchronize()
+            if not torch.equal(first, ref0):
+                got = first          # report the first call's mismatch below
         torch.cuda.synchronize()
         ok = got.shape == ref.shape and torch.equal(got, ref)
         st = mxgg.device_status(clear=True)
@@ -98,6 +102,33 @@ def test_ep_grouped_mm_two_ranks(E, impl, align):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, E, impl, align, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, msg = q.get(timeout=300)
+            results[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert results.get(r) == "ok", results.get(r)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_fused_full_grid():
+    """A GEMM that fills every SM while it streams in peers' rows: the
+    senders' flags must still get through (they are stream memory operations,
+    not kernels that would need a free SM)."""
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, 4, "fused", 32, port, q, True)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}

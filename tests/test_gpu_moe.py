@@ -106,11 +106,14 @@ def _worker(rank, world, fp4, port, q):
         cap = 2 * T + 32 * E
         ep = FusedExpertParallel(pl, max_recv_rows=world * cap, max_local_rows=cap, max_k=d_ff, max_n=d_ff)
         layer = MoELayer(up[mine].cuda(), down[mine].cuda(), E, weights_fp4=fp4, placement=pl, ep=ep)
-        got = None
-        for _ in range(2):
-            got = layer.forward(x, logits)
+        # a first call on other tokens, then the checked one: stale rows in the
+        # shared buffers cannot pass for fresh ones
+        x0 = torch.randn(T, d_model, generator=g).to(torch.bfloat16).cuda()
+        first = layer.forward(x0, logits).clone()
+        single0 = MoELayer(up.cuda(), down.cuda(), E, weights_fp4=fp4).forward(x0, logits)
+        got = layer.forward(x, logits).clone()
         torch.cuda.synchronize()
-        ok = torch.equal(got, single)
+        ok = torch.equal(got, single) and torch.equal(first, single0)
         st = mxgg.device_status(clear=True)
         ep.close()
         dist.barrier()
