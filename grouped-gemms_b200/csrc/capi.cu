@@ -15,6 +15,7 @@
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
 #include "scale_pack.cuh"
+#include "moe.cuh"
 #include "peer.cuh"
 #include "tile_map.cuh"
 
@@ -901,6 +902,23 @@ int mxgg_inbox_unpack(const void* inbox, void* out, const int32_t* row_blocks, i
   inbox_unpack_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(inbox), static_cast<uint8_t*>(out), row_blocks, (int)n_row_blocks,
       (int)(row_bytes / 64), (long long)row_bytes);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_combine_topk(const void* y, int64_t y_rows, const int64_t* pos, const float* weights, int64_t tokens,
+                      int64_t N, int32_t k, void* out, void* stream) {
+  if (tokens < 0 || N < 0 || k < 1 || y_rows < 0) return fail(MXGG_ERR_INVALID, "mxgg_combine_topk: bad sizes");
+  if (tokens == 0 || N == 0) return MXGG_OK;
+  if (N % 8 != 0) return fail(MXGG_ERR_UNSUPPORTED, "mxgg_combine_topk: N %% 8 != 0");
+  if (!y || !pos || !weights || !out || !aligned(y, 16) || !aligned(out, 16))
+    return fail(MXGG_ERR_INVALID, "mxgg_combine_topk: null or unaligned pointer");
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long blocks = std::max(1LL, std::min<long long>((tokens + 7) / 8, (long long)st->num_sms * 16));
+  combine_topk_bf16<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), pos, weights, y_rows, (int)tokens, (int)N, (int)k,
+      static_cast<__nv_bfloat16*>(out));
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
 }

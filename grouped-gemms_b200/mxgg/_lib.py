@@ -49,6 +49,7 @@ SIGNATURES = {
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
     "mxgg_quantize_mx_fp4": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _vp]),
     "mxgg_quantize_mx_gather": (_int, [_vp, _int, _i64, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "mxgg_combine_topk": (_int, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _vp]),
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
     "mxgg_set_tile_config": (_int, [_i32, _i32, _i32]),
     "mxgg_set_schedule": (_int, [_i32, _i32]),

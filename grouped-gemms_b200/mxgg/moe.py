@@ -73,9 +73,18 @@ def quantize_gather(x: Tensor, row_index: Tensor):
 
 
 def combine_top2(y: Tensor, layout: DispatchLayout, weights: Tensor, out_dtype=torch.bfloat16) -> Tensor:
-    """out[t] = sum_k weights[t, k] * y[pair_pos[t, k]] (fp32 sum)."""
-    g = y[layout.pair_pos.reshape(-1)].float().reshape(*layout.pair_pos.shape, y.shape[1])
-    return (g * weights[..., None]).sum(1).to(out_dtype)
+    """out[t] = sum_k weights[t, k] * y[pair_pos[t, k]] (fp32 sum in choice order, one pass)."""
+    if out_dtype != torch.bfloat16 or y.dtype != torch.bfloat16:
+        raise TypeError("combine_top2 takes and returns bf16 rows")
+    y = y.contiguous()
+    T, k = layout.pair_pos.shape
+    N = y.shape[1]
+    out = torch.empty((T, N), dtype=torch.bfloat16, device=y.device)
+    pos = layout.pair_pos.to(torch.int64).contiguous()
+    w = weights.to(torch.float32).contiguous()
+    _lib.check(_lib.load().mxgg_combine_topk(_ptr(y), y.shape[0], _ptr(pos), _ptr(w), T, N, k, _ptr(out),
+                                             _stream(y.device)), "mxgg_combine_topk")
+    return out
 
 
 def _quantize_weights(w: Tensor, fp4: bool):

@@ -246,6 +246,13 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
 int mxgg_quantize_mx_gather(const void* x, int x_dtype, int64_t in_rows, const int32_t* row_index, int64_t n_rows,
                             int64_t cols, void* q, void* scales, void* stream);
 
+/* MoE combine: out[t] = sum_j weights[t*k + j] * y[pos[t*k + j]] (bf16 rows of
+ * length N, fp32 sum in choice order, bf16 out); positions outside [0, y_rows)
+ * contribute nothing.  pos int64, weights fp32, both (tokens, k) on the
+ * device.  No counterpart in the reference. */
+int mxgg_combine_topk(const void* y, int64_t y_rows, const int64_t* pos, const float* weights, int64_t tokens,
+                      int64_t N, int32_t k, void* out, void* stream);
+
 /* MXFP4 quantiser (rows mode): FLOOR scaling with emax 2, e2m1 elements
  * packed two per byte (element 2i in the low nibble) into q (rows, cols/2),
  * scales (rows, cols/32) e8m0.  Values saturate to +-6; NaN becomes +6 (e2m1

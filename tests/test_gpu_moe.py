@@ -60,6 +60,20 @@ def test_quantize_gather_bit_exact():
     assert torch.equal(s, rs) and torch.equal(q.view(torch.uint8), rq.view(torch.uint8))
 
 
+def test_combine_top2_matches_torch():
+    from mxgg.moe import combine_top2, dispatch_layout, route_top2
+    g = torch.Generator().manual_seed(4)
+    T, E, N = 300, 6, 512
+    e, w = route_top2(torch.randn(T, E, generator=g).cuda())
+    lay = dispatch_layout(e, E)
+    y = torch.randn(sum(lay.counts), N, generator=g).to(torch.bfloat16).cuda()
+    got = combine_top2(y, lay, w)
+    ref = (y[lay.pair_pos.reshape(-1)].float().reshape(T, 2, N) * w[..., None]).sum(1)
+    torch.cuda.synchronize()
+    # fp32 sums that may differ by one fused multiply-add rounding, then bf16
+    torch.testing.assert_close(got.float(), ref, rtol=1e-2, atol=1e-2)
+
+
 @pytest.mark.parametrize("fp4,min_sqnr", [(False, 20.0), (True, 10.0)])
 def test_moe_layer_single_gpu(fp4, min_sqnr):
     from mxgg.moe import MoELayer
