@@ -49,3 +49,32 @@ def offsets(E, M, multiple_of=32, seed=0):
 def gpu_status_clear():
     import mxgg
     return mxgg.device_status(clear=True)
+
+
+def run_ranks(worker, world, *args, timeout=300):
+    """Run `worker(rank, world, store, queue, *args)` in `world` spawned
+    processes that rendezvous through a fresh file store (no TCP port to
+    collide with another test's), and return {rank: message}."""
+    import shutil
+    import tempfile
+
+    import torch.multiprocessing as mp
+    d = tempfile.mkdtemp(prefix="mxgg_ranks_")
+    store = os.path.join(d, "store")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=worker, args=(r, world, store, q) + tuple(args)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r, msg = q.get(timeout=timeout)
+            results[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+        shutil.rmtree(d, ignore_errors=True)
+    return results

@@ -5,14 +5,10 @@ A stand-in for the local GEMM multiplies every received row by (1 + its
 expert's global index), read from the segment tables, so the round trip
 checks that rows reach the right expert and come back in their owner's order.
 """
-import os
-import socket
-
 import pytest
 import torch
 import torch.distributed as dist
-import torch.multiprocessing as mp
-
+from helpers import run_ranks
 from mxgg.ep import ExpertPlacement, combine, dispatch, plan_dispatch, replica_allreduce, replica_groups
 
 
@@ -40,17 +36,9 @@ def test_placement(world, E):
             assert got == [world // pl.replicas] * pl.replicas
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank, world, E, port, q):
+def _worker(rank, world, store, q, E):
     try:
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        dist.init_process_group("gloo", rank=rank, world_size=world)
+        dist.init_process_group("gloo", init_method="file://" + store, rank=rank, world_size=world)
         pl = ExpertPlacement(world, E)
         g = torch.Generator().manual_seed(100 + rank)
         counts = [int(c) * 32 for c in torch.randint(0, 4, (E,), generator=g)]
@@ -98,17 +86,6 @@ def _worker(rank, world, E, port, q):
 
 @pytest.mark.parametrize("world,E", [(2, 4), (2, 2), (2, 1), (4, 8), (4, 2)])
 def test_dispatch_combine_gloo(world, E):
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, E, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = {}
-    for _ in range(world):
-        r, msg = q.get(timeout=120)
-        results[r] = msg
-    for p in procs:
-        p.join(timeout=60)
+    results = run_ranks(_worker, world, E, timeout=120)
     for r in range(world):
         assert results.get(r) == "ok", results.get(r)

@@ -9,30 +9,23 @@ single-GPU grouped GEMM of the same rows.  With whole-tile scheduling every
 output element is the same fp32 MMA chain in both, so the check is bit-exact.
 """
 import os
-import socket
 
 import pytest
 import torch
 
+from helpers import run_ranks
+
 pytestmark = pytest.mark.gpu
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank, world, E, impl, align, port, q, big=False):
+def _worker(rank, world, store, q, E, impl, align, big=False):
     import datetime
     import torch.distributed as dist
     try:
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", rank))
+        dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
         import kernels
         import mxgg
         import utils
@@ -96,25 +89,8 @@ def _worker(rank, world, E, impl, align, port, q, big=False):
 def test_ep_grouped_mm_two_ranks(E, impl, align):
     """align 32: peers' output blocks travel through inboxes; align 16: some
     segments start off the 32-row grid and rows are stored in place."""
-    import torch.multiprocessing as mp
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, E, impl, align, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = {}
-    try:
-        for _ in range(world):
-            r, msg = q.get(timeout=300)
-            results[r] = msg
-    finally:
-        for p in procs:
-            p.join(timeout=60)
-            if p.is_alive():
-                p.kill()
-    for r in range(world):
+    results = run_ranks(_worker, 2, E, impl, align)
+    for r in range(2):
         assert results.get(r) == "ok", results.get(r)
 
 
@@ -123,23 +99,6 @@ def test_ep_fused_full_grid():
     """A GEMM that fills every SM while it streams in peers' rows: the
     senders' flags must still get through (they are stream memory operations,
     not kernels that would need a free SM)."""
-    import torch.multiprocessing as mp
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, 4, "fused", 32, port, q, True)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = {}
-    try:
-        for _ in range(world):
-            r, msg = q.get(timeout=300)
-            results[r] = msg
-    finally:
-        for p in procs:
-            p.join(timeout=60)
-            if p.is_alive():
-                p.kill()
-    for r in range(world):
+    results = run_ranks(_worker, 2, 4, "fused", 32, True)
+    for r in range(2):
         assert results.get(r) == "ok", results.get(r)

@@ -8,12 +8,11 @@ bit-exact against to_mx of the gathered rows.
 (whole-tile schedule) for MXFP8 and MXFP4 weights.
 """
 import os
-import socket
 
 import pytest
 import torch
 
-from helpers import O, f32, gpu_status_clear
+from helpers import O, f32, gpu_status_clear, run_ranks
 
 pytestmark = pytest.mark.gpu
 
@@ -90,21 +89,14 @@ def test_moe_layer_single_gpu(fp4, min_sqnr):
     assert sqnr >= min_sqnr, sqnr
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank, world, fp4, port, q):
+def _worker(rank, world, store, q, fp4):
     import datetime
     import torch.distributed as dist
     try:
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", rank))
+        dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
         import mxgg
         from mxgg.ep import ExpertPlacement, FusedExpertParallel
         from mxgg.moe import MoELayer
@@ -142,23 +134,6 @@ def _worker(rank, world, fp4, port, q):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("fp4", [False, True])
 def test_moe_layer_expert_parallel_two_ranks(fp4):
-    import torch.multiprocessing as mp
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, fp4, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = {}
-    try:
-        for _ in range(world):
-            r, msg = q.get(timeout=300)
-            results[r] = msg
-    finally:
-        for p in procs:
-            p.join(timeout=60)
-            if p.is_alive():
-                p.kill()
-    for r in range(world):
+    results = run_ranks(_worker, 2, fp4)
+    for r in range(2):
         assert results.get(r) == "ok", results.get(r)
