@@ -234,6 +234,77 @@ class FusedPlan:
     remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
 
 
+def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int, tile_m: int) -> dict:
+    """The fused path's routing arithmetic for `rank`, from every rank's
+    per-expert row counts C[s][e] (rows sorted by expert on each rank).
+
+    Receiver d's layout: sources in arrival order d, d-1, d-2, ..., each
+    source's rows grouped by d's local experts.  Returns plain lists:
+      copies   (dest, first row there, first local row, rows), to peers, in sending order d+1, d+2, ...
+      pack     (dest, cumulative segment ends, first m-tile there, first local row, rows), this rank included
+      seg      offs / expert / src / dst_row / local_row of this rank's receive segments
+      self_base, rows_recv, rows_local, dst_rows, need_recv, inbox_ok, remote_blocks
+    """
+    world, E = pl.world, pl.n_experts
+    send = [[0] * world for _ in range(world)]
+    start = [[0] * world for _ in range(world)]
+    seen = [[False] * world for _ in range(world)]
+    for s in range(world):
+        row = 0
+        for e in range(E):
+            d = pl.dest(s, e)
+            if not seen[s][d]:
+                start[s][d], seen[s][d] = row, True
+            send[s][d] += C[s][e]
+            row += C[s][e]
+
+    def order(d):                       # sources, in arrival order
+        return [(d - j) % world for j in range(world)]
+
+    def seg_rows(s, d):
+        return [C[s][e] if pl.dest(s, e) == d else 0 for e in pl.experts_of(d)]
+
+    # where each source's rows and atoms start at each receiver
+    recv_off = [[0] * world for _ in range(world)]
+    m0 = [[0] * world for _ in range(world)]
+    for d in range(world):
+        r = m = 0
+        for s in order(d):
+            recv_off[s][d], m0[s][d] = r, m
+            r += send[s][d]
+            m += sum((c + tile_m - 1) // tile_m for c in seg_rows(s, d))
+    copies, pack = [], []
+    for j in range(world):
+        d = (rank + j) % world
+        if send[rank][d]:
+            if d != rank:
+                copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
+            cum, acc = [], 0
+            for c in seg_rows(rank, d):
+                acc += c
+                cum.append(acc)
+            pack.append((d, cum, m0[rank][d], start[rank][d], send[rank][d]))
+    seg = {"offs": [], "expert": [], "src": [], "dst_row": [], "local_row": []}
+    total = 0
+    for s in order(rank):
+        for le, (e, rows) in enumerate(zip(pl.experts_of(rank), seg_rows(s, rank))):
+            seg["local_row"].append(total)
+            total += rows
+            seg["offs"].append(total)
+            seg["expert"].append(le)
+            seg["src"].append(s)
+            seg["dst_row"].append(sum(C[s][:e]))
+    blocks, row = [], 0
+    for e in range(E):
+        if pl.dest(rank, e) != rank:
+            blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
+        row += C[rank][e]
+    return {"copies": copies, "pack": pack, "seg": seg, "self_base": start[rank][rank] - recv_off[rank][rank],
+            "rows_recv": total, "rows_local": sum(C[rank]), "dst_rows": [sum(C[d]) for d in range(world)],
+            "need_recv": [sum(send[s][d] for s in range(world)) for d in range(world)],
+            "inbox_ok": all(c % 32 == 0 for row_ in C for c in row_), "remote_blocks": blocks}
+
+
 class FusedExpertParallel:
     """Expert-parallel forward / dgrad over NVLink peer memory, with the
     dispatch streamed into the GEMM and the combine fused into its epilogue.
@@ -313,69 +384,21 @@ class FusedExpertParallel:
         dist.all_gather_into_tensor(allc, mine, group=self.group)
         C = allc.tolist()                                     # C[s][e], one device sync
         tile_m = int(_lib.load().mxgg_query_tile_m())
-        # rows rank s sends to rank d, and where they start in s's local order
-        send = [[0] * world for _ in range(world)]
-        start = [[0] * world for _ in range(world)]
-        seen = [[False] * world for _ in range(world)]
-        for s in range(world):
-            row = 0
-            for e in range(E):
-                d = pl.dest(s, e)
-                if not seen[s][d]:
-                    start[s][d], seen[s][d] = row, True
-                send[s][d] += C[s][e]
-                row += C[s][e]
-        order = lambda d: [(d - j) % world for j in range(world)]   # noqa: E731  (sources, arrival order)
-
-        def seg_rows(s, d):
-            return [C[s][e] if pl.dest(s, e) == d else 0 for e in pl.experts_of(d)]
-
-        # where each source's rows and atoms start at each receiver
-        recv_off = [[0] * world for _ in range(world)]
-        m0 = [[0] * world for _ in range(world)]
+        lay = fused_layout(C, pl, rank, tile_m)
         for d in range(world):
-            r = m = 0
-            for s in order(d):
-                recv_off[s][d], m0[s][d] = r, m
-                r += send[s][d]
-                m += sum((c + tile_m - 1) // tile_m for c in seg_rows(s, d))
+            if lay["need_recv"][d] > self._caps[d][0] or lay["dst_rows"][d] > self._caps[d][1]:
+                raise ValueError(f"fused EP buffers of rank {d} too small: {lay['need_recv'][d]} received / "
+                                 f"{lay['dst_rows'][d]} local rows for {self._caps[d][0]} / {self._caps[d][1]}")
         i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
-        copies, pack = [], []
-        for j in range(world):
-            d = (rank + j) % world
-            if send[rank][d]:
-                if d != rank:
-                    copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
-                cum = torch.tensor(seg_rows(rank, d), dtype=torch.int64).cumsum(0).to(torch.int32)
-                pack.append((d, cum.to(dev), m0[rank][d], start[rank][d], send[rank][d]))
-        offs, expert, dsts, first, lfirst = [], [], [], [], []
-        total = 0
-        for s in order(rank):
-            for le, (e, rows) in enumerate(zip(pl.experts_of(rank), seg_rows(s, rank))):
-                lfirst.append(total)
-                total += rows
-                offs.append(total)
-                expert.append(le)
-                dsts.append(s)
-                first.append(sum(C[s][:e]))
-        for d in range(world):
-            need_recv = sum(send[s][d] for s in range(world))
-            if need_recv > self._caps[d][0] or sum(C[d]) > self._caps[d][1]:
-                raise ValueError(f"fused EP buffers of rank {d} too small: {need_recv} received / {sum(C[d])} "
-                                 f"local rows for {self._caps[d][0]} / {self._caps[d][1]}")
-        inbox_ok = all(c % 32 == 0 for row in C for c in row)
-        blocks, row = [], 0
-        for e in range(E):
-            if pl.dest(rank, e) != rank:
-                blocks.extend(range(row // 32, (row + C[rank][e]) // 32))
-            row += C[rank][e]
-        o, x, sr = i32(offs), i32(expert), i32(dsts)
-        return FusedPlan(rows_local=sum(C[rank]), rows_recv=total, copies=copies, pack=pack,
-                         self_base=start[rank][rank] - recv_off[rank][rank],
-                         seg=_Segments(o, x, sr, i32(first), sr),
-                         local_seg=_Segments(o, x, i32([rank] * len(offs)), i32(lfirst), sr),
-                         dst_rows=[sum(C[d]) for d in range(world)], tile_m=tile_m, inbox_ok=inbox_ok,
-                         remote_blocks=i32(blocks if inbox_ok else []))
+        pack = [(d, i32(cum), m0, src_row, rows) for (d, cum, m0, src_row, rows) in lay["pack"]]
+        seg = lay["seg"]
+        o, x, sr = i32(seg["offs"]), i32(seg["expert"]), i32(seg["src"])
+        return FusedPlan(rows_local=lay["rows_local"], rows_recv=lay["rows_recv"], copies=lay["copies"], pack=pack,
+                         self_base=lay["self_base"],
+                         seg=_Segments(o, x, sr, i32(seg["dst_row"]), sr),
+                         local_seg=_Segments(o, x, i32([rank] * len(seg["offs"])), i32(seg["local_row"]), sr),
+                         dst_rows=lay["dst_rows"], tile_m=tile_m, inbox_ok=lay["inbox_ok"],
+                         remote_blocks=i32(lay["remote_blocks"] if lay["inbox_ok"] else []))
 
     # ---------------------------------------------------------------- calls
     def barrier(self) -> None:
