@@ -276,7 +276,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
              const int32_t* offs, int64_t M, int64_t N, int64_t K, int64_t E, void* out, int out_dtype,
              void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
              const int32_t* group_expert = nullptr, int64_t n_experts = -1,
-             const char* what = nullptr, const EpRoute* route = nullptr, int b_format = MXGG_FMT_E4M3) {
+             const char* what = nullptr, const EpRoute* route = nullptr, int b_format = MXGG_FMT_E4M3,
+             bool accumulate = false) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (n_experts < 0) n_experts = E;
@@ -290,6 +291,8 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (b_format != MXGG_FMT_E4M3 && b_format != MXGG_FMT_E2M1)
     return fail(MXGG_ERR_INVALID, "%s: unknown B format %d", what, b_format);
   const bool b_fp4 = b_format == MXGG_FMT_E2M1;
+  if (accumulate && (out_dtype != MXGG_DTYPE_F32 || route))
+    return fail(MXGG_ERR_UNSUPPORTED, "%s: accumulating into the output needs an fp32 output on one GPU", what);
   if (b_fp4 && (mode != kFwd || K % 128 != 0 || !aligned(b, 32)))
     return fail(MXGG_ERR_UNSUPPORTED, "%s: e2m1 weights need the forward pass, K %% 128 == 0 and a 32-byte "
                 "aligned B", what);
@@ -325,8 +328,9 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (C == 0) {
     // empty contraction: every product is the zero accumulator (the
     // reference's loops run zero times and store zeros, backward.py:67,
-    // forward.py:207-212)
-    MXGG_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(out_rows * out_cols * out_esize(out_dtype)), stream));
+    // forward.py:207-212); accumulating zeros changes nothing
+    if (!accumulate)
+      MXGG_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(out_rows * out_cols * out_esize(out_dtype)), stream));
     return MXGG_OK;
   }
   if (!a || !b || !a_scale || !b_scale || !offs) return fail(MXGG_ERR_INVALID, "%s: null input pointer", what);
@@ -434,6 +438,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     p.self_src = -1;
   }
   p.group_m = pick_group_m(tc);
+  p.accumulate = accumulate ? 1 : 0;
   p.split_tail = split_tail ? 1 : 0;
   p.split_max = g_split_max;
   p.part_slots = part_slots;
@@ -664,6 +669,14 @@ int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols,
   }
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
+}
+
+int mxgg_wgrad_accumulate(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                          const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, float* out,
+                          void* workspace, int64_t workspace_bytes, void* stream) {
+  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, MXGG_DTYPE_F32,
+                  workspace, workspace_bytes, stream, true, nullptr, -1, "mxgg_wgrad_accumulate", nullptr,
+                  MXGG_FMT_E4M3, true);
 }
 
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales, int mode,

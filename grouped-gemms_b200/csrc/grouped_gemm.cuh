@@ -76,6 +76,7 @@ struct GemmParams {
   int out_cols;              // valid output columns (fwd: N, wgrad: K)
   int stages;                // 128-element contraction stages of the packed scales
   int tma_store;             // 1: output rows are 16-byte aligned for TMA stores
+  int accumulate;            // 1: add the result into `out` (fp32 outputs, single-GPU calls)
   int group_m;               // rasterisation band in row tiles (row tile fastest inside a band)
   int split_tail;            // 1: split the tiles of the last, partial round along the contraction
   int split_max;             // most pieces per split tile (0: about sqrt(stages))
@@ -823,14 +824,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
+            if (p.accumulate)
+              ptx::tma_reduce_add_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
+            else
+              ptx::tma_store_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
             ptx::bulk_commit();
           }
           buf ^= 1;
         } else if (lane < rows_here && grow < p.out_rows) {
           OutT* dst = reinterpret_cast<OutT*>(p.out) + grow * p.out_ld + col0;
           const int ncols = min(kEpiCols, p.out_cols - col0);
-          if (ncols == kEpiCols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+          if (sizeof(OutT) == 4 && p.accumulate) {
+            // read-add-write; every element belongs to exactly one tile
+            float* d = reinterpret_cast<float*>(dst);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (j < ncols) d[j] += __uint_as_float(w[j]);
+          } else if (ncols == kEpiCols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
             uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
             for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);

@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                : "memory");
 }
 
+// element-wise add of a shared tile into global memory (TMA reduction)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
 // contiguous shared -> global bulk copy (no tensor map; both addresses and
 // the size multiples of 16 bytes)
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t src, uint32_t bytes) {

@@ -27,6 +27,7 @@ def triton_mxfp8_wgrad(
     BLOCK_M: int = 64,
     num_warps: int = 8,
     num_stages: int = 2,
+    out: torch.Tensor = None,
 ) -> torch.Tensor:
     """MXFP8 weight gradient: ``grad_W[g] = grad_output[group_g]^T @ input_act[group_g]``.
 
@@ -36,7 +37,14 @@ def triton_mxfp8_wgrad(
         group_end_offsets: ``(E,)`` int32, multiples of 32.
 
     Returns ``(E, N, K)`` of ``out_dtype``; empty groups give zeros.
+
+    ``out`` (not in the reference): an existing fp32 ``(E, N, K)`` gradient
+    buffer to accumulate into (``out += grad_W``, one deterministic add per
+    element); it is returned.
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
+    if out is not None:
+        mxgg.wgrad_accumulate_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
+        return out
     return mxgg.wgrad_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)

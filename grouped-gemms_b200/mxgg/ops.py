@@ -217,6 +217,34 @@ def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype):
     return go_t.new_empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype)
 
 
+@torch.library.custom_op("mxgg::wgrad_accumulate_", mutates_args=("out",))
+def wgrad_accumulate_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
+                        out: Tensor) -> None:
+    """out[g] += the group's weight gradient, in place (fp32 out)."""
+    _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, out, what="mxgg::wgrad_accumulate_")
+    N, M = go_t.shape
+    K = ia_t.shape[0]
+    E = offs.shape[0]
+    if out.dtype != torch.float32 or out.shape != (E, N, K) or not out.is_contiguous():
+        raise ValueError(f"mxgg::wgrad_accumulate_: out must be a contiguous fp32 ({E}, {N}, {K}) tensor")
+    go_t = go_t.contiguous()
+    ia_t = ia_t.contiguous()
+    go_scale = as_u8(go_scale).contiguous()
+    ia_scale = as_u8(ia_scale).contiguous()
+    offs = offs.to(torch.int32).contiguous()
+    lib = _lib.load()
+    ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
+    with torch.cuda.device(go_t.device):
+        _lib.check(lib.mxgg_wgrad_accumulate(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
+                                             N, K, M, E, _ptr(out), _ptr(ws), ws.numel(), _stream(go_t.device)),
+                   "mxgg_wgrad_accumulate")
+
+
+@wgrad_accumulate_op.register_fake
+def _(go_t, go_scale, ia_t, ia_scale, offs, out):
+    return None
+
+
 def build_tile_map(offs: Tensor, M: int, block_m: int) -> Tensor:
     """Routing tables in the reference's _build_expt_data layout (forward.py:340-365)."""
     _require_cuda(offs, what="mxgg.build_tile_map")

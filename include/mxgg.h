@@ -227,6 +227,18 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
                int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * mxgg_wgrad, accumulating: out[g] += GO_t[:, group g] @ X_t[:, group g]^T
+ * into an existing fp32 (E, N, K) gradient buffer (gradient accumulation
+ * across micro-batches without a separate add pass).  Each element is added
+ * once per call (TMA reduce-add), so the result is deterministic.  Workspace
+ * as mxgg_wgrad.  No counterpart in the reference, which always allocates a
+ * fresh output (backward.py:251).
+ */
+int mxgg_wgrad_accumulate(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                          const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, float* out,
+                          void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * MX quantiser, FLOOR scaling, e4m3 elements, 32-element blocks.
  * Bit-exact with the reference's to_mx (utils.py:67-105).
  *   x        (rows, cols) of x_dtype, contiguous.

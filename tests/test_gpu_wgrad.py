@@ -194,3 +194,22 @@ def test_split_tail_deterministic(K_, schedule):
     torch.cuda.synchronize()
     for x in outs[1:]:
         assert torch.equal(x, outs[0])
+
+
+@pytest.mark.parametrize("sched", [_lib.SCHED_TILES, _lib.SCHED_SPLIT_TAIL])
+@pytest.mark.parametrize("N", [384, 360])       # 360: warps cut by the tile edge read-add-write instead of TMA reduce
+def test_wgrad_accumulate_into_fp32(K_, schedule, sched, N):
+    """out += wgrad, one fp32 add per element: bit-exact against the plain
+    fp32 result added in torch (same schedule, so the same products)."""
+    schedule(sched, 64)
+    E, M, K = 3, 4096, 512
+    offs = [1024, 1024, 4096]
+    _, _, go_s, go_q, ia_s, ia_q = _inputs(M, N, K, seed=21)
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    fresh = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out_dtype=torch.float32)
+    base = torch.randn(E, N, K, generator=torch.Generator().manual_seed(3)).cuda()
+    want = base + fresh
+    got = K_.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, o, out=base)
+    torch.cuda.synchronize()
+    assert got is base
+    assert torch.equal(got, want)
