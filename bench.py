@@ -14,8 +14,20 @@
   the device timing) is preceded by an L2 flush (a 512 MiB memset, outside
   the events) and bracketed by CUDA events on the launching stream.
 * TFLOPS = 2*M*N*K / t per (shape, pass) (bench.py:200); ``value`` is the
-  geomean over the 108 points, summed over ranks for N > 1 (each rank runs
-  the full sweep on its own GPU: weak scaling, replicas).
+  geomean over the 108 points, times N for N > 1.
+* N > 1 (one process per GPU): the same sweep, expert parallel.  Every rank
+  holds M tokens (the single-GPU group sizes, rotated by rank so every rank
+  computes M rows: weak scaling).  fwd and dgrad stream their rows to the
+  hosting ranks over NVLink and send the output tiles back from the GEMM's
+  epilogue (``mxgg.ep.FusedExpertParallel``; ``--ep-impl nccl`` for the NCCL
+  all-to-all baseline).  wgrad runs on the hosting rank, plus an all-reduce
+  over replicated experts when E < N.  Times are the max over ranks;
+  ``expert_parallel`` splits them into phases.
+* ``moe_layer``: BASELINE config 5, weak-scaled (8 experts and 16384 tokens
+  per GPU; 64 and 131072 at 8 GPUs): a top-2 MoE layer forward, up
+  5120 -> 8192 and down 8192 -> 5120, with MXFP8 weights and with MXFP4
+  weights.  ``mxfp4_weights`` (1 GPU): the 36 forward shapes with e2m1
+  weights.
 * ``e2e``: the same geomean measured through the public entry points with
   host (pinned) inputs: H2D of the fp8 operands, scales and offsets, the GEMM,
   and D2H of the output, all inside the events.
