@@ -498,6 +498,9 @@ def dist_setup(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # no NVLink multicast objects: a rank that dies while bound to one can
+        # fault its peers' GPUs; plain NVLink transfers are what we time
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
