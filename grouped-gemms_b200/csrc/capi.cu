@@ -268,6 +268,13 @@ struct EpRoute {
   int64_t self_row_base = 0;
 };
 
+// Quantised forward output (see GemmParams::q_data).
+struct QuantOut {
+  void* data = nullptr;     // (M, N) e4m3
+  void* scales = nullptr;   // (M, N / 32) e8m0, row-major
+  bool only = false;        // no high-precision output
+};
+
 // split_ok = 0: the caller's scratch only needs the packed scales and the
 // tail of the schedule is dealt as whole tiles.
 // Forward groups may be segments that share B slices: group g multiplies
@@ -277,7 +284,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
              void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
              const int32_t* group_expert = nullptr, int64_t n_experts = -1,
              const char* what = nullptr, const EpRoute* route = nullptr, int b_format = MXGG_FMT_E4M3,
-             bool accumulate = false) {
+             bool accumulate = false, const QuantOut* quant = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
   if (n_experts < 0) n_experts = E;
@@ -305,6 +312,19 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (C % 32 != 0)
     return fail(MXGG_ERR_INVALID, "%s: contraction length %lld must be a multiple of 32", what, (long long)C);
   const int es_out = out_esize(out_dtype);
+  if (quant) {
+    bool local_rows = true;   // an expert-parallel call may quantise only rows that stay on this GPU
+    if (route)
+      for (int i = 0; i < route->n_dst && i < kMaxDst; ++i)
+        if (i != route->local_dst && route->rows_dst[i] != 0) local_rows = false;
+    if (mode != kFwd || !local_rows || accumulate || es_out != 2 || out_cols % 32 != 0)
+      return fail(MXGG_ERR_UNSUPPORTED, "%s: a quantised output needs the forward pass with every row stored on "
+                  "this GPU, a bf16 or f16 output type and N %% 32 == 0 (N = %lld)", what, (long long)out_cols);
+    if (out_rows > 0 && out_cols > 0 && (!quant->data || !quant->scales || !aligned(quant->data, 16)))
+      return fail(MXGG_ERR_INVALID, "%s: the quantised output needs a 16-byte aligned data buffer and a scale buffer",
+                  what);
+  }
+  const bool out_written = !(quant && quant->only);
   if (route) {
     if (mode != kFwd || route->n_dst < 1 || route->n_dst > kMaxDst || route->local_dst < 0 ||
         route->local_dst >= route->n_dst || !route->group_dst || !route->group_dst_row)
@@ -312,15 +332,18 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                   route->local_dst);
     if (C == 0 || (out_cols * es_out) % 16 != 0)
       return fail(MXGG_ERR_UNSUPPORTED, "%s: expert-parallel outputs need K > 0 and 16-byte output rows", what);
-    for (int i = 0; i < route->n_dst; ++i)
+    for (int i = 0; i < route->n_dst; ++i) {
+      if (i == route->local_dst && !out_written && !route->out_dst[i]) continue;   // quantised rows only
       if (route->rows_dst[i] < 0 || (route->rows_dst[i] > 0 && (!route->out_dst[i] || !aligned(route->out_dst[i], 16))))
         return fail(MXGG_ERR_INVALID, "%s: destination %d needs a 16-byte aligned output", what, i);
+    }
     out = route->out_dst[route->local_dst];
     out_rows = route->rows_dst[route->local_dst];
     if (M == 0 || out_cols == 0) return MXGG_OK;
   } else {
     if (out_rows == 0 || out_cols == 0) return MXGG_OK;
-    if (!out) return fail(MXGG_ERR_INVALID, "%s: null output", what);
+    if (!out && out_written) return fail(MXGG_ERR_INVALID, "%s: null output", what);
+    if (!out_written) out = nullptr;
   }
   const int64_t lim = (int64_t)1 << 31;
   if (rows_a >= lim || rows_b >= lim || out_rows >= lim || C >= lim || out_cols >= lim)
@@ -329,8 +352,13 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     // empty contraction: every product is the zero accumulator (the
     // reference's loops run zero times and store zeros, backward.py:67,
     // forward.py:207-212); accumulating zeros changes nothing
-    if (!accumulate)
+    if (!accumulate && out)
       MXGG_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(out_rows * out_cols * out_esize(out_dtype)), stream));
+    if (quant) {
+      // zero blocks quantise to zero codes with scale 0 (FLT_MIN's exponent - 8 clamps to 0)
+      MXGG_CUDA_TRY(cudaMemsetAsync(quant->data, 0, (size_t)(out_rows * out_cols), stream));
+      MXGG_CUDA_TRY(cudaMemsetAsync(quant->scales, 0, (size_t)(out_rows * (out_cols / 32)), stream));
+    }
     return MXGG_OK;
   }
   if (!a || !b || !a_scale || !b_scale || !offs) return fail(MXGG_ERR_INVALID, "%s: null input pointer", what);
@@ -410,7 +438,12 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.out_rows = out_rows;
   p.out_cols = (int)out_cols;
   const int es = out_esize(out_dtype);
-  p.tma_store = out_rows > 0 && aligned(out, 16) && ((out_cols * es) % 16 == 0);
+  p.tma_store = out != nullptr && out_rows > 0 && aligned(out, 16) && ((out_cols * es) % 16 == 0);
+  if (quant) {
+    p.q_data = static_cast<uint8_t*>(quant->data);
+    p.q_scale = static_cast<uint8_t*>(quant->scales);
+    p.q_only = out_written ? 0 : 1;
+  }
   if (route) {
     p.group_dst = route->group_dst;
     p.group_dst_row = route->group_dst_row;
@@ -480,7 +513,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (route) {
     // one map per destination with rows (the peers' outputs take TMA stores too)
     for (int i = 0; i < route->n_dst; ++i) {
-      if (route->rows_dst[i] <= 0) continue;
+      if (route->rows_dst[i] <= 0 || !route->out_dst[i]) continue;
       if (int rc = make_tmap_2d(&maps.out.m[i], route->out_dst[i], out_tmap_dtype(out_dtype), es,
                                 (uint64_t)route->rows_dst[i], (uint64_t)out_cols, (uint64_t)out_cols, 64 / es, 32,
                                 CU_TENSOR_MAP_SWIZZLE_64B))
@@ -555,6 +588,19 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
                   workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments", nullptr,
                   b_format);
+}
+
+int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                       const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                       int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out, int out_dtype,
+                       void* q_out, void* q_scales, void* workspace, int64_t workspace_bytes, void* stream) {
+  QuantOut q;
+  q.data = q_out;
+  q.scales = q_scales;
+  q.only = out == nullptr;
+  return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, segment_expert, segment_expert ? n_experts : n_segments,
+                  "mxgg_grouped_mm_mx", nullptr, b_format, false, &q);
 }
 
 int mxgg_grouped_mm_noalloc(const void* a, const void* b, const void* a_scale, const void* b_scale,
@@ -749,7 +795,8 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                        void* const* dst_inbox, int32_t n_dst, int32_t local_dst, const void* a_atoms,
                        const int32_t* src_flags, int32_t src_epoch, const int32_t* segment_src,
                        const void* a_self, int64_t a_self_rows, int32_t self_src, int64_t self_row_base,
-                       int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+                       void* q_out, void* q_scales, int out_dtype, void* workspace, int64_t workspace_bytes,
+                       void* stream) {
   if (!segment_expert || !dst_out || !dst_rows)
     return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_ep: null segment or destination table");
   if (n_dst < 1 || n_dst > kMaxDst)
@@ -775,9 +822,15 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
   r.a_self_rows = a_self_rows;
   r.self_src = self_src;
   r.self_row_base = self_row_base;
+  QuantOut q;
+  if (q_out) {
+    q.data = q_out;
+    q.scales = q_scales;
+    q.only = local_dst >= 0 && local_dst < n_dst && dst_out[local_dst] == nullptr;
+  }
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, nullptr, out_dtype,
                   workspace, workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_ep", &r,
-                  b_format);
+                  b_format, false, q_out ? &q : nullptr);
 }
 
 int32_t mxgg_query_tile_m(void) { return pick_tiles(256).tile_m; }

@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include "ptx.cuh"
+#include "quantize.cuh"
 
 namespace mxgg {
 
@@ -77,6 +78,15 @@ struct GemmParams {
   int stages;                // 128-element contraction stages of the packed scales
   int tma_store;             // 1: output rows are 16-byte aligned for TMA stores
   int accumulate;            // 1: add the result into `out` (fp32 outputs, single-GPU calls)
+  // Quantised output (fwd, 2-byte output types, single GPU): every 32-column
+  // block of an output row is also written as MX e4m3 -- q_data, (rows,
+  // out_ld) bytes -- with its e8m0 scale in q_scale, (rows, out_ld / 32)
+  // row-major, quantised from the values rounded to the output type: the
+  // to_mx of the output, without writing and re-reading it.  q_only: the
+  // output itself is not written.
+  uint8_t* q_data;
+  uint8_t* q_scale;
+  int q_only;
   int group_m;               // rasterisation band in row tiles (row tile fastest inside a band)
   int split_tail;            // 1: split the tiles of the last, partial round along the contraction
   int split_max;             // most pieces per split tile (0: about sqrt(stages))
@@ -398,6 +408,42 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// the two 16-bit values of a pack2 word, as floats
+template <typename OutT>
+__device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
+template <>
+__device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+template <>
+__device__ __forceinline__ void unpack2<__half>(uint32_t w, float& a, float& b) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  a = f.x;
+  b = f.y;
+}
+
+// One 32-column block of one output row (16 pack2 words) -> 32 e4m3 bytes at
+// q and the block's e8m0 scale, with the rows-mode quantiser's arithmetic.
+template <typename OutT>
+__device__ __forceinline__ void quantize_block32(const uint32_t (&w)[16], uint8_t* q, uint8_t* scale) {
+  float f[32];
+  uint32_t amax = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) unpack2<OutT>(w[i], f[2 * i], f[2 * i + 1]);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = max(amax, abs_bits(f[i]));
+  const uint32_t sc = floor_scale(amax, 8);
+  const float mult = __uint_as_float((254u - sc) << 23);    // 2^(127 - s)
+  uint2 b[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) b[k] = e4m3x8(*reinterpret_cast<const float(*)[8]>(f + 8 * k), mult, amax);
+  uint4* q4 = reinterpret_cast<uint4*>(q);
+  q4[0] = make_uint4(b[0].x, b[0].y, b[1].x, b[1].y);
+  q4[1] = make_uint4(b[2].x, b[2].y, b[3].x, b[3].y);
+  *scale = (uint8_t)sc;
 }
 
 __device__ __forceinline__ void raise_error(const GemmParams& p, volatile int* abort, uint32_t code) {
@@ -748,6 +794,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = pack2<OutT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          if (p.q_data != nullptr) {
+            // to_mx of this row's 32 output columns (host: out_cols % 32 == 0)
+            if (lane < rows_here && grow < p.out_rows)
+              quantize_block32<OutT>(w, p.q_data + grow * p.out_ld + col0, p.q_scale + grow * (p.out_ld / 32) + col0 / 32);
+            if (p.q_only) return;
+          }
         }
         if (u.dst != p.local_dst && rows_here < 32) {
           // A peer GPU's output, rows cut by the group edge: stage the warp's

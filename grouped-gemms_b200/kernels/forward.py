@@ -67,3 +67,34 @@ def triton_mxfp8_grouped_mm(
                                            experts, out_dtype)
     assert K == K2, f"K mismatch: A={K}, B={K2}"
     return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
+
+
+def mxfp8_grouped_mm_to_mx(
+    input_act: torch.Tensor,
+    weight: torch.Tensor,
+    input_act_scales: torch.Tensor,
+    weight_scales: torch.Tensor,
+    group_end_offsets: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    return_output: bool = False,
+):
+    """``to_mx(triton_mxfp8_grouped_mm(...))`` in one kernel: the next
+    layer's MXFP8 operand written by the GEMM's epilogue.
+
+    Same arguments as ``triton_mxfp8_grouped_mm`` (``out_dtype`` bf16 or
+    f16, ``N % 32 == 0``).  Returns ``(scales (M, N//32) uint8, data (M, N)
+    float8_e4m3fn)`` -- ``to_mx``'s order -- bit for bit what ``to_mx`` gives
+    for the ``out_dtype`` output, which is never written to HBM unless
+    ``return_output`` (then ``(scales, data, output)``).  Rows at or past
+    ``group_end_offsets[-1]`` are left unwritten.  The reference runs the GEMM
+    (kernels/forward.py:461-606) and ``to_mx`` (utils.py:67-105) separately.
+    """
+    if not _mxfp8_available:
+        raise NotImplementedError(_UNAVAILABLE_MSG)
+    M, K = input_act.shape
+    E, N, K2 = weight.shape
+    packed = weight.dtype == torch.float4_e2m1fn_x2
+    assert K == (2 * K2 if packed else K2), f"K mismatch: A={K}, B={2 * K2 if packed else K2}"
+    s, q, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, None,
+                                      out_dtype, return_output)
+    return (s, q, out) if return_output else (s, q)

@@ -9,8 +9,8 @@ torch custom ops built on it.
 
 from . import _lib
 from ._lib import MxggError, device_status, set_tile_config, set_schedule
-from .ops import (build_tile_map, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op, to_mx_op,
-                  wgrad_accumulate_op, wgrad_op)
+from .ops import (build_tile_map, grouped_mm_mx_op, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op,
+                  to_mx_op, wgrad_accumulate_op, wgrad_op)
 
 
 def available() -> bool:
@@ -25,5 +25,5 @@ def available() -> bool:
     return torch.cuda.get_device_capability() == (10, 0)
 
 
-__all__ = ["MxggError", "available", "build_tile_map", "device_status", "grouped_mm_op", "grouped_mm_segments_op", "set_tile_config",
-           "set_schedule", "to_mx_fp4_op", "to_mx_op", "wgrad_accumulate_op", "wgrad_op"]
+__all__ = ["MxggError", "available", "build_tile_map", "device_status", "grouped_mm_mx_op", "grouped_mm_op",
+           "grouped_mm_segments_op", "set_tile_config", "set_schedule", "to_mx_fp4_op", "to_mx_op", "wgrad_accumulate_op", "wgrad_op"]

@@ -31,9 +31,11 @@ SIGNATURES = {
     "mxgg_grouped_mm_segments_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int,
                                         _vp, _i64, _vp]),
+    "mxgg_grouped_mm_mx": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int, _vp,
+                                  _vp, _vp, _i64, _vp]),
     "mxgg_grouped_mm_ep": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                   ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_vp), _i32, _i32, _vp, _vp,
-                                  _i32, _vp, _vp, _i64, _i32, _i64, _int, _vp, _i64, _vp]),
+                                  _i32, _vp, _vp, _i64, _i32, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "mxgg_query_tile_m": (_i32, []),
     "mxgg_ep_atom_bytes": (_i64, [_i64, _i64, _i64]),
     "mxgg_pack_a_atoms": (_int, [_vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp]),

@@ -28,7 +28,7 @@ received counts on the host to size the NCCL transfers.
 
 import math
 from dataclasses import dataclass
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 from torch import Tensor
@@ -453,7 +453,7 @@ class FusedExpertParallel:
         return self.recv_a.view((plan.rows_recv, K), torch.uint8).view(torch.float8_e4m3fn)
 
     def _ep_gemm(self, plan, seg, a_q, K, w_q, w_s, out_dtype, outs, rows, inboxes, a_atoms, src_flags, a_s=None,
-                 a_self=None):
+                 a_self=None, quant=None):
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES, _workspace, as_u8, b_format_of
@@ -475,29 +475,39 @@ class FusedExpertParallel:
                                           ctypes.c_void_p(src_flags) if src_flags else None, self.src_epoch,
                                           p(seg.src), p(a_self[0]) if a_self else None, a_self[0].shape[0] if a_self else 0,
                                           self.rank, a_self[1] if a_self else 0,
+                                          p(quant[0]) if quant else None, p(quant[1]) if quant else None,
                                           _OUT_DTYPES[out_dtype], p(ws), ws.numel(),
                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
                    "mxgg_grouped_mm_ep")
 
     def gemm_received(self, plan: FusedPlan, K: int, w_q: Tensor, w_s: Tensor,
-                      out_dtype: torch.dtype = torch.bfloat16, local_out: Optional[Tensor] = None) -> None:
+                      out_dtype: torch.dtype = torch.bfloat16, local_out: Optional[Tensor] = None,
+                      local_mx: Optional[Tuple[Tensor, Tensor]] = None) -> None:
         """GEMM over the receive buffer as it fills (after `dispatch`).  Output
         rows go to their owners, or, with `local_out` ((rows_recv, N)), stay
-        here in receive order."""
+        here in receive order.  `local_mx` = (data (rows_recv, N) e4m3, scales
+        (rows_recv, N//32) uint8): the rows stay here and are written in MXFP8
+        by the epilogue (to_mx of the out_dtype output, fused); `local_out`
+        may then be None."""
         import ctypes
         L, N, _ = w_q.shape
         if N > self.max_n:
             raise ValueError(f"N={N} exceeds the output buffer's {self.max_n}")
         a = self.recv_a.view((plan.rows_recv, K), torch.uint8)
-        if local_out is not None:
-            if local_out.shape != (plan.rows_recv, N) or not local_out.is_contiguous():
+        if local_out is not None or local_mx is not None:
+            if local_out is not None and (local_out.shape != (plan.rows_recv, N) or not local_out.is_contiguous()):
                 raise ValueError("local_out must be a contiguous (rows_recv, N) tensor")
-            outs = (ctypes.c_void_p * self.world)(*[local_out.data_ptr() if r == self.rank else 0
-                                                    for r in range(self.world)])
+            if local_mx is not None and (local_mx[0].shape != (plan.rows_recv, N) or
+                                         local_mx[1].shape != (plan.rows_recv, N // 32) or
+                                         not (local_mx[0].is_contiguous() and local_mx[1].is_contiguous())):
+                raise ValueError("local_mx must be contiguous (rows_recv, N) data and (rows_recv, N//32) scales")
+            here = local_out.data_ptr() if local_out is not None else 0
+            outs = (ctypes.c_void_p * self.world)(*[here if r == self.rank else 0 for r in range(self.world)])
             rows = (ctypes.c_int64 * self.world)(*[plan.rows_recv if r == self.rank else 0
                                                    for r in range(self.world)])
             self._ep_gemm(plan, plan.local_seg, a, K, w_q, w_s, out_dtype, outs, rows, None,
-                          self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank], a_self=self._a_self)
+                          self.atoms.ptrs[self.rank], self.src_flags.ptrs[self.rank], a_self=self._a_self,
+                          quant=local_mx)
             return
         outs = (ctypes.c_void_p * self.world)(*self.out.ptrs)
         rows = (ctypes.c_int64 * self.world)(*plan.dst_rows)

@@ -1,7 +1,7 @@
 """Mixture-of-experts layer on the mxgg kernels (forward).
 
     logits -> top-2 routing -> quantise-on-dispatch (gather + to_mx, one pass)
-    -> up projection (d_model -> d_ff) per expert -> to_mx
+    -> up projection (d_model -> d_ff) per expert, to_mx fused into its epilogue
     -> down projection (d_ff -> d_model) per expert -> weighted top-2 combine
 
 Expert weights are MXFP8, or MXFP4 (e2m1) with MXFP8 activations.  Each
@@ -23,7 +23,8 @@ from torch import Tensor
 
 from . import _lib
 from .ep import ExpertPlacement, FusedExpertParallel
-from .ops import _IN_DTYPES, _ptr, _stream, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op, to_mx_op
+from .ops import (_IN_DTYPES, _ptr, _stream, grouped_mm_mx_op, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op,
+                  to_mx_op)
 
 PAD = 32
 
@@ -121,8 +122,8 @@ class MoELayer:
         if self.ep is None:
             offs = torch.tensor(layout.counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(x.device)
             seg_e = torch.arange(self.n_experts, dtype=torch.int32, device=x.device)
-            h = grouped_mm_segments_op(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16)
-            h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
+            # the up projection's epilogue writes to_mx of its bf16 output
+            h_s, h_q, _ = grouped_mm_mx_op(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16, False)
             y = grouped_mm_segments_op(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
         else:
             # rows stream into the hosts' receive buffers while the up projection
@@ -130,9 +131,9 @@ class MoELayer:
             ep = self.ep
             plan = ep.plan(layout.counts, self.placement)
             ep.dispatch(plan, a_q, a_s)
-            h = torch.empty((plan.rows_recv, self.d_ff), dtype=torch.bfloat16, device=x.device)
-            ep.gemm_received(plan, self.d_model, self.up_q, self.up_s, torch.bfloat16, local_out=h)
-            h_s, h_q = to_mx_op(h, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
+            h_q = torch.empty((plan.rows_recv, self.d_ff), dtype=torch.float8_e4m3fn, device=x.device)
+            h_s = torch.empty((plan.rows_recv, self.d_ff // 32), dtype=torch.uint8, device=x.device)
+            ep.gemm_received(plan, self.d_model, self.up_q, self.up_s, torch.bfloat16, local_mx=(h_q, h_s))
             ep.gemm_local(plan, h_q, h_s, self.down_q, self.down_s, torch.bfloat16)
             y = ep.finish(plan, self.d_model, torch.bfloat16)
         return combine_top2(y, layout, weights)

@@ -8,7 +8,7 @@ tensors raise.
 """
 
 import ctypes
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 from torch import Tensor
@@ -185,6 +185,54 @@ def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tenso
 @grouped_mm_segments_op.register_fake
 def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
+
+
+@torch.library.custom_op("mxgg::grouped_mm_mx", mutates_args=())
+def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
+                     seg_expert: Optional[Tensor], out_dtype: torch.dtype,
+                     keep_out: bool) -> Tuple[Tensor, Tensor, Tensor]:
+    """The forward (segments as in grouped_mm_segments_op; seg_expert None:
+    segment s uses expert s) with to_mx of its output fused into the
+    epilogue.  Returns (scales (M, N//32) uint8, data (M, N) e4m3, out): out is
+    the (M, N) high-precision output when keep_out, else an empty tensor."""
+    _require_cuda(a, b, a_scale, b_scale, seg_offs, what="mxgg::grouped_mm_mx")
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"mxgg::grouped_mm_mx: out_dtype must be bf16 or f16, got {out_dtype}")
+    M, K = a.shape
+    E, N, _ = b.shape
+    if N % 32 != 0:
+        raise ValueError(f"mxgg::grouped_mm_mx: N={N} must be a multiple of 32")
+    b_format = b_format_of(b)
+    S = seg_offs.shape[0]
+    a = a.contiguous()
+    b = b.contiguous()
+    a_scale = as_u8(a_scale).contiguous()
+    b_scale = as_u8(b_scale).contiguous()
+    seg_offs = seg_offs.to(torch.int32).contiguous()
+    if seg_expert is not None:
+        _require_cuda(seg_expert, what="mxgg::grouped_mm_mx")
+        seg_expert = seg_expert.to(torch.int32).contiguous()
+    elif S != E:
+        raise ValueError(f"mxgg::grouped_mm_mx: {S} segments need a segment -> expert map for {E} experts")
+    out = torch.empty((M, N) if keep_out else (0,), dtype=out_dtype, device=a.device)
+    q = torch.empty((M, N), dtype=torch.float8_e4m3fn, device=a.device)
+    s = torch.empty((M, N // 32), dtype=torch.uint8, device=a.device)
+    lib = _lib.load()
+    ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), a.device)
+    with torch.cuda.device(a.device):
+        _lib.check(lib.mxgg_grouped_mm_mx(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
+                                          _ptr(seg_expert) if seg_expert is not None else None, M, N, K, S, E,
+                                          b_format, _ptr(out) if keep_out else None, _OUT_DTYPES[out_dtype],
+                                          _ptr(q), _ptr(s), _ptr(ws), ws.numel(), _stream(a.device)),
+                   "mxgg_grouped_mm_mx")
+    return s, q, out
+
+
+@grouped_mm_mx_op.register_fake
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out):
+    M, N = a.shape[0], b.shape[1]
+    return (a.new_empty((M, N // 32), dtype=torch.uint8), a.new_empty((M, N), dtype=torch.float8_e4m3fn),
+            a.new_empty((M, N) if keep_out else (0,), dtype=out_dtype))
 
 
 # --------------------------------------------------------------------- wgrad

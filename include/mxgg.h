@@ -126,6 +126,25 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
                              int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Forward with the output's MX quantisation fused into the epilogue: as
+ * mxgg_grouped_mm_segments (segment_expert may be null: segment s uses
+ * expert s, n_experts = n_segments), and every 32-column block of output row
+ * r is also written as e4m3 to q_out (M, N) bytes with its e8m0 scale at
+ * q_scales[r * N / 32 + block] -- bit for bit what to_mx (mxgg_quantize_mx,
+ * rows mode, row-major scales) returns for the bf16 / f16 output, which is
+ * rounded first.  out may be null: only the quantised output is written.
+ * Needs N % 32 == 0, a 16-byte aligned q_out, out_dtype bf16 or f16.  Rows
+ * past segment_end_offsets[n_segments-1] are not written.  The workspace is
+ * mxgg_grouped_mm_segments_workspace_size's.  Replaces the pair
+ * triton_mxfp8_grouped_mm + to_mx of its output (kernels/forward.py:461-606,
+ * utils.py:67-105) that the next layer's forward runs.
+ */
+int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                       const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                       int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out, int out_dtype,
+                       void* q_out, void* q_scales, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Expert-parallel forward with the combine fused into the epilogue: as
  * mxgg_grouped_mm_segments, but segment s's output rows are stored to
  * destination segment_dst[s] from row segment_dst_row[s] on, where
@@ -152,7 +171,8 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                        void* const* dst_inbox, int32_t n_dst, int32_t local_dst, const void* a_atoms,
                        const int32_t* src_flags, int32_t src_epoch, const int32_t* segment_src,
                        const void* a_self, int64_t a_self_rows, int32_t self_src, int64_t self_row_base,
-                       int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+                       void* q_out, void* q_scales, int out_dtype, void* workspace, int64_t workspace_bytes,
+                       void* stream);
 
 /* Streaming dispatch for mxgg_grouped_mm_ep.  a_atoms (or null): the A
  * scales already packed into the GEMM's 128x4 atoms by the senders
@@ -167,7 +187,12 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
  * a_self (or null): an (a_self_rows, K) e4m3 tensor holding the rows of
  * source self_src, read in place -- segment rows of that source at receive
  * row r are a_self row r + self_row_base -- so a rank's own rows need no copy
- * and no wait. */
+ * and no wait.
+ * q_out, q_scales (or null): when every row stays on this GPU (dst_rows is 0
+ * for every destination but local_dst), the local output is also written in
+ * MXFP8 as by mxgg_grouped_mm_mx -- q_out (dst_rows[local_dst], N) e4m3,
+ * q_scales (dst_rows[local_dst], N/32) e8m0 -- and dst_out[local_dst] may
+ * be null (quantised rows only). */
 int32_t mxgg_query_tile_m(void);
 int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments);
 /* Packs the scales of `rows` rows (a_scale (rows, K/32) row-major) grouped

@@ -127,3 +127,24 @@ def test_no_cpu_fallback():
     if not kernels._mxfp8_available:
         with pytest.raises(NotImplementedError):
             kernels.triton_mxfp8_grouped_mm(None, torch.empty(1, 1, 1), None, None, None)
+
+
+def test_grouped_mm_mx_rejects_unsupported_outputs():
+    """The fused quantised output needs N % 32 == 0, a 2-byte output type and
+    an aligned data buffer; all checked before any device work."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(4096)
+    # N = 48: blocks of 32 output columns would straddle rows
+    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 48, 64, 1, 1, 0, None, 0, p, p, p, 1 << 20, None))
+    assert rc == 3 and "N % 32" in msg
+    # fp32 output (dtype code 2)
+    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 2, p, p, p, 1 << 20, None))
+    assert rc == 3 and "bf16 or f16" in msg
+    # misaligned quantised data
+    q = ctypes.c_void_p(4097)
+    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 0, q, p, p, 1 << 20, None))
+    assert rc == 1 and "16-byte aligned" in msg
+    # neither an output nor a quantised buffer
+    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 0, None, None, p, 1 << 20,
+                                          None))
+    assert rc == 1
