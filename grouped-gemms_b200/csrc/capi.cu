@@ -1046,4 +1046,9 @@ const char* mxgg_last_error(void) { return g_last_error.c_str(); }
 
 int32_t mxgg_version(void) { return 1; }
 
+#ifndef MXGG_BUILD_ID
+#define MXGG_BUILD_ID "unversioned"
+#endif
+const char* mxgg_build_id(void) { return MXGG_BUILD_ID; }
+
 }  // extern "C"

@@ -10,6 +10,31 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmxgg.so")
+_DEFAULT_LIB_PATH = LIB_PATH
+_CSRC = os.path.join(os.path.dirname(_HERE), "csrc")
+_HEADER = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "mxgg.h")
+
+
+def source_files():
+    """The files libmxgg.so is compiled from (kernels, C ABI, public header)."""
+    return [os.path.join(_CSRC, f) for f in sorted(os.listdir(_CSRC)) if f.endswith((".cu", ".cuh"))] + [_HEADER]
+
+
+def source_digest():
+    """First 16 hex digits of the sha256 over the library's sources (names
+    and contents), or None where the sources are not present.  The build
+    embeds it (mxgg_build_id), so a library built from other sources is
+    refused instead of being called with argument lists it does not take."""
+    import hashlib
+    if not (os.path.isdir(_CSRC) and os.path.exists(_HEADER)):
+        return None
+    h = hashlib.sha256()
+    for f in source_files():
+        h.update(os.path.basename(f).encode() + b"\0")
+        with open(f, "rb") as fh:
+            h.update(fh.read())
+        h.update(b"\0")
+    return h.hexdigest()[:16]
 
 MXGG_OK = 0
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
@@ -59,6 +84,7 @@ SIGNATURES = {
     "mxgg_device_status": (_int, [ctypes.POINTER(ctypes.c_uint32), _int, _vp]),
     "mxgg_last_error": (ctypes.c_char_p, []),
     "mxgg_version": (_i32, []),
+    "mxgg_build_id": (ctypes.c_char_p, []),
 }
 
 _lib = None
@@ -82,6 +108,14 @@ def load():
                 f"mxgg CUDA library not found at {LIB_PATH}; build it with "
                 "`python grouped-gemms_b200/build.py` (nvcc, sm_100a)")
         lib = ctypes.CDLL(LIB_PATH)
+        if LIB_PATH == _DEFAULT_LIB_PATH:
+            want = source_digest()
+            lib.mxgg_build_id.restype = ctypes.c_char_p
+            got = lib.mxgg_build_id().decode()
+            if want is not None and got != want:
+                raise MxggError(
+                    f"{LIB_PATH} was built from other sources (build id {got}, sources {want}); rebuild it "
+                    "with `python grouped-gemms_b200/build.py`")
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.restype = res

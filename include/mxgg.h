@@ -331,6 +331,10 @@ int mxgg_device_status(uint32_t* status_out, int clear, void* stream);
 
 const char* mxgg_last_error(void);
 int32_t mxgg_version(void);
+/* Digest of the sources this library was built from (build.py embeds it);
+ * the Python loader refuses a library whose digest differs from the sources
+ * beside it. */
+const char* mxgg_build_id(void);
 
 #ifdef __cplusplus
 }

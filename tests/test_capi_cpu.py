@@ -148,3 +148,18 @@ def test_grouped_mm_mx_rejects_unsupported_outputs():
     rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 0, None, None, p, 1 << 20,
                                           None))
     assert rc == 1
+
+
+def test_library_matches_its_sources():
+    """libmxgg.so carries the digest of the sources it was built from; the
+    loader refuses one built from other sources (a stale build would be
+    called with argument lists it does not take)."""
+    lib = _lib.load()
+    assert lib.mxgg_build_id().decode() == _lib.source_digest()
+
+
+def test_loader_refuses_a_stale_library(monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "source_digest", lambda: "0" * 16)
+    with pytest.raises(_lib.MxggError, match="built from other sources"):
+        _lib.load()
