@@ -270,8 +270,10 @@ struct EpRoute {
 
 // Quantised forward output (see GemmParams::q_data).
 struct QuantOut {
-  void* data = nullptr;     // (M, N) e4m3
+  void* data = nullptr;     // (M, N) e4m3 (or null)
   void* scales = nullptr;   // (M, N / 32) e8m0, row-major
+  void* tdata = nullptr;    // (N, M) e4m3: the transpose, quantised along M (or null)
+  void* tscales = nullptr;  // (N, M / 32) e8m0, row-major
   bool only = false;        // no high-precision output
 };
 
@@ -320,9 +322,16 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     if (mode != kFwd || !local_rows || accumulate || es_out != 2 || out_cols % 32 != 0)
       return fail(MXGG_ERR_UNSUPPORTED, "%s: a quantised output needs the forward pass with every row stored on "
                   "this GPU, a bf16 or f16 output type and N %% 32 == 0 (N = %lld)", what, (long long)out_cols);
-    if (out_rows > 0 && out_cols > 0 && (!quant->data || !quant->scales || !aligned(quant->data, 16)))
-      return fail(MXGG_ERR_INVALID, "%s: the quantised output needs a 16-byte aligned data buffer and a scale buffer",
-                  what);
+    if (out_rows > 0 && out_cols > 0) {
+      if (!quant->data && !quant->tdata)
+        return fail(MXGG_ERR_INVALID, "%s: no quantised output buffer", what);
+      if (quant->data && (!quant->scales || !aligned(quant->data, 16)))
+        return fail(MXGG_ERR_INVALID, "%s: the quantised output needs a 16-byte aligned data buffer and a scale "
+                    "buffer", what);
+      if (quant->tdata && (!quant->tscales || !aligned(quant->tdata, 16) || out_rows % 32 != 0))
+        return fail(MXGG_ERR_INVALID, "%s: the transposed quantised output needs M %% 32 == 0 (M = %lld), a "
+                    "16-byte aligned data buffer and a scale buffer", what, (long long)out_rows);
+    }
   }
   const bool out_written = !(quant && quant->only);
   if (route) {
@@ -356,8 +365,14 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
       MXGG_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(out_rows * out_cols * out_esize(out_dtype)), stream));
     if (quant) {
       // zero blocks quantise to zero codes with scale 0 (FLT_MIN's exponent - 8 clamps to 0)
-      MXGG_CUDA_TRY(cudaMemsetAsync(quant->data, 0, (size_t)(out_rows * out_cols), stream));
-      MXGG_CUDA_TRY(cudaMemsetAsync(quant->scales, 0, (size_t)(out_rows * (out_cols / 32)), stream));
+      if (quant->data) {
+        MXGG_CUDA_TRY(cudaMemsetAsync(quant->data, 0, (size_t)(out_rows * out_cols), stream));
+        MXGG_CUDA_TRY(cudaMemsetAsync(quant->scales, 0, (size_t)(out_rows * (out_cols / 32)), stream));
+      }
+      if (quant->tdata) {
+        MXGG_CUDA_TRY(cudaMemsetAsync(quant->tdata, 0, (size_t)(out_rows * out_cols), stream));
+        MXGG_CUDA_TRY(cudaMemsetAsync(quant->tscales, 0, (size_t)((out_rows / 32) * out_cols), stream));
+      }
     }
     return MXGG_OK;
   }
@@ -442,6 +457,9 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   if (quant) {
     p.q_data = static_cast<uint8_t*>(quant->data);
     p.q_scale = static_cast<uint8_t*>(quant->scales);
+    p.qt_data = static_cast<uint8_t*>(quant->tdata);
+    p.qt_scale = static_cast<uint8_t*>(quant->tscales);
+    p.qt_rows = out_rows;
     p.q_only = out_written ? 0 : 1;
   }
   if (route) {
@@ -593,10 +611,13 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
 int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const void* b_scale,
                        const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
                        int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out, int out_dtype,
-                       void* q_out, void* q_scales, void* workspace, int64_t workspace_bytes, void* stream) {
+                       void* q_out, void* q_scales, void* qt_out, void* qt_scales, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
   QuantOut q;
   q.data = q_out;
   q.scales = q_scales;
+  q.tdata = qt_out;
+  q.tscales = qt_scales;
   q.only = out == nullptr;
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
                   workspace_bytes, stream, true, segment_expert, segment_expert ? n_experts : n_segments,

@@ -59,6 +59,7 @@ enum : uint32_t {
   kErrDrain = 32u,
   // 64 is the cross-GPU barrier's (peer.cuh)
   kErrSourceWait = 128u,     // expert parallel: a source's rows never arrived
+  kErrQtRows = 256u,         // transposed quantised output: a group not on the 32-row grid
 };
 
 struct GemmParams {
@@ -87,6 +88,13 @@ struct GemmParams {
   uint8_t* q_data;
   uint8_t* q_scale;
   int q_only;
+  // Transposed quantised output (same conditions; groups on the 32-row grid):
+  // qt_data (out_ld, qt_rows) e4m3 holds the output's transpose quantised
+  // along its rows -- to_mx(out.t()) -- with scales qt_scale (out_ld,
+  // qt_rows / 32): the operand layout of the next weight-gradient pass.
+  uint8_t* qt_data;
+  uint8_t* qt_scale;
+  long long qt_rows;
   int group_m;               // rasterisation band in row tiles (row tile fastest inside a band)
   int split_tail;            // 1: split the tiles of the last, partial round along the contraction
   int split_max;             // most pieces per split tile (0: about sqrt(stages))
@@ -794,12 +802,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = pack2<OutT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          if (p.qt_data != nullptr) {
+            // to_mx of the transposed 32 x 32 block: stage the warp's rows
+            // (64-byte swizzle, as for a TMA store), then lane j reads column
+            // j down the 32 rows and quantises it as one block of row col0 + j
+            // of the transpose.  Needs the warp's rows on the 32-row grid.
+            const long long row0 = u.out_row + my_row0;
+            if (rows_here == 32 && (row0 & 31) == 0 && row0 + 32 <= p.qt_rows) {
+              uint8_t* stg = sm->epi[q][buf];
+              if (lane == 0) ptx::bulk_wait_read<1>();   // a TMA store may still read this buffer
+              __syncwarp();
+              const uint32_t stg_u = ptx::smem_u32(stg);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t chunk = (uint32_t)(j ^ ((lane >> 1) & 3));
+                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(stg_u + lane * 64 + chunk * 16),
+                             "r"(w[4 * j]), "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                             : "memory");
+              }
+              __syncwarp();
+              uint32_t t[16];   // column `lane`, rows 2i and 2i + 1 in word i
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                uint16_t lo, hi;
+                const uint32_t off = (uint32_t)((lane >> 3) * 16 + (lane & 7) * 2);
+                const int r0 = 2 * i, r1 = 2 * i + 1;
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(lo)
+                             : "r"(stg_u + r0 * 64 + ((((uint32_t)lane >> 3) ^ ((r0 >> 1) & 3)) * 16) + (off & 15))
+                             : "memory");
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hi)
+                             : "r"(stg_u + r1 * 64 + ((((uint32_t)lane >> 3) ^ ((r1 >> 1) & 3)) * 16) + (off & 15))
+                             : "memory");
+                t[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+              }
+              __syncwarp();   // every lane has read the block before the buffer is written again
+              const long long trow = (long long)col0 + lane;
+              quantize_block32<OutT>(t, p.qt_data + trow * p.qt_rows + row0, p.qt_scale + trow * (p.qt_rows / 32) + row0 / 32);
+            } else if (rows_here > 0) {
+              if (lane == 0) atomicOr(p.status, kErrQtRows);
+            }
+          }
           if (p.q_data != nullptr) {
             // to_mx of this row's 32 output columns (host: out_cols % 32 == 0)
             if (lane < rows_here && grow < p.out_rows)
               quantize_block32<OutT>(w, p.q_data + grow * p.out_ld + col0, p.q_scale + grow * (p.out_ld / 32) + col0 / 32);
-            if (p.q_only) return;
           }
+          if (p.q_only) return;
         }
         if (u.dst != p.local_dst && rows_here < 32) {
           // A peer GPU's output, rows cut by the group edge: stage the warp's

@@ -77,6 +77,7 @@ def mxfp8_grouped_mm_to_mx(
     group_end_offsets: torch.Tensor,
     out_dtype: torch.dtype = torch.bfloat16,
     return_output: bool = False,
+    dim1: bool = False,
 ):
     """``to_mx(triton_mxfp8_grouped_mm(...))`` in one kernel: the next
     layer's MXFP8 operand written by the GEMM's epilogue.
@@ -85,7 +86,12 @@ def mxfp8_grouped_mm_to_mx(
     f16, ``N % 32 == 0``).  Returns ``(scales (M, N//32) uint8, data (M, N)
     float8_e4m3fn)`` -- ``to_mx``'s order -- bit for bit what ``to_mx`` gives
     for the ``out_dtype`` output, which is never written to HBM unless
-    ``return_output`` (then ``(scales, data, output)``).  Rows at or past
+    ``return_output`` (then ``(scales, data, output)``).  With ``dim1`` the
+    epilogue also writes ``utils.to_mx_dim1`` of the output -- the transpose
+    quantised along tokens, ``(scales_t (N, M//32), data_t (N, M))``, the
+    operand layout of the next ``triton_mxfp8_wgrad`` -- appended after
+    ``data``; it needs ``M % 32 == 0`` and group ends on multiples of 32 (a
+    group off that grid sets device status bit 256).  Rows at or past
     ``group_end_offsets[-1]`` are left unwritten.  The reference runs the GEMM
     (kernels/forward.py:461-606) and ``to_mx`` (utils.py:67-105) separately.
     """
@@ -95,6 +101,7 @@ def mxfp8_grouped_mm_to_mx(
     E, N, K2 = weight.shape
     packed = weight.dtype == torch.float4_e2m1fn_x2
     assert K == (2 * K2 if packed else K2), f"K mismatch: A={K}, B={2 * K2 if packed else K2}"
-    s, q, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, None,
-                                      out_dtype, return_output)
-    return (s, q, out) if return_output else (s, q)
+    s, q, st, qt, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets,
+                                              None, out_dtype, return_output, True, dim1)
+    res = (s, q, st, qt) if dim1 else (s, q)
+    return res + (out,) if return_output else res

@@ -57,7 +57,7 @@ SIGNATURES = {
     "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int,
                                         _vp, _i64, _vp]),
     "mxgg_grouped_mm_mx": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int, _vp,
-                                  _vp, _vp, _i64, _vp]),
+                                  _vp, _vp, _vp, _vp, _i64, _vp]),
     "mxgg_grouped_mm_ep": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                   ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_vp), _i32, _i32, _vp, _vp,
                                   _i32, _vp, _vp, _i64, _i32, _i64, _vp, _vp, _int, _vp, _i64, _vp]),

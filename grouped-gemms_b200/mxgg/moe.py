@@ -123,7 +123,7 @@ class MoELayer:
             offs = torch.tensor(layout.counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(x.device)
             seg_e = torch.arange(self.n_experts, dtype=torch.int32, device=x.device)
             # the up projection's epilogue writes to_mx of its bf16 output
-            h_s, h_q, _ = grouped_mm_mx_op(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16, False)
+            h_s, h_q, _, _, _ = grouped_mm_mx_op(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16, False)
             y = grouped_mm_segments_op(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
         else:
             # rows stream into the hosts' receive buffers while the up projection

@@ -189,12 +189,16 @@ def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype):
 
 @torch.library.custom_op("mxgg::grouped_mm_mx", mutates_args=())
 def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
-                     seg_expert: Optional[Tensor], out_dtype: torch.dtype,
-                     keep_out: bool) -> Tuple[Tensor, Tensor, Tensor]:
+                     seg_expert: Optional[Tensor], out_dtype: torch.dtype, keep_out: bool, rows: bool = True,
+                     cols: bool = False) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The forward (segments as in grouped_mm_segments_op; seg_expert None:
-    segment s uses expert s) with to_mx of its output fused into the
-    epilogue.  Returns (scales (M, N//32) uint8, data (M, N) e4m3, out): out is
-    the (M, N) high-precision output when keep_out, else an empty tensor."""
+    segment s uses expert s) with MX quantisation of its output fused into
+    the epilogue.  Returns (scales, data, scales_t, data_t, out):
+      rows: to_mx(out)      -- scales (M, N//32) uint8, data (M, N) e4m3;
+      cols: to_mx(out.t())  -- scales_t (N, M//32), data_t (N, M) (M % 32 == 0,
+            segments on the 32-row grid);
+      keep_out: out (M, N) of out_dtype.
+    Parts not asked for come back as empty tensors."""
     _require_cuda(a, b, a_scale, b_scale, seg_offs, what="mxgg::grouped_mm_mx")
     if out_dtype not in (torch.bfloat16, torch.float16):
         raise TypeError(f"mxgg::grouped_mm_mx: out_dtype must be bf16 or f16, got {out_dtype}")
@@ -202,6 +206,10 @@ def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg
     E, N, _ = b.shape
     if N % 32 != 0:
         raise ValueError(f"mxgg::grouped_mm_mx: N={N} must be a multiple of 32")
+    if not (rows or cols):
+        raise ValueError("mxgg::grouped_mm_mx: ask for rows and/or cols")
+    if cols and M % 32 != 0:
+        raise ValueError(f"mxgg::grouped_mm_mx: the transposed output needs M % 32 == 0 (M={M})")
     b_format = b_format_of(b)
     S = seg_offs.shape[0]
     a = a.contiguous()
@@ -214,25 +222,32 @@ def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg
         seg_expert = seg_expert.to(torch.int32).contiguous()
     elif S != E:
         raise ValueError(f"mxgg::grouped_mm_mx: {S} segments need a segment -> expert map for {E} experts")
-    out = torch.empty((M, N) if keep_out else (0,), dtype=out_dtype, device=a.device)
-    q = torch.empty((M, N), dtype=torch.float8_e4m3fn, device=a.device)
-    s = torch.empty((M, N // 32), dtype=torch.uint8, device=a.device)
+    dev = a.device
+    out = torch.empty((M, N) if keep_out else (0,), dtype=out_dtype, device=dev)
+    q = torch.empty((M, N) if rows else (0,), dtype=torch.float8_e4m3fn, device=dev)
+    s = torch.empty((M, N // 32) if rows else (0,), dtype=torch.uint8, device=dev)
+    qt = torch.empty((N, M) if cols else (0,), dtype=torch.float8_e4m3fn, device=dev)
+    st = torch.empty((N, M // 32) if cols else (0,), dtype=torch.uint8, device=dev)
+    opt = lambda t, on: _ptr(t) if on else None  # noqa: E731
     lib = _lib.load()
-    ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), a.device)
-    with torch.cuda.device(a.device):
+    ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), dev)
+    with torch.cuda.device(dev):
         _lib.check(lib.mxgg_grouped_mm_mx(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
                                           _ptr(seg_expert) if seg_expert is not None else None, M, N, K, S, E,
-                                          b_format, _ptr(out) if keep_out else None, _OUT_DTYPES[out_dtype],
-                                          _ptr(q), _ptr(s), _ptr(ws), ws.numel(), _stream(a.device)),
+                                          b_format, opt(out, keep_out), _OUT_DTYPES[out_dtype], opt(q, rows),
+                                          opt(s, rows), opt(qt, cols), opt(st, cols), _ptr(ws), ws.numel(),
+                                          _stream(dev)),
                    "mxgg_grouped_mm_mx")
-    return s, q, out
+    return s, q, st, qt, out
 
 
 @grouped_mm_mx_op.register_fake
-def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out):
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False):
     M, N = a.shape[0], b.shape[1]
-    return (a.new_empty((M, N // 32), dtype=torch.uint8), a.new_empty((M, N), dtype=torch.float8_e4m3fn),
-            a.new_empty((M, N) if keep_out else (0,), dtype=out_dtype))
+    e = lambda shape, on, dt: a.new_empty(shape if on else (0,), dtype=dt)  # noqa: E731
+    return (e((M, N // 32), rows, torch.uint8), e((M, N), rows, torch.float8_e4m3fn),
+            e((N, M // 32), cols, torch.uint8), e((N, M), cols, torch.float8_e4m3fn),
+            e((M, N), keep_out, out_dtype))
 
 
 # --------------------------------------------------------------------- wgrad

@@ -132,9 +132,16 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
  * r is also written as e4m3 to q_out (M, N) bytes with its e8m0 scale at
  * q_scales[r * N / 32 + block] -- bit for bit what to_mx (mxgg_quantize_mx,
  * rows mode, row-major scales) returns for the bf16 / f16 output, which is
- * rounded first.  out may be null: only the quantised output is written.
- * Needs N % 32 == 0, a 16-byte aligned q_out, out_dtype bf16 or f16.  Rows
- * past segment_end_offsets[n_segments-1] are not written.  The workspace is
+ * rounded first.  out may be null: only the quantised outputs are written.
+ * qt_out, qt_scales (or null): the output's transpose quantised along M --
+ * to_mx(out.t()), what mxgg_quantize_mx's cols mode returns, the (N, M)
+ * operand layout of the next weight-gradient pass -- (N, M) e4m3 and
+ * (N, M/32) e8m0; needs M % 32 == 0 and every segment starting on the 32-row
+ * grid (a segment off the grid sets device status bit 256 and its blocks are
+ * not written).  q_out may be null when qt_out is not.
+ * Needs N % 32 == 0, 16-byte aligned q_out / qt_out, out_dtype bf16 or f16.
+ * Rows past segment_end_offsets[n_segments-1] (columns, for qt_out) are not
+ * written.  The workspace is
  * mxgg_grouped_mm_segments_workspace_size's.  Replaces the pair
  * triton_mxfp8_grouped_mm + to_mx of its output (kernels/forward.py:461-606,
  * utils.py:67-105) that the next layer's forward runs.
@@ -142,7 +149,8 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
 int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const void* b_scale,
                        const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
                        int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out, int out_dtype,
-                       void* q_out, void* q_scales, void* workspace, int64_t workspace_bytes, void* stream);
+                       void* q_out, void* q_scales, void* qt_out, void* qt_scales, void* workspace,
+                       int64_t workspace_bytes, void* stream);
 
 /*
  * Expert-parallel forward with the combine fused into the epilogue: as
@@ -326,7 +334,8 @@ enum { MXGG_SCHED_DEFAULT = 0, MXGG_SCHED_TILES = 1, MXGG_SCHED_SPLIT_TAIL = 2 }
 int mxgg_set_schedule(int32_t schedule, int32_t split_max);
 
 /* Error bits raised by device-side bounded waits since the last clear
- * (0 = none).  Synchronises `stream`.  clear != 0 resets the word. */
+ * (0 = none; bit 256: a transposed quantised output met a group off the
+ * 32-row grid).  Synchronises `stream`.  clear != 0 resets the word. */
 int mxgg_device_status(uint32_t* status_out, int clear, void* stream);
 
 const char* mxgg_last_error(void);

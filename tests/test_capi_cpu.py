@@ -130,24 +130,31 @@ def test_no_cpu_fallback():
 
 
 def test_grouped_mm_mx_rejects_unsupported_outputs():
-    """The fused quantised output needs N % 32 == 0, a 2-byte output type and
-    an aligned data buffer; all checked before any device work."""
+    """The fused quantised outputs need N % 32 == 0, a 2-byte output type,
+    aligned data buffers and, for the transposed one, M % 32 == 0; all
+    checked before any device work."""
     lib = _lib.load()
     p = ctypes.c_void_p(4096)
+
+    def call(M, N, dtype, q, s, qt, st):
+        return _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, M, N, 64, 1, 1, 0, None, dtype, q, s, qt, st, p,
+                                           1 << 20, None))
+
     # N = 48: blocks of 32 output columns would straddle rows
-    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 48, 64, 1, 1, 0, None, 0, p, p, p, 1 << 20, None))
+    rc, msg = call(64, 48, 0, p, p, None, None)
     assert rc == 3 and "N % 32" in msg
     # fp32 output (dtype code 2)
-    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 2, p, p, p, 1 << 20, None))
+    rc, msg = call(64, 64, 2, p, p, None, None)
     assert rc == 3 and "bf16 or f16" in msg
     # misaligned quantised data
-    q = ctypes.c_void_p(4097)
-    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 0, q, p, p, 1 << 20, None))
+    rc, msg = call(64, 64, 0, ctypes.c_void_p(4097), p, None, None)
     assert rc == 1 and "16-byte aligned" in msg
     # neither an output nor a quantised buffer
-    rc, msg = _err(lib.mxgg_grouped_mm_mx(p, p, p, p, p, None, 64, 64, 64, 1, 1, 0, None, 0, None, None, p, 1 << 20,
-                                          None))
-    assert rc == 1
+    rc, msg = call(64, 64, 0, None, None, None, None)
+    assert rc == 1 and "no quantised output" in msg
+    # transposed output with M = 48
+    rc, msg = call(48, 64, 0, None, None, p, p)
+    assert rc == 1 and "M % 32" in msg
 
 
 def test_library_matches_its_sources():

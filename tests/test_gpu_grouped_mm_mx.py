@@ -1,11 +1,12 @@
 """Forward GEMM with to_mx of its output fused into the epilogue, on the GPU.
 
-The fused output must be bit for bit what ``to_mx`` gives for the GEMM's own
+The fused outputs must be bit for bit what ``to_mx`` (rows) and
+``to_mx_dim1`` (the transpose, quantised along tokens) give for the GEMM's own
 bf16 / f16 output (integer and byte work: exact).  Checked twice: against the
-separate GPU calls (``triton_mxfp8_grouped_mm`` then ``utils.to_mx``) and
-against the oracle's FLOOR-mode ``to_mx`` (pinned to the reference's
-utils.py:67-105) applied to that output on the CPU.  Rows at or past the last
-group end are not written and are not compared.
+separate GPU calls (``triton_mxfp8_grouped_mm`` then ``utils.to_mx`` /
+``utils.to_mx_dim1``) and against the oracle's FLOOR-mode ``to_mx`` (pinned to
+the reference's utils.py:67-105) applied to that output on the CPU.  Rows at
+or past the last group end are not written and are not compared.
 """
 import numpy as np
 import pytest
@@ -62,6 +63,17 @@ def _check(args, out_dtype=torch.bfloat16):
     os_, oq = O.to_mx(out.float().cpu().numpy())
     assert np.array_equal(u8(s[:rows]), os_)
     assert np.array_equal(u8(q[:rows]), oq)
+    if M % 32 == 0 and all(int(o) % 32 == 0 for o in offs.tolist()):
+        s3, q3, st, qt = kernels.mxfp8_grouped_mm_to_mx(*args, out_dtype=out_dtype, dim1=True)
+        torch.cuda.synchronize()
+        assert st.shape == (N, M // 32) and qt.shape == (N, M)
+        assert np.array_equal(u8(s3[:rows]), u8(rs)) and np.array_equal(u8(q3[:rows]), u8(rq))
+        ts, tq = utils.to_mx_dim1(out)
+        assert np.array_equal(u8(st[:, :rows // 32]), u8(ts))
+        assert np.array_equal(u8(qt[:, :rows]), u8(tq))
+        ots, otq = O.to_mx(np.ascontiguousarray(out.float().cpu().numpy().T))
+        assert np.array_equal(u8(st[:, :rows // 32]), ots)
+        assert np.array_equal(u8(qt[:, :rows]), otq)
 
 
 @pytest.mark.parametrize("E,M,N,K", [(4, 1024, 256, 512), (1, 640, 2048, 256), (8, 2080, 512, 1024),
@@ -123,12 +135,34 @@ def test_fused_to_mx_segments_sharing_experts():
     import mxgg
     import utils
     a_q, b_q, a_s, b_s, _ = _make(3, 640, 512, 256, [640], seed=7)
-    seg_offs = torch.tensor([64, 200, 200, 352, 640], dtype=torch.int32, device="cuda")
+    seg_offs = torch.tensor([64, 192, 192, 352, 640], dtype=torch.int32, device="cuda")   # on the 32-row grid
     seg_e = torch.tensor([0, 2, 1, 0, 1], dtype=torch.int32, device="cuda")
-    mxgg.grouped_mm_mx_op(_roll(a_q, 3), b_q, a_s, b_s, seg_offs, seg_e, torch.bfloat16, True)
+    mxgg.grouped_mm_mx_op(_roll(a_q, 3), b_q, a_s, b_s, seg_offs, seg_e, torch.bfloat16, True, True, True)
     out = mxgg.grouped_mm_segments_op(a_q, b_q, a_s, b_s, seg_offs, seg_e, torch.bfloat16)
-    s, q, out2 = mxgg.grouped_mm_mx_op(a_q, b_q, a_s, b_s, seg_offs, seg_e, torch.bfloat16, True)
+    s, q, st, qt, out2 = mxgg.grouped_mm_mx_op(a_q, b_q, a_s, b_s, seg_offs, seg_e, torch.bfloat16, True, True, True)
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+    rs, rq = utils.to_mx(out)
+    assert np.array_equal(u8(s), u8(rs)) and np.array_equal(u8(q), u8(rq))
+    ts, tq = utils.to_mx_dim1(out)
+    assert np.array_equal(u8(st), u8(ts)) and np.array_equal(u8(qt), u8(tq))
+
+
+def test_fused_dim1_only_and_off_grid_groups():
+    """dim1 without the row-wise output; a group starting off the 32-row grid
+    raises device status bit 256 (its blocks are skipped), the row-wise
+    output stays exact."""
+    import mxgg
+    import utils
+    a_q, b_q, a_s, b_s, offs = _make(2, 256, 256, 256, [128, 256], seed=8)
+    _, _, st, qt, out = mxgg.grouped_mm_mx_op(a_q, b_q, a_s, b_s, offs, None, torch.bfloat16, True, False, True)
+    torch.cuda.synchronize()
+    ts, tq = utils.to_mx_dim1(out)
+    assert np.array_equal(u8(st), u8(ts)) and np.array_equal(u8(qt), u8(tq))
+    assert mxgg.device_status(clear=True) == 0
+    offs = torch.tensor([48, 256], dtype=torch.int32, device="cuda")
+    s, q, _, _, out = mxgg.grouped_mm_mx_op(a_q, b_q, a_s, b_s, offs, None, torch.bfloat16, True, True, True)
+    torch.cuda.synchronize()
+    assert mxgg.device_status(clear=True) & 256
     rs, rq = utils.to_mx(out)
     assert np.array_equal(u8(s), u8(rs)) and np.array_equal(u8(q), u8(rq))
