@@ -5,12 +5,14 @@ Same signature and argument meaning as the reference
 input_act[group_g]`` with both inputs dim1-quantised (scales along tokens).
 The reference stores bf16 whatever ``out_dtype`` says (backward.py:103,214);
 this implementation honours ``out_dtype`` (bf16, fp16 or fp32).  The Triton
-tile keywords are accepted and ignored.
+tile keywords are accepted and ignored; a table measured by ``mxgg.tune``
+supplies B200 tiles per call shape when one is installed.
 """
 
 import torch
 
 import mxgg
+from mxgg import tune as _tune
 
 from ._common import _UNAVAILABLE_MSG, _mxfp8_available
 
@@ -44,7 +46,9 @@ def triton_mxfp8_wgrad(
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
-    if out is not None:
-        mxgg.wgrad_accumulate_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
-        return out
-    return mxgg.wgrad_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)
+    cfg = _tune.pick("wgrad", group_end_offsets.shape[0], go_t.shape[0], ia_t.shape[0])
+    with _tune.applied(cfg):
+        if out is not None:
+            mxgg.wgrad_accumulate_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
+            return out
+        return mxgg.wgrad_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)

@@ -9,12 +9,15 @@ the same call with ``input_act = grad_output`` quantised along N and
 The Triton/AMD tuning keywords (BLOCK_*, GROUP_M, XCD_SWIZZLE, num_warps,
 num_stages, matrix_instr_nonkdim, waves_per_eu, kpack, cache hints) are
 accepted for drop-in compatibility (the reference's tuner passes them,
-tune_worker.py:87-91) and ignored: the sm_100a kernel picks its own tiles.
+tune_worker.py:87-91) and ignored: the sm_100a kernel picks its own tiles,
+or takes them from a table ``mxgg.tune`` measured on B200 (the counterpart
+of the reference's ``_BEST_CFGS`` / ``_pick_config``, forward.py:399-459).
 """
 
 import torch
 
 import mxgg
+from mxgg import tune as _tune
 
 from ._common import _UNAVAILABLE_MSG, _mxfp8_available
 
@@ -63,10 +66,13 @@ def triton_mxfp8_grouped_mm(
     if weight.dtype == torch.float4_e2m1fn_x2:
         assert K == 2 * K2, f"K mismatch: A={K}, B={2 * K2} (e2m1 packed)"
         experts = torch.arange(E, dtype=torch.int32, device=weight.device)
-        return mxgg.grouped_mm_segments_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets,
-                                           experts, out_dtype)
+        with _tune.applied(_tune.pick("fwd", E, N, K)):
+            return mxgg.grouped_mm_segments_op(input_act, weight, input_act_scales, weight_scales,
+                                               group_end_offsets, experts, out_dtype)
     assert K == K2, f"K mismatch: A={K}, B={K2}"
-    return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
+    # a tuned config for this call shape (mxgg.tune), else the library's choice
+    with _tune.applied(_tune.pick("fwd", E, N, K)):
+        return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
 
 
 def mxfp8_grouped_mm_to_mx(
@@ -101,7 +107,8 @@ def mxfp8_grouped_mm_to_mx(
     E, N, K2 = weight.shape
     packed = weight.dtype == torch.float4_e2m1fn_x2
     assert K == (2 * K2 if packed else K2), f"K mismatch: A={K}, B={2 * K2 if packed else K2}"
-    s, q, st, qt, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets,
-                                              None, out_dtype, return_output, True, dim1)
+    with _tune.applied(_tune.pick("fwd", E, N, K)):
+        s, q, st, qt, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales,
+                                                  group_end_offsets, None, out_dtype, return_output, True, dim1)
     res = (s, q, st, qt) if dim1 else (s, q)
     return res + (out,) if return_output else res
