@@ -34,6 +34,8 @@
 * ``--impl reference``: the reference's CPU path (dequantise + per-group fp32
   matmul, the oracle restatement -- the reference's Triton kernels are
   ROCm-only) timed on this host's cores over a bounded sample.
+* ``--torch-arm`` (1 GPU): adds ``torch_scaled_grouped_mm``, torch's own
+  MXFP8 grouped GEMM timed beside this library's on the same forward points.
 """
 
 import argparse
@@ -348,6 +350,78 @@ def run_problem(p):
     if p["pass_"] == "wgrad":
         return kernels.triton_mxfp8_wgrad(*p["args"])
     return kernels.triton_mxfp8_grouped_mm(*p["args"])
+
+
+def _blocked_scales(s2d):
+    """(R, C) e8m0 scales -> the 128x4 blocked layout of block-scaled tensor
+    cores (rows padded to 128, columns to 4; atom byte (r % 32) * 16 +
+    (r % 128) // 32 * 4 + c % 4), returned as a (R', C') tensor."""
+    import torch
+    R, C = s2d.shape
+    Rp, Cp = -(-R // 128) * 128, -(-C // 4) * 4
+    pad = torch.zeros((Rp, Cp), dtype=torch.uint8, device=s2d.device)
+    pad[:R, :C] = s2d.view(torch.uint8)
+    b = pad.view(Rp // 128, 128, Cp // 4, 4).permute(0, 2, 1, 3).reshape(-1, 4, 32, 4).transpose(1, 2)
+    return b.reshape(Rp, Cp)
+
+
+def torch_grouped_arm(device, shapes, steps=5):
+    """torch's own MXFP8 grouped GEMM (torch._scaled_grouped_mm, sm_100) on
+    the same forward points, beside this library's: its counterpart of the
+    reference's vendor comparison arms (bench.py:95-110).  Scales are re-laid
+    into torch's per-group blocked layout outside the timed region (this
+    library packs its own scales inside every call).  Returns per-point
+    TFLOPS and the rel-L2 between the two outputs, or why torch refused."""
+    import random
+
+    import torch
+
+    import kernels
+    import utils
+    rows = []
+    for (E, M, N, K) in shapes:
+        random.seed(123)
+        g = torch.Generator(device=device).manual_seed(123)
+        offs = utils.generate_jagged_offs(E, M, multiple_of=32, device=device)
+        a_s, a_q = utils.to_mx(torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=g))
+        b_s, b_q = utils.to_mx(torch.randn(E, N, K, device=device, dtype=torch.bfloat16, generator=g))
+        ends = [0] + offs.tolist()
+        sa = torch.cat([_blocked_scales(a_s[ends[i]:ends[i + 1]]) for i in range(E) if ends[i + 1] > ends[i]])
+        sb = torch.stack([_blocked_scales(b_s[e]).reshape(-1) for e in range(E)])   # (E, blocked N x K/32)
+        sa, sb = sa.view(torch.float8_e8m0fnu), sb.view(torch.float8_e8m0fnu)
+        ours = kernels.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, offs)
+        try:
+            theirs = torch._scaled_grouped_mm(a_q, b_q.transpose(-2, -1), sa, sb, offs=offs,
+                                              out_dtype=torch.bfloat16)
+        except Exception as e:   # torch rejects the layout or has no sm_100 MXFP8 grouped path
+            return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+        torch.cuda.synchronize()
+        d = (theirs.float() - ours.float()).norm() / ours.float().norm().clamp_min(1e-30)
+
+        def t(fn):
+            for _ in range(2):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            scratch = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+            for s_, e_ in ev:
+                scratch.zero_()
+                s_.record()
+                fn()
+                e_.record()
+            torch.cuda.synchronize()
+            return sum(s_.elapsed_time(e_) for s_, e_ in ev) / steps * 1e-3
+
+        fl = 2.0 * M * N * K
+        t_ours = t(lambda: kernels.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, offs))
+        t_theirs = t(lambda: torch._scaled_grouped_mm(a_q, b_q.transpose(-2, -1), sa, sb, offs=offs,
+                                                      out_dtype=torch.bfloat16))
+        rows.append({"E": E, "N": N, "K": K, "mxgg_tflops": round(fl / t_ours / 1e12, 1),
+                     "torch_tflops": round(fl / t_theirs / 1e12, 1), "rel_l2": float(f"{d.item():.3g}")})
+        del a_q, b_q, a_s, b_s, sa, sb, ours, theirs
+    return {"points": rows,
+            "mxgg_geomean": round(geomean([r["mxgg_tflops"] for r in rows]), 1),
+            "torch_geomean": round(geomean([r["torch_tflops"] for r in rows]), 1),
+            "note": "forward calls; torch's scale re-layout is outside its timed region"}
 
 
 # ------------------------------------------------------------------ peaks
@@ -668,6 +742,8 @@ def main():
                     help="GEMM work schedule: split the last partial round's tiles (split_tail, the default) "
                          "or deal whole tiles")
     ap.add_argument("--split-max", type=int, default=0, help="most pieces per split tile (0 = automatic)")
+    ap.add_argument("--torch-arm", action="store_true",
+                    help="also time torch._scaled_grouped_mm (MXFP8) on the same forward shapes (1 GPU)")
     ap.add_argument("--ep-impl", default="fused", choices=["fused", "nccl"],
                     help="N > 1: peer-memory dispatch with the combine fused into the GEMM (fused), "
                          "or NCCL all-to-all dispatch/combine around the segment GEMM (nccl)")
@@ -824,6 +900,8 @@ def main():
             line["moe_layer"] = moe
         if fp4:
             line["mxfp4_weights"] = fp4
+        if args.torch_arm and world == 1:
+            line["torch_scaled_grouped_mm"] = torch_grouped_arm(dev, [shapes[i] for i in idx])
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier(world)
