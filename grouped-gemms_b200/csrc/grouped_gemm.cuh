@@ -23,7 +23,9 @@
 //               into TMEM, then tcgen05.mma.kind::mxf8f6f4.block_scale (K=32)
 //   warp 3      builds the group table in the prologue
 //   warps 4-7   epilogue: TMEM -> registers -> bf16/fp32 -> swizzled smem ->
-//               TMA store; ragged group edges fall back to predicated stores
+//               TMA store; ragged group edges fall back to predicated stores;
+//               on request also the MX-quantised rows and transpose (to_mx and
+//               to_mx_dim1 of the output) from the same registers
 //
 // Scheduling: a persistent grid (one CTA per SM) walks a device-built
 // group->tile map: every CTA reads the group end offsets once, builds the
