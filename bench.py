@@ -298,7 +298,7 @@ def run_ep_problem(p, marks=None):
     local GEMM | combine."""
     import kernels
     from mxgg import ep
-    from mxgg.ops import grouped_mm_segments_op
+    from mxgg.ops import grouped_mm_segments
     plan = p["plan"]
     if p["pass_"] == "wgrad":
         if marks:
@@ -328,7 +328,7 @@ def run_ep_problem(p, marks=None):
     recv_q, recv_s = ep.dispatch(plan, *p["args"])
     if marks:
         marks[0].record()
-    y = grouped_mm_segments_op(recv_q, p["weights"][0], recv_s, p["weights"][1], plan.seg_offs, plan.seg_expert,
+    y = grouped_mm_segments(recv_q, p["weights"][0], recv_s, p["weights"][1], plan.seg_offs, plan.seg_expert,
                                torch_bf16())
     if marks:
         marks[1].record()
@@ -383,8 +383,10 @@ def torch_grouped_arm(device, shapes, steps=5):
         random.seed(123)
         g = torch.Generator(device=device).manual_seed(123)
         offs = utils.generate_jagged_offs(E, M, multiple_of=32, device=device)
-        a_s, a_q = utils.to_mx(torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=g))
-        b_s, b_q = utils.to_mx(torch.randn(E, N, K, device=device, dtype=torch.bfloat16, generator=g))
+        A = torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=g)
+        W = torch.randn(E, N, K, device=device, dtype=torch.bfloat16, generator=g)
+        a_s, a_q = utils.to_mx(A)
+        b_s, b_q = utils.to_mx(W)
         ends = [0] + offs.tolist()
         sa = torch.cat([_blocked_scales(a_s[ends[i]:ends[i + 1]]) for i in range(E) if ends[i + 1] > ends[i]])
         sb = torch.stack([_blocked_scales(b_s[e]).reshape(-1) for e in range(E)])   # (E, blocked N x K/32)
@@ -415,13 +417,18 @@ def torch_grouped_arm(device, shapes, steps=5):
         t_ours = t(lambda: kernels.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, offs))
         t_theirs = t(lambda: torch._scaled_grouped_mm(a_q, b_q.transpose(-2, -1), sa, sb, offs=offs,
                                                       out_dtype=torch.bfloat16))
+        # the reference bench's own baseline column: bf16 torch._grouped_mm (bench.py:125-183)
+        t_bf16 = t(lambda: torch._grouped_mm(A, W.transpose(-2, -1), offs=offs))
         rows.append({"E": E, "N": N, "K": K, "mxgg_tflops": round(fl / t_ours / 1e12, 1),
-                     "torch_tflops": round(fl / t_theirs / 1e12, 1), "rel_l2": float(f"{d.item():.3g}")})
-        del a_q, b_q, a_s, b_s, sa, sb, ours, theirs
+                     "torch_tflops": round(fl / t_theirs / 1e12, 1), "bf16_tflops": round(fl / t_bf16 / 1e12, 1),
+                     "rel_l2": float(f"{d.item():.3g}")})
+        del a_q, b_q, a_s, b_s, sa, sb, ours, theirs, A, W
     return {"points": rows,
             "mxgg_geomean": round(geomean([r["mxgg_tflops"] for r in rows]), 1),
             "torch_geomean": round(geomean([r["torch_tflops"] for r in rows]), 1),
-            "note": "forward calls; torch's scale re-layout is outside its timed region"}
+            "bf16_grouped_mm_geomean": round(geomean([r["bf16_tflops"] for r in rows]), 1),
+            "note": "forward calls; torch's scale re-layout is outside its timed region; bf16 = "
+                    "torch._grouped_mm on the unquantised operands (the reference bench's baseline)"}
 
 
 # ------------------------------------------------------------------ peaks

@@ -49,6 +49,6 @@ def triton_mxfp8_wgrad(
     cfg = _tune.pick("wgrad", group_end_offsets.shape[0], go_t.shape[0], ia_t.shape[0])
     with _tune.applied(cfg):
         if out is not None:
-            mxgg.wgrad_accumulate_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
+            mxgg.ops.wgrad_accumulate(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
             return out
-        return mxgg.wgrad_op(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)
+        return mxgg.ops.wgrad(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)

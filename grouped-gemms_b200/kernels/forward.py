@@ -67,12 +67,12 @@ def triton_mxfp8_grouped_mm(
         assert K == 2 * K2, f"K mismatch: A={K}, B={2 * K2} (e2m1 packed)"
         experts = torch.arange(E, dtype=torch.int32, device=weight.device)
         with _tune.applied(_tune.pick("fwd", E, N, K)):
-            return mxgg.grouped_mm_segments_op(input_act, weight, input_act_scales, weight_scales,
-                                               group_end_offsets, experts, out_dtype)
+            return mxgg.ops.grouped_mm_segments(input_act, weight, input_act_scales, weight_scales,
+                                                 group_end_offsets, experts, out_dtype)
     assert K == K2, f"K mismatch: A={K}, B={K2}"
     # a tuned config for this call shape (mxgg.tune), else the library's choice
     with _tune.applied(_tune.pick("fwd", E, N, K)):
-        return mxgg.grouped_mm_op(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
+        return mxgg.ops.grouped_mm(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
 
 
 def mxfp8_grouped_mm_to_mx(
@@ -108,7 +108,7 @@ def mxfp8_grouped_mm_to_mx(
     packed = weight.dtype == torch.float4_e2m1fn_x2
     assert K == (2 * K2 if packed else K2), f"K mismatch: A={K}, B={2 * K2 if packed else K2}"
     with _tune.applied(_tune.pick("fwd", E, N, K)):
-        s, q, st, qt, out = mxgg.grouped_mm_mx_op(input_act, weight, input_act_scales, weight_scales,
-                                                  group_end_offsets, None, out_dtype, return_output, True, dim1)
+        s, q, st, qt, out = mxgg.ops.grouped_mm_mx(input_act, weight, input_act_scales, weight_scales,
+                                                   group_end_offsets, None, out_dtype, return_output, True, dim1)
     res = (s, q, st, qt) if dim1 else (s, q)
     return res + (out,) if return_output else res

@@ -166,9 +166,9 @@ def ep_grouped_mm(plan: DispatchPlan, a_q: Tensor, a_s: Tensor, w_q: Tensor, w_s
     sorted by expert; w_q (L, N, K) / w_s (L, N, K/32) are the hosted experts.
     Returns (rows_local, N) in this rank's row order.
     """
-    from .ops import grouped_mm_segments_op
+    from .ops import grouped_mm_segments
     recv_q, recv_s = dispatch(plan, a_q, a_s, group=group)
-    y = grouped_mm_segments_op(recv_q, w_q, recv_s, w_s, plan.seg_offs, plan.seg_expert, out_dtype)
+    y = grouped_mm_segments(recv_q, w_q, recv_s, w_s, plan.seg_offs, plan.seg_expert, out_dtype)
     return combine(plan, y, group=group)
 
 

@@ -23,8 +23,7 @@ from torch import Tensor
 
 from . import _lib
 from .ep import ExpertPlacement, FusedExpertParallel
-from .ops import (_IN_DTYPES, _ptr, _stream, grouped_mm_mx_op, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op,
-                  to_mx_op)
+from .ops import _IN_DTYPES, _ptr, _stream, grouped_mm_mx, grouped_mm_segments, to_mx, to_mx_fp4
 
 PAD = 32
 
@@ -92,9 +91,9 @@ def _quantize_weights(w: Tensor, fp4: bool):
     L, N, K = w.shape
     w2 = w.reshape(L * N, K)
     if fp4:
-        s, q = to_mx_fp4_op(w2, _lib.SCALE_ROW_MAJOR)
+        s, q = to_mx_fp4(w2, _lib.SCALE_ROW_MAJOR)
         return q.view(torch.uint8).reshape(L, N, K // 2).view(torch.float4_e2m1fn_x2), s.reshape(L, N, K // 32)
-    s, q = to_mx_op(w2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
+    s, q = to_mx(w2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
     return q.reshape(L, N, K), s.reshape(L, N, K // 32)
 
 
@@ -123,8 +122,8 @@ class MoELayer:
             offs = torch.tensor(layout.counts, dtype=torch.int64).cumsum(0).to(torch.int32).to(x.device)
             seg_e = torch.arange(self.n_experts, dtype=torch.int32, device=x.device)
             # the up projection's epilogue writes to_mx of its bf16 output
-            h_s, h_q, _, _, _ = grouped_mm_mx_op(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16, False)
-            y = grouped_mm_segments_op(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
+            h_s, h_q, _, _, _ = grouped_mm_mx(a_q, self.up_q, a_s, self.up_s, offs, seg_e, torch.bfloat16, False)
+            y = grouped_mm_segments(h_q, self.down_q, h_s, self.down_s, offs, seg_e, torch.bfloat16)
         else:
             # rows stream into the hosts' receive buffers while the up projection
             # consumes them; the down projection sends its rows to their owners

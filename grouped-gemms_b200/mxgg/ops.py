@@ -12,6 +12,7 @@ from typing import Optional, Tuple
 
 import torch
 from torch import Tensor
+from torch.utils._python_dispatch import _get_current_dispatch_mode
 
 from . import _lib
 
@@ -52,9 +53,31 @@ def as_u8(t: Tensor) -> Tensor:
     return t if t.dtype == torch.uint8 else t.view(torch.uint8)
 
 
+def _eager(args) -> bool:
+    """True when a call may run its implementation directly instead of going
+    through the torch.library dispatcher (which costs ~15 us of host time per
+    call): eager mode, no dispatch mode active (FakeTensor tracing, flop
+    counters), and plain tensors that need no autograd.  Anything else takes
+    the registered op, so torch.compile and tensor subclasses see it."""
+    if torch.compiler.is_compiling() or _get_current_dispatch_mode() is not None:
+        return False
+    for t in args:
+        if isinstance(t, Tensor) and (type(t) is not Tensor or t.requires_grad):
+            return False
+    return True
+
+
+def _fast(op, impl):
+    """`op`'s eager fast path: `impl` directly when `_eager` allows, else `op`."""
+    def call(*args):
+        return impl(*args) if _eager(args) else op(*args)
+    call.__name__ = getattr(impl, "__name__", "call").lstrip("_").replace("_impl", "")
+    call.__doc__ = impl.__doc__
+    return call
+
+
 # --------------------------------------------------------------------- to_mx
-@torch.library.custom_op("mxgg::to_mx", mutates_args=())
-def to_mx_op(x: Tensor, mode: int, scale_layout: int) -> Tuple[Tensor, Tensor]:
+def _to_mx_impl(x: Tensor, mode: int, scale_layout: int) -> Tuple[Tensor, Tensor]:
     _require_cuda(x, what="mxgg::to_mx")
     if x.dtype not in _IN_DTYPES:
         raise TypeError(f"mxgg::to_mx: unsupported input dtype {x.dtype}")
@@ -77,6 +100,10 @@ def to_mx_op(x: Tensor, mode: int, scale_layout: int) -> Tuple[Tensor, Tensor]:
     return s, q
 
 
+to_mx_op = torch.library.custom_op("mxgg::to_mx", _to_mx_impl, mutates_args=())
+to_mx = _fast(to_mx_op, _to_mx_impl)
+
+
 @to_mx_op.register_fake
 def _(x, mode, scale_layout):
     R, C = x.shape
@@ -93,8 +120,7 @@ def _(x, mode, scale_layout):
     return s, q
 
 
-@torch.library.custom_op("mxgg::to_mx_fp4", mutates_args=())
-def to_mx_fp4_op(x: Tensor, scale_layout: int) -> Tuple[Tensor, Tensor]:
+def _to_mx_fp4_impl(x: Tensor, scale_layout: int) -> Tuple[Tensor, Tensor]:
     """MXFP4 along the last dim: (scales (R, C/32) u8, q (R, C/2) float4_e2m1fn_x2)."""
     _require_cuda(x, what="mxgg::to_mx_fp4")
     if x.dtype not in _IN_DTYPES:
@@ -112,6 +138,10 @@ def to_mx_fp4_op(x: Tensor, scale_layout: int) -> Tuple[Tensor, Tensor]:
     return s, q.view(torch.float4_e2m1fn_x2)
 
 
+to_mx_fp4_op = torch.library.custom_op("mxgg::to_mx_fp4", _to_mx_fp4_impl, mutates_args=())
+to_mx_fp4 = _fast(to_mx_fp4_op, _to_mx_fp4_impl)
+
+
 @to_mx_fp4_op.register_fake
 def _(x, scale_layout):
     R, C = x.shape
@@ -124,8 +154,7 @@ def _(x, scale_layout):
 
 
 # ---------------------------------------------------------------- grouped_mm
-@torch.library.custom_op("mxgg::grouped_mm", mutates_args=())
-def grouped_mm_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
+def _grouped_mm_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
                   out_dtype: torch.dtype) -> Tensor:
     _require_cuda(a, b, a_scale, b_scale, offs, what="mxgg::grouped_mm")
     if out_dtype not in _OUT_DTYPES:
@@ -147,14 +176,17 @@ def grouped_mm_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: 
     return out
 
 
+grouped_mm_op = torch.library.custom_op("mxgg::grouped_mm", _grouped_mm_impl, mutates_args=())
+grouped_mm = _fast(grouped_mm_op, _grouped_mm_impl)
+
+
 @grouped_mm_op.register_fake
 def _(a, b, a_scale, b_scale, offs, out_dtype):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
 # ------------------------------------------------------- grouped_mm_segments
-@torch.library.custom_op("mxgg::grouped_mm_segments", mutates_args=())
-def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
+def _grouped_mm_segments_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
                            seg_expert: Tensor, out_dtype: torch.dtype) -> Tensor:
     """Rows of segment s times B[seg_expert[s]]: the layout an expert-parallel
     all-to-all delivers (source-major, then expert)."""
@@ -182,13 +214,17 @@ def grouped_mm_segments_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tenso
     return out
 
 
+grouped_mm_segments_op = torch.library.custom_op("mxgg::grouped_mm_segments", _grouped_mm_segments_impl,
+                                                 mutates_args=())
+grouped_mm_segments = _fast(grouped_mm_segments_op, _grouped_mm_segments_impl)
+
+
 @grouped_mm_segments_op.register_fake
 def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
-@torch.library.custom_op("mxgg::grouped_mm_mx", mutates_args=())
-def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
+def _grouped_mm_mx_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
                      seg_expert: Optional[Tensor], out_dtype: torch.dtype, keep_out: bool, rows: bool = True,
                      cols: bool = False) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The forward (segments as in grouped_mm_segments_op; seg_expert None:
@@ -241,6 +277,10 @@ def grouped_mm_mx_op(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg
     return s, q, st, qt, out
 
 
+grouped_mm_mx_op = torch.library.custom_op("mxgg::grouped_mm_mx", _grouped_mm_mx_impl, mutates_args=())
+grouped_mm_mx = _fast(grouped_mm_mx_op, _grouped_mm_mx_impl)
+
+
 @grouped_mm_mx_op.register_fake
 def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False):
     M, N = a.shape[0], b.shape[1]
@@ -251,8 +291,7 @@ def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=Tr
 
 
 # --------------------------------------------------------------------- wgrad
-@torch.library.custom_op("mxgg::wgrad", mutates_args=())
-def wgrad_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
+def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
              out_dtype: torch.dtype) -> Tensor:
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, what="mxgg::wgrad")
     if out_dtype not in _OUT_DTYPES:
@@ -275,13 +314,16 @@ def wgrad_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, off
     return out
 
 
+wgrad_op = torch.library.custom_op("mxgg::wgrad", _wgrad_impl, mutates_args=())
+wgrad = _fast(wgrad_op, _wgrad_impl)
+
+
 @wgrad_op.register_fake
 def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype):
     return go_t.new_empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype)
 
 
-@torch.library.custom_op("mxgg::wgrad_accumulate_", mutates_args=("out",))
-def wgrad_accumulate_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
+def _wgrad_accumulate_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
                         out: Tensor) -> None:
     """out[g] += the group's weight gradient, in place (fp32 out)."""
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, out, what="mxgg::wgrad_accumulate_")
@@ -301,6 +343,11 @@ def wgrad_accumulate_op(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: 
         _lib.check(lib.mxgg_wgrad_accumulate(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
                                              N, K, M, E, _ptr(out), _ptr(ws), ws.numel(), _stream(go_t.device)),
                    "mxgg_wgrad_accumulate")
+
+
+wgrad_accumulate_op = torch.library.custom_op("mxgg::wgrad_accumulate_", _wgrad_accumulate_impl,
+                                              mutates_args=("out",))
+wgrad_accumulate = _fast(wgrad_accumulate_op, _wgrad_accumulate_impl)
 
 
 @wgrad_accumulate_op.register_fake

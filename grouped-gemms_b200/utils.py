@@ -42,11 +42,11 @@ def to_mx(data: torch.Tensor, elem_dtype=torch.float8_e4m3fn, block_size: int = 
     if elem_dtype is torch.float4_e2m1fn_x2:
         # MXFP4 (no reference counterpart): FLOOR scaling with emax 2, two
         # e2m1 values per byte, element 2i in the low nibble
-        s, q = mxgg.to_mx_fp4_op(x2, _lib.SCALE_ROW_MAJOR)
+        s, q = mxgg.ops.to_mx_fp4(x2, _lib.SCALE_ROW_MAJOR)
         q_shape = list(orig_shape)
         q_shape[-1] = orig_shape[-1] // 2
         return s.reshape(scale_shape), q.reshape(q_shape)
-    s, q = mxgg.to_mx_op(x2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
+    s, q = mxgg.ops.to_mx(x2, _lib.QUANT_ROWS, _lib.SCALE_ROW_MAJOR)
     return s.reshape(scale_shape), q.reshape(orig_shape)
 
 
@@ -57,7 +57,7 @@ def to_mx_dim1(data: torch.Tensor, elem_dtype=torch.float8_e4m3fn, block_size: i
     """
     assert data.dim() == 2, "to_mx_dim1 takes a 2-D tensor"
     _check_to_mx_args(data.t(), elem_dtype, block_size)
-    return mxgg.to_mx_op(data, _lib.QUANT_COLS, _lib.SCALE_ROW_MAJOR)
+    return mxgg.ops.to_mx(data, _lib.QUANT_COLS, _lib.SCALE_ROW_MAJOR)
 
 
 def to_mx_blocked_scales(data: torch.Tensor):
@@ -66,7 +66,7 @@ def to_mx_blocked_scales(data: torch.Tensor):
     and ``torch._scaled_mm`` consume.  Returns ``(scales_flat_u8, data_fp8)``.
     """
     assert data.dim() == 2 and data.shape[-1] % 32 == 0
-    return mxgg.to_mx_op(data, _lib.QUANT_ROWS, _lib.SCALE_BLOCKED)
+    return mxgg.ops.to_mx(data, _lib.QUANT_ROWS, _lib.SCALE_BLOCKED)
 
 
 def generate_jagged_offs(E: int, M: int, multiple_of: int = 32, dtype=torch.int32, device="cuda") -> torch.Tensor:

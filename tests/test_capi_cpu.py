@@ -170,3 +170,40 @@ def test_loader_refuses_a_stale_library(monkeypatch):
     monkeypatch.setattr(_lib, "source_digest", lambda: "0" * 16)
     with pytest.raises(_lib.MxggError, match="built from other sources"):
         _lib.load()
+
+
+def test_eager_fast_path_conditions():
+    """Plain eager calls skip the torch.library dispatcher; tracing modes,
+    tensor subclasses and autograd inputs take the registered op."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from mxgg import ops
+    x = torch.zeros(4)
+    assert ops._eager((x, 3, torch.bfloat16))
+    assert not ops._eager((torch.zeros(4, requires_grad=True),))
+    assert not ops._eager((torch.nn.Parameter(torch.zeros(4)),))
+    with FakeTensorMode():
+        assert not ops._eager((x,))
+
+
+def test_fake_mode_uses_the_registered_fake_kernel():
+    """Under FakeTensorMode (what torch.compile traces with) the entry points
+    return shape-correct fakes without touching the library or a GPU."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from mxgg import ops
+    with FakeTensorMode():
+        a = torch.empty(1024, 512, dtype=torch.float8_e4m3fn, device="cuda")
+        b = torch.empty(4, 256, 512, dtype=torch.float8_e4m3fn, device="cuda")
+        sa = torch.empty(1024, 16, dtype=torch.uint8, device="cuda")
+        sb = torch.empty(4, 256, 16, dtype=torch.uint8, device="cuda")
+        offs = torch.empty(4, dtype=torch.int32, device="cuda")
+        out = ops.grouped_mm(a, b, sa, sb, offs, torch.bfloat16)
+        s, q, st, qt, o = ops.grouped_mm_mx(a, b, sa, sb, offs, None, torch.bfloat16, False, True, True)
+        go = torch.empty(256, 1024, dtype=torch.float8_e4m3fn, device="cuda")
+        gs = torch.empty(256, 32, dtype=torch.uint8, device="cuda")
+        w = ops.wgrad(go, gs, go, gs, offs, torch.float32)
+    assert out.shape == (1024, 256) and out.dtype == torch.bfloat16
+    assert s.shape == (1024, 8) and q.shape == (1024, 256) and st.shape == (256, 32) and qt.shape == (256, 1024)
+    assert o.numel() == 0
+    assert w.shape == (4, 256, 256) and w.dtype == torch.float32
