@@ -27,6 +27,12 @@ int main(void) {
   int ok = mxgg_set_tile_config(0, 0, 0);
   printf("%d %lld %lld %lld %d %d %s\n", v, (long long)fwd, (long long)wg, (long long)bad, rc, ok,
          strstr(msg, "tile_m") ? "msg-ok" : msg);
+  /* the fused quantised output rejects N % 32 != 0 before touching a GPU */
+  char buf[64];
+  void* p = (void*)(((uintptr_t)buf + 15) & ~(uintptr_t)15);
+  int rq = mxgg_grouped_mm_mx(p, p, p, p, (const int32_t*)p, 0, 64, 48, 64, 1, 1, MXGG_FMT_E4M3, 0,
+                              MXGG_DTYPE_BF16, p, p, 0, 0, p, 1 << 20, 0);
+  printf("%d %s %s\n", rq, strstr(mxgg_last_error(), "N % 32") ? "mx-ok" : mxgg_last_error(), mxgg_build_id());
   return 0;
 }
 """
@@ -47,9 +53,11 @@ def test_c_program_links_and_calls_the_abi():
         out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()
     finally:
         shutil.rmtree(d, ignore_errors=True)
-    v, fwd, wg, bad, rc, ok, msg = out
+    v, fwd, wg, bad, rc, ok, msg, rq, mx_msg, build_id = out
     assert int(v) > 0
     assert int(fwd) > 0 and int(wg) > 0
     assert int(bad) == -1
     assert int(rc) == 1 and int(ok) == 0           # MXGG_ERR_INVALID, then MXGG_OK
     assert msg == "msg-ok"
+    assert int(rq) == 3 and mx_msg == "mx-ok"                  # MXGG_ERR_UNSUPPORTED
+    assert len(build_id) == 16 and build_id != "unversioned"
