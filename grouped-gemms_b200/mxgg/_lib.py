@@ -136,14 +136,27 @@ def device_status(clear: bool = True, stream=None) -> int:
     return v.value
 
 
+# the library's process-wide GEMM config as last set through this module
+_config = {"tile": (0, 0, 0), "schedule": (SCHED_DEFAULT, 0)}
+
+
 def set_tile_config(tile_m: int = 0, tile_n: int = 0, group_m: int = 0) -> None:
     """Tile shape for later GEMM calls (0 = automatic): tile_m 128 (one CTA)
-    or 256 (a CTA pair), tile_n 128 or 256, group_m the rasterisation band."""
+    or 256 (a CTA pair), tile_n 128 or 256, group_m the rasterisation band.
+    The setting is process-wide (every thread, every device)."""
     check(load().mxgg_set_tile_config(tile_m, tile_n, group_m), "mxgg_set_tile_config")
+    _config["tile"] = (tile_m, tile_n, group_m)
 
 
 def set_schedule(schedule: int = SCHED_DEFAULT, split_max: int = 0) -> None:
     """Work schedule of later GEMM calls: SCHED_SPLIT_TAIL (default) cuts the
     tiles of the last partial round along the contraction for idle CTA pairs,
-    SCHED_TILES deals whole tiles; split_max caps the pieces per tile."""
+    SCHED_TILES deals whole tiles; split_max caps the pieces per tile.
+    Process-wide, like set_tile_config."""
     check(load().mxgg_set_schedule(schedule, split_max), "mxgg_set_schedule")
+    _config["schedule"] = (schedule, split_max)
+
+
+def current_config():
+    """((tile_m, tile_n, group_m), (schedule, split_max)) as last set here."""
+    return _config["tile"], _config["schedule"]

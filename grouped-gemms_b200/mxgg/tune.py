@@ -82,9 +82,6 @@ def config_space(tile_ms: Sequence[int] = (256, 128), tile_ns: Sequence[int] = (
     return out
 
 
-_base = DEFAULT   # what `applied` restores
-
-
 def _set(cfg: Config) -> None:
     _lib.set_tile_config(cfg.tile_m, cfg.tile_n, cfg.group_m)
     _lib.set_schedule(cfg.schedule, cfg.split_max)
@@ -92,19 +89,22 @@ def _set(cfg: Config) -> None:
 
 @contextlib.contextmanager
 def applied(cfg: Optional[Config]):
-    """Run the body with `cfg` in force (None: as is), then restore the base
-    config.  The library reads its config on the host while it enqueues a
-    call, so restoring right after the call is safe."""
+    """Run the body with `cfg` in force (None: as is), then restore the
+    config that was set before (`mxgg.set_tile_config` / `set_schedule`).
+    The library reads its config on the host while it enqueues a call, so
+    restoring right after the call is safe.  The config is process-wide:
+    threads that issue GEMMs concurrently share it."""
     if cfg is None:
         yield
         return
     if not cfg.valid():
         raise ValueError(f"invalid config {cfg}")
+    (tm, tn, gm), (sch, smax) = _lib.current_config()
     _set(cfg)
     try:
         yield
     finally:
-        _set(_base)
+        _set(Config(tm, tn, gm, sch, smax))
 
 
 # ------------------------------------------------------------------ tables

@@ -135,3 +135,17 @@ def test_install_and_pick():
     finally:
         tune.install(None)
     assert tune.pick("fwd", 2, 256, 512) is None
+
+
+def test_applied_restores_the_callers_config():
+    """A config set by the caller (bench --tile-m, say) comes back after a
+    tuned call, not the library default."""
+    try:
+        _lib.set_tile_config(128, 256, 4)
+        _lib.set_schedule(_lib.SCHED_TILES, 0)
+        with tune.applied(tune.Config(256, 128, 16, _lib.SCHED_SPLIT_TAIL, 3)):
+            assert _lib.current_config() == ((256, 128, 16), (_lib.SCHED_SPLIT_TAIL, 3))
+        assert _lib.current_config() == ((128, 256, 4), (_lib.SCHED_TILES, 0))
+    finally:
+        _lib.set_tile_config(0, 0, 0)
+        _lib.set_schedule(_lib.SCHED_DEFAULT, 0)
