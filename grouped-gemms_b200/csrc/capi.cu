@@ -53,11 +53,18 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
-int g_tile_m = 0;
-int g_tile_n = 0;
-int g_group_m = 0;
-int g_schedule = MXGG_SCHED_DEFAULT;
-int g_split_max = 0;
+
+// Tile and schedule choice of one call: the process defaults
+// (mxgg_set_tile_config / mxgg_set_schedule, read under g_mu) overridden by
+// the non-zero fields of the call's own mxgg_gemm_config.
+struct GemmCfg {
+  int tile_m = 0;
+  int tile_n = 0;
+  int group_m = 0;
+  int schedule = MXGG_SCHED_DEFAULT;
+  int split_max = 0;
+};
+GemmCfg g_default_cfg;   // guarded by g_mu
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -237,16 +244,50 @@ struct TileChoice {
 // Default tiles: a CTA pair per 256 x 256 tile with raster bands of 16 row
 // tiles (best on 101 of the 108 Llama4 sweep points against one CTA per
 // 128 x 256 tile, measured in one run); single-CTA tiles prefer bands of 2.
-TileChoice pick_tiles(int64_t n_extent) {
+TileChoice pick_tiles(int64_t n_extent, const GemmCfg& cfg) {
   TileChoice c;
-  c.tile_m = (g_tile_m == 128 || g_tile_m == 256) ? g_tile_m : 256;
-  c.tile_n = (g_tile_n == 128 || g_tile_n == 256) ? g_tile_n : (n_extent >= 256 ? 256 : 128);
+  c.tile_m = (cfg.tile_m == 128 || cfg.tile_m == 256) ? cfg.tile_m : 256;
+  c.tile_n = (cfg.tile_n == 128 || cfg.tile_n == 256) ? cfg.tile_n : (n_extent >= 256 ? 256 : 128);
   return c;
 }
 
-int pick_group_m(const TileChoice& c) {
-  if (g_group_m > 0) return g_group_m;
+int pick_group_m(const TileChoice& c, const GemmCfg& cfg) {
+  if (cfg.group_m > 0) return cfg.group_m;
   return c.tile_m == 128 ? 2 : 16;
+}
+
+int check_cfg_fields(int tile_m, int tile_n, int group_m, int schedule, int split_max, const char* what) {
+  if (tile_m != 0 && tile_m != 128 && tile_m != 256)
+    return fail(MXGG_ERR_INVALID, "%s: tile_m must be 0, 128 or 256 (got %d)", what, tile_m);
+  if (tile_n != 0 && tile_n != 128 && tile_n != 256)
+    return fail(MXGG_ERR_INVALID, "%s: tile_n must be 0, 128 or 256 (got %d)", what, tile_n);
+  if (group_m < 0) return fail(MXGG_ERR_INVALID, "%s: group_m must be >= 0 (got %d)", what, group_m);
+  if (schedule != MXGG_SCHED_DEFAULT && schedule != MXGG_SCHED_TILES && schedule != MXGG_SCHED_SPLIT_TAIL)
+    return fail(MXGG_ERR_INVALID, "%s: unknown schedule %d", what, schedule);
+  if (split_max < 0 || split_max == 1 || split_max > 64)
+    return fail(MXGG_ERR_INVALID, "%s: split_max must be 0 (automatic) or 2..64 (got %d)", what, split_max);
+  return MXGG_OK;
+}
+
+// The call's configuration: a snapshot of the process defaults taken under
+// the lock (so a concurrent mxgg_set_* never tears it), with the non-zero
+// fields of `user` (may be null) on top.
+int resolve_cfg(const mxgg_gemm_config* user, GemmCfg* out, const char* what) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    *out = g_default_cfg;
+  }
+  if (!user) return MXGG_OK;
+  if (user->reserved[0] || user->reserved[1] || user->reserved[2])
+    return fail(MXGG_ERR_INVALID, "%s: mxgg_gemm_config.reserved must be zero", what);
+  if (int rc = check_cfg_fields(user->tile_m, user->tile_n, user->group_m, user->schedule, user->split_max, what))
+    return rc;
+  if (user->tile_m) out->tile_m = user->tile_m;
+  if (user->tile_n) out->tile_n = user->tile_n;
+  if (user->group_m) out->group_m = user->group_m;
+  if (user->schedule != MXGG_SCHED_DEFAULT) out->schedule = user->schedule;
+  if (user->split_max) out->split_max = user->split_max;
+  return MXGG_OK;
 }
 
 // Expert-parallel output routing of a forward call (see GemmParams).
@@ -286,9 +327,11 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
              void* workspace, int64_t workspace_bytes, void* stream_v, bool split_ok = true,
              const int32_t* group_expert = nullptr, int64_t n_experts = -1,
              const char* what = nullptr, const EpRoute* route = nullptr, int b_format = MXGG_FMT_E4M3,
-             bool accumulate = false, const QuantOut* quant = nullptr) {
+             bool accumulate = false, const QuantOut* quant = nullptr, const mxgg_gemm_config* user_cfg = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (!what) what = mode == kFwd ? "mxgg_grouped_mm" : "mxgg_wgrad";
+  GemmCfg cfg;
+  if (int rc = resolve_cfg(user_cfg, &cfg, what)) return rc;
   if (n_experts < 0) n_experts = E;
   if (out_dtype != MXGG_DTYPE_BF16 && out_dtype != MXGG_DTYPE_F16 && out_dtype != MXGG_DTYPE_F32)
     return fail(MXGG_ERR_INVALID, "%s: unknown out_dtype %d", what, out_dtype);
@@ -383,7 +426,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   DeviceState* st = nullptr;
   if (int rc = get_device_state(&st)) return rc;
 
-  const TileChoice tc = pick_tiles(out_cols);
+  const TileChoice tc = pick_tiles(out_cols, cfg);
   const int bn = tc.tile_n;
   const int pair = tc.tile_m / kBM;
   const WsPlan ws = plan_workspace(mode, M, N, K, E, n_experts, tc.tile_m, bn);
@@ -395,7 +438,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   uint8_t* ws_b = ws_a + ws.a_bytes;
   float* part_slots = reinterpret_cast<float*>(ws_b + ws.b_bytes);
   int* part_counters = reinterpret_cast<int*>(ws_b + ws.b_bytes + ws.part_bytes);
-  const bool split_tail = split_ok && g_schedule != MXGG_SCHED_TILES;
+  const bool split_tail = split_ok && cfg.schedule != MXGG_SCHED_TILES;
 
   // 1) pack the row-major scales into the atoms the GEMM loads
   {
@@ -488,10 +531,10 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     p.out_rows_dst[0] = out_rows;
     p.self_src = -1;
   }
-  p.group_m = pick_group_m(tc);
+  p.group_m = pick_group_m(tc, cfg);
   p.accumulate = accumulate ? 1 : 0;
   p.split_tail = split_tail ? 1 : 0;
-  p.split_max = g_split_max;
+  p.split_max = cfg.split_max;
   p.part_slots = part_slots;
   p.part_counters = part_counters;
   p.status = st->status;
@@ -592,6 +635,15 @@ int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const voi
                   workspace_bytes, stream);
 }
 
+int mxgg_grouped_mm_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                        const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E, void* out,
+                        int out_dtype, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                        void* stream) {
+  return run_gemm(kFwd, a, b, a_scale, b_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, nullptr, -1, "mxgg_grouped_mm_cfg", nullptr, MXGG_FMT_E4M3, false,
+                  nullptr, config);
+}
+
 int64_t mxgg_grouped_mm_segments_workspace_size(int64_t M, int64_t N, int64_t K, int64_t n_segments,
                                                 int64_t n_experts) {
   if (M < 0 || N < 0 || K < 0 || n_segments < 1 || n_experts < 1) return -1;
@@ -606,6 +658,34 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
   return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
                   workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments", nullptr,
                   b_format);
+}
+
+int mxgg_grouped_mm_segments_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                                 const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M,
+                                 int64_t N, int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format,
+                                 void* out, int out_dtype, const mxgg_gemm_config* config, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+  if (!segment_expert && n_segments > 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_grouped_mm_segments_cfg: null segment_expert");
+  return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, segment_expert, n_experts, "mxgg_grouped_mm_segments_cfg", nullptr,
+                  b_format, false, nullptr, config);
+}
+
+int mxgg_grouped_mm_mx_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                           const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                           int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out,
+                           int out_dtype, void* q_out, void* q_scales, void* qt_out, void* qt_scales,
+                           const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes, void* stream) {
+  QuantOut q;
+  q.data = q_out;
+  q.scales = q_scales;
+  q.tdata = qt_out;
+  q.tscales = qt_scales;
+  q.only = out == nullptr;
+  return run_gemm(kFwd, a, b, a_scale, b_scale, segment_end_offsets, M, N, K, n_segments, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, segment_expert, segment_expert ? n_experts : n_segments,
+                  "mxgg_grouped_mm_mx_cfg", nullptr, b_format, false, &q, config);
 }
 
 int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const void* b_scale,
@@ -662,6 +742,15 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
                int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
                   workspace_bytes, stream);
+}
+
+int mxgg_wgrad_cfg(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                   const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
+                   int out_dtype, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                   void* stream) {
+  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, out_dtype, workspace,
+                  workspace_bytes, stream, true, nullptr, -1, "mxgg_wgrad_cfg", nullptr, MXGG_FMT_E4M3, false,
+                  nullptr, config);
 }
 
 int mxgg_quantize_mx_gather(const void* x, int x_dtype, int64_t in_rows, const int32_t* row_index, int64_t n_rows,
@@ -744,6 +833,15 @@ int mxgg_wgrad_accumulate(const void* go_t, const void* go_scale, const void* ia
   return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, MXGG_DTYPE_F32,
                   workspace, workspace_bytes, stream, true, nullptr, -1, "mxgg_wgrad_accumulate", nullptr,
                   MXGG_FMT_E4M3, true);
+}
+
+int mxgg_wgrad_accumulate_cfg(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                              const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E,
+                              float* out, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  return run_gemm(kWgrad, go_t, ia_t, go_scale, ia_scale, group_end_offsets, M, N, K, E, out, MXGG_DTYPE_F32,
+                  workspace, workspace_bytes, stream, true, nullptr, -1, "mxgg_wgrad_accumulate_cfg", nullptr,
+                  MXGG_FMT_E4M3, true, nullptr, config);
 }
 
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales, int mode,
@@ -854,7 +952,11 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
                   b_format, false, q_out ? &q : nullptr);
 }
 
-int32_t mxgg_query_tile_m(void) { return pick_tiles(256).tile_m; }
+int32_t mxgg_query_tile_m(void) {
+  GemmCfg cfg;
+  resolve_cfg(nullptr, &cfg, "mxgg_query_tile_m");
+  return pick_tiles(256, cfg).tile_m;
+}
 
 int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments) {
   if (M < 0 || K < 0 || n_segments < 1) return -1;
@@ -1025,26 +1127,19 @@ int mxgg_build_tile_map(const int32_t* offs, int64_t E, int64_t M, int32_t block
 }
 
 int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m) {
-  if (tile_m != 0 && tile_m != 128 && tile_m != 256)
-    return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: tile_m must be 0, 128 or 256");
-  if (tile_n != 0 && tile_n != 128 && tile_n != 256)
-    return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: tile_n must be 0, 128 or 256");
-  if (group_m < 0) return fail(MXGG_ERR_INVALID, "mxgg_set_tile_config: group_m must be >= 0");
+  if (int rc = check_cfg_fields(tile_m, tile_n, group_m, MXGG_SCHED_DEFAULT, 0, "mxgg_set_tile_config")) return rc;
   std::lock_guard<std::mutex> lk(g_mu);
-  g_tile_m = tile_m;
-  g_tile_n = tile_n;
-  g_group_m = group_m;
+  g_default_cfg.tile_m = tile_m;
+  g_default_cfg.tile_n = tile_n;
+  g_default_cfg.group_m = group_m;
   return MXGG_OK;
 }
 
 int mxgg_set_schedule(int32_t schedule, int32_t split_max) {
-  if (schedule != MXGG_SCHED_DEFAULT && schedule != MXGG_SCHED_TILES && schedule != MXGG_SCHED_SPLIT_TAIL)
-    return fail(MXGG_ERR_INVALID, "mxgg_set_schedule: unknown schedule %d", (int)schedule);
-  if (split_max < 0 || split_max == 1 || split_max > 64)
-    return fail(MXGG_ERR_INVALID, "mxgg_set_schedule: split_max must be 0 (automatic) or 2..64");
+  if (int rc = check_cfg_fields(0, 0, 0, schedule, split_max, "mxgg_set_schedule")) return rc;
   std::lock_guard<std::mutex> lk(g_mu);
-  g_schedule = schedule;
-  g_split_max = split_max;
+  g_default_cfg.schedule = schedule;
+  g_default_cfg.split_max = split_max;
   return MXGG_OK;
 }
 

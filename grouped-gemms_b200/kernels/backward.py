@@ -46,9 +46,9 @@ def triton_mxfp8_wgrad(
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
-    cfg = _tune.pick("wgrad", group_end_offsets.shape[0], go_t.shape[0], ia_t.shape[0])
-    with _tune.applied(cfg):
-        if out is not None:
-            mxgg.ops.wgrad_accumulate(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out)
-            return out
-        return mxgg.ops.wgrad(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype)
+    # a tuned config for this call shape (mxgg.tune), passed with the call
+    cfg = _tune.call_config(_tune.pick("wgrad", group_end_offsets.shape[0], go_t.shape[0], ia_t.shape[0]))
+    if out is not None:
+        mxgg.ops.wgrad_accumulate(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out, cfg)
+        return out
+    return mxgg.ops.wgrad(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype, cfg)

@@ -66,13 +66,14 @@ def triton_mxfp8_grouped_mm(
     if weight.dtype == torch.float4_e2m1fn_x2:
         assert K == 2 * K2, f"K mismatch: A={K}, B={2 * K2} (e2m1 packed)"
         experts = torch.arange(E, dtype=torch.int32, device=weight.device)
-        with _tune.applied(_tune.pick("fwd", E, N, K)):
-            return mxgg.ops.grouped_mm_segments(input_act, weight, input_act_scales, weight_scales,
-                                                 group_end_offsets, experts, out_dtype)
+        return mxgg.ops.grouped_mm_segments(input_act, weight, input_act_scales, weight_scales,
+                                            group_end_offsets, experts, out_dtype,
+                                            _tune.call_config(_tune.pick("fwd", E, N, K)))
     assert K == K2, f"K mismatch: A={K}, B={K2}"
-    # a tuned config for this call shape (mxgg.tune), else the library's choice
-    with _tune.applied(_tune.pick("fwd", E, N, K)):
-        return mxgg.ops.grouped_mm(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype)
+    # a tuned config for this call shape (mxgg.tune), passed with the call;
+    # None: the library's choice
+    return mxgg.ops.grouped_mm(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype,
+                               _tune.call_config(_tune.pick("fwd", E, N, K)))
 
 
 def mxfp8_grouped_mm_to_mx(
@@ -107,8 +108,8 @@ def mxfp8_grouped_mm_to_mx(
     E, N, K2 = weight.shape
     packed = weight.dtype == torch.float4_e2m1fn_x2
     assert K == (2 * K2 if packed else K2), f"K mismatch: A={K}, B={2 * K2 if packed else K2}"
-    with _tune.applied(_tune.pick("fwd", E, N, K)):
-        s, q, st, qt, out = mxgg.ops.grouped_mm_mx(input_act, weight, input_act_scales, weight_scales,
-                                                   group_end_offsets, None, out_dtype, return_output, True, dim1)
+    s, q, st, qt, out = mxgg.ops.grouped_mm_mx(input_act, weight, input_act_scales, weight_scales,
+                                               group_end_offsets, None, out_dtype, return_output, True, dim1,
+                                               _tune.call_config(_tune.pick("fwd", E, N, K)))
     res = (s, q, st, qt) if dim1 else (s, q)
     return res + (out,) if return_output else res

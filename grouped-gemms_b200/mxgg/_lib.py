@@ -43,15 +43,42 @@ SCALE_ROW_MAJOR, SCALE_BLOCKED = 0, 1
 SCHED_DEFAULT, SCHED_TILES, SCHED_SPLIT_TAIL = 0, 1, 2
 FMT_E4M3, FMT_E2M1 = 0, 1
 
+
+
+class GemmConfig(ctypes.Structure):
+    """``mxgg_gemm_config``: a call's tile and schedule choice (0 = the
+    process default, which defaults to the library's heuristic)."""
+    _fields_ = [("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("group_m", ctypes.c_int32),
+                ("schedule", ctypes.c_int32), ("split_max", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
+def gemm_config(cfg):
+    """A pointer to a GemmConfig for `cfg` -- a (tile_m, tile_n, group_m,
+    schedule, split_max) sequence -- or None for the process defaults."""
+    if cfg is None:
+        return None
+    return ctypes.pointer(GemmConfig(*[int(v) for v in cfg]))
+
+
 # every symbol include/mxgg.h declares, with (restype, argtypes)
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
 _int = ctypes.c_int
+_cfg = ctypes.POINTER(GemmConfig)
 SIGNATURES = {
     "mxgg_grouped_mm_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "mxgg_wgrad_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "mxgg_grouped_mm": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
+    "mxgg_grouped_mm_cfg": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _cfg, _vp, _i64,
+                                   _vp]),
+    "mxgg_wgrad_cfg": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _cfg, _vp, _i64, _vp]),
+    "mxgg_grouped_mm_segments_cfg": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp,
+                                            _int, _cfg, _vp, _i64, _vp]),
+    "mxgg_grouped_mm_mx_cfg": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int,
+                                      _vp, _vp, _vp, _vp, _cfg, _vp, _i64, _vp]),
+    "mxgg_wgrad_accumulate_cfg": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _cfg, _vp, _i64,
+                                         _vp]),
     "mxgg_wgrad": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _vp]),
     "mxgg_grouped_mm_segments_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "mxgg_grouped_mm_segments": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _int,

@@ -8,7 +8,7 @@ tensors raise.
 """
 
 import ctypes
-from typing import Optional, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 from torch import Tensor
@@ -155,7 +155,9 @@ def _(x, scale_layout):
 
 # ---------------------------------------------------------------- grouped_mm
 def _grouped_mm_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
-                  out_dtype: torch.dtype) -> Tensor:
+                  out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
+    """cfg: this call's (tile_m, tile_n, group_m, schedule, split_max), zeros
+    for the process defaults (mxgg_gemm_config); None: all defaults."""
     _require_cuda(a, b, a_scale, b_scale, offs, what="mxgg::grouped_mm")
     if out_dtype not in _OUT_DTYPES:
         raise TypeError(f"mxgg::grouped_mm: unsupported out_dtype {out_dtype}")
@@ -170,9 +172,9 @@ def _grouped_mm_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, off
     lib = _lib.load()
     ws = _workspace(lib.mxgg_grouped_mm_workspace_size(M, N, K, E), a.device)
     with torch.cuda.device(a.device):
-        _lib.check(lib.mxgg_grouped_mm(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
-                                       M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(),
-                                       _stream(a.device)), "mxgg_grouped_mm")
+        _lib.check(lib.mxgg_grouped_mm_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
+                                           M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                           _ptr(ws), ws.numel(), _stream(a.device)), "mxgg_grouped_mm")
     return out
 
 
@@ -181,13 +183,13 @@ grouped_mm = _fast(grouped_mm_op, _grouped_mm_impl)
 
 
 @grouped_mm_op.register_fake
-def _(a, b, a_scale, b_scale, offs, out_dtype):
+def _(a, b, a_scale, b_scale, offs, out_dtype, cfg=None):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
 # ------------------------------------------------------- grouped_mm_segments
 def _grouped_mm_segments_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
-                           seg_expert: Tensor, out_dtype: torch.dtype) -> Tensor:
+                           seg_expert: Tensor, out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
     """Rows of segment s times B[seg_expert[s]]: the layout an expert-parallel
     all-to-all delivers (source-major, then expert)."""
     _require_cuda(a, b, a_scale, b_scale, seg_offs, seg_expert, what="mxgg::grouped_mm_segments")
@@ -207,9 +209,10 @@ def _grouped_mm_segments_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Te
     lib = _lib.load()
     ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), a.device)
     with torch.cuda.device(a.device):
-        _lib.check(lib.mxgg_grouped_mm_segments(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
-                                                _ptr(seg_expert), M, N, K, S, E, b_format, _ptr(out),
-                                                _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(), _stream(a.device)),
+        _lib.check(lib.mxgg_grouped_mm_segments_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale),
+                                                    _ptr(seg_offs), _ptr(seg_expert), M, N, K, S, E, b_format,
+                                                    _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                                    _ptr(ws), ws.numel(), _stream(a.device)),
                    "mxgg_grouped_mm_segments")
     return out
 
@@ -220,13 +223,14 @@ grouped_mm_segments = _fast(grouped_mm_segments_op, _grouped_mm_segments_impl)
 
 
 @grouped_mm_segments_op.register_fake
-def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype):
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, cfg=None):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
 def _grouped_mm_mx_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
                      seg_expert: Optional[Tensor], out_dtype: torch.dtype, keep_out: bool, rows: bool = True,
-                     cols: bool = False) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+                     cols: bool = False, cfg: Optional[List[int]] = None) -> Tuple[Tensor, Tensor, Tensor, Tensor,
+                                                                                  Tensor]:
     """The forward (segments as in grouped_mm_segments_op; seg_expert None:
     segment s uses expert s) with MX quantisation of its output fused into
     the epilogue.  Returns (scales, data, scales_t, data_t, out):
@@ -268,11 +272,11 @@ def _grouped_mm_mx_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, 
     lib = _lib.load()
     ws = _workspace(lib.mxgg_grouped_mm_segments_workspace_size(M, N, K, S, E), dev)
     with torch.cuda.device(dev):
-        _lib.check(lib.mxgg_grouped_mm_mx(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
-                                          _ptr(seg_expert) if seg_expert is not None else None, M, N, K, S, E,
-                                          b_format, opt(out, keep_out), _OUT_DTYPES[out_dtype], opt(q, rows),
-                                          opt(s, rows), opt(qt, cols), opt(st, cols), _ptr(ws), ws.numel(),
-                                          _stream(dev)),
+        _lib.check(lib.mxgg_grouped_mm_mx_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
+                                              _ptr(seg_expert) if seg_expert is not None else None, M, N, K, S, E,
+                                              b_format, opt(out, keep_out), _OUT_DTYPES[out_dtype], opt(q, rows),
+                                              opt(s, rows), opt(qt, cols), opt(st, cols), _lib.gemm_config(cfg),
+                                              _ptr(ws), ws.numel(), _stream(dev)),
                    "mxgg_grouped_mm_mx")
     return s, q, st, qt, out
 
@@ -282,7 +286,7 @@ grouped_mm_mx = _fast(grouped_mm_mx_op, _grouped_mm_mx_impl)
 
 
 @grouped_mm_mx_op.register_fake
-def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False):
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False, cfg=None):
     M, N = a.shape[0], b.shape[1]
     e = lambda shape, on, dt: a.new_empty(shape if on else (0,), dtype=dt)  # noqa: E731
     return (e((M, N // 32), rows, torch.uint8), e((M, N), rows, torch.float8_e4m3fn),
@@ -292,7 +296,7 @@ def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=Tr
 
 # --------------------------------------------------------------------- wgrad
 def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
-             out_dtype: torch.dtype) -> Tensor:
+             out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, what="mxgg::wgrad")
     if out_dtype not in _OUT_DTYPES:
         raise TypeError(f"mxgg::wgrad: unsupported out_dtype {out_dtype}")
@@ -308,9 +312,9 @@ def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, 
     lib = _lib.load()
     ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
-        _lib.check(lib.mxgg_wgrad(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
-                                  N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _ptr(ws), ws.numel(),
-                                  _stream(go_t.device)), "mxgg_wgrad")
+        _lib.check(lib.mxgg_wgrad_cfg(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
+                                      N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                      _ptr(ws), ws.numel(), _stream(go_t.device)), "mxgg_wgrad")
     return out
 
 
@@ -319,12 +323,12 @@ wgrad = _fast(wgrad_op, _wgrad_impl)
 
 
 @wgrad_op.register_fake
-def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype):
+def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype, cfg=None):
     return go_t.new_empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype)
 
 
 def _wgrad_accumulate_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
-                        out: Tensor) -> None:
+                        out: Tensor, cfg: Optional[List[int]] = None) -> None:
     """out[g] += the group's weight gradient, in place (fp32 out)."""
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, out, what="mxgg::wgrad_accumulate_")
     N, M = go_t.shape
@@ -340,8 +344,9 @@ def _wgrad_accumulate_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scal
     lib = _lib.load()
     ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
-        _lib.check(lib.mxgg_wgrad_accumulate(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
-                                             N, K, M, E, _ptr(out), _ptr(ws), ws.numel(), _stream(go_t.device)),
+        _lib.check(lib.mxgg_wgrad_accumulate_cfg(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale),
+                                                 _ptr(offs), N, K, M, E, _ptr(out), _lib.gemm_config(cfg),
+                                                 _ptr(ws), ws.numel(), _stream(go_t.device)),
                    "mxgg_wgrad_accumulate")
 
 
@@ -351,7 +356,7 @@ wgrad_accumulate = _fast(wgrad_accumulate_op, _wgrad_accumulate_impl)
 
 
 @wgrad_accumulate_op.register_fake
-def _(go_t, go_scale, ia_t, ia_scale, offs, out):
+def _(go_t, go_scale, ia_t, ia_scale, offs, out, cfg=None):
     return None
 
 

@@ -23,8 +23,9 @@ A table is JSON: ``{"device": ..., "entries": [{"pass": "fwd", "E": 8,
 keyed on the call: ("fwd", E, N, K) for ``triton_mxfp8_grouped_mm`` with
 weight (E, N, K) -- dgrad included, as the forward call with N and K swapped
 -- and ("wgrad", E, N, K) for ``triton_mxfp8_wgrad`` with output (E, N, K).
-``install(table)`` makes those entry points look up their call before each
-call.  The environment variable ``MXGG_TUNE_TABLE``
+``install(table)`` makes those entry points look up their call and pass the
+entry's config with the call itself (``mxgg_gemm_config``): no process-wide
+setting changes, so threads issuing differently tuned GEMMs do not race.  The environment variable ``MXGG_TUNE_TABLE``
 names a table to install at import.  Without an entry, the library's own
 heuristic applies.
 
@@ -32,7 +33,6 @@ heuristic applies.
 """
 
 import argparse
-import contextlib
 import json
 import os
 import tempfile
@@ -59,6 +59,10 @@ class Config:
     schedule: int = _lib.SCHED_DEFAULT
     split_max: int = 0
 
+    def as_list(self) -> List[int]:
+        """The fields in ``mxgg_gemm_config`` order."""
+        return [self.tile_m, self.tile_n, self.group_m, self.schedule, self.split_max]
+
     def valid(self) -> bool:
         return (self.tile_m in (0, 128, 256) and self.tile_n in (0, 128, 256) and self.group_m >= 0
                 and self.schedule in (_lib.SCHED_DEFAULT, _lib.SCHED_TILES, _lib.SCHED_SPLIT_TAIL)
@@ -82,29 +86,15 @@ def config_space(tile_ms: Sequence[int] = (256, 128), tile_ns: Sequence[int] = (
     return out
 
 
-def _set(cfg: Config) -> None:
-    _lib.set_tile_config(cfg.tile_m, cfg.tile_n, cfg.group_m)
-    _lib.set_schedule(cfg.schedule, cfg.split_max)
-
-
-@contextlib.contextmanager
-def applied(cfg: Optional[Config]):
-    """Run the body with `cfg` in force (None: as is), then restore the
-    config that was set before (`mxgg.set_tile_config` / `set_schedule`).
-    The library reads its config on the host while it enqueues a call, so
-    restoring right after the call is safe.  The config is process-wide:
-    threads that issue GEMMs concurrently share it."""
+def call_config(cfg: Optional[Config]) -> Optional[List[int]]:
+    """The per-call config argument of the mxgg ops for `cfg` (None: the
+    process defaults).  Nothing process-wide is changed: the library takes the
+    config with the call (``mxgg_gemm_config``)."""
     if cfg is None:
-        yield
-        return
+        return None
     if not cfg.valid():
         raise ValueError(f"invalid config {cfg}")
-    (tm, tn, gm), (sch, smax) = _lib.current_config()
-    _set(cfg)
-    try:
-        yield
-    finally:
-        _set(Config(tm, tn, gm, sch, smax))
+    return cfg.as_list()
 
 
 # ------------------------------------------------------------------ tables
@@ -209,15 +199,15 @@ def best(times: Dict[Config, float]) -> Tuple[Config, float]:
     return cfg, times[cfg]
 
 
-def tune_point(run: Callable[[], object], configs: Iterable[Config],
+def tune_point(run: Callable[[Optional[List[int]]], object], configs: Iterable[Config],
                timer: Callable[[Callable[[], object]], float]) -> Dict[Config, float]:
-    """Seconds per call of `run` under each config (a config the library
-    rejects is skipped)."""
+    """Seconds per call of `run(config)` under each config, the config passed
+    with the call (a config the library rejects is skipped)."""
     out: Dict[Config, float] = {}
     for cfg in configs:
+        c = call_config(cfg)
         try:
-            with applied(cfg):
-                out[cfg] = timer(run)
+            out[cfg] = timer(lambda: run(c))
         except _lib.MxggError:
             continue
     return out
@@ -252,24 +242,26 @@ def cuda_timer(reps: int = 10, warmup: int = 3, flush_bytes: int = 512 << 20):
 def build_point(pass_: str, E: int, M: int, N: int, K: int, seed: int = 123):
     """Quantised operands of one call shape ("fwd": out (M, N) over K;
     "wgrad": out (E, N, K) over M tokens), offsets as the reference draws them
-    (utils.generate_jagged_offs, multiples of 32), and the call to time."""
+    (utils.generate_jagged_offs, multiples of 32), and the call to time as a
+    function of its config."""
     import random
 
     import torch
 
-    import kernels
     import utils
+
+    from . import ops
     random.seed(seed + E)
     g = torch.Generator(device="cuda").manual_seed(seed)
     offs = utils.generate_jagged_offs(E, M, multiple_of=32, device="cuda")
     if pass_ == "fwd":
         a_s, a_q = utils.to_mx(torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g))
         b_s, b_q = utils.to_mx(torch.randn(E, N, K, device="cuda", dtype=torch.bfloat16, generator=g))
-        return lambda: kernels.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, offs)
+        return lambda cfg: ops.grouped_mm(a_q, b_q, a_s, b_s, offs, torch.bfloat16, cfg)
     if pass_ == "wgrad":
         go_s, go_q = utils.to_mx_dim1(torch.randn(M, N, device="cuda", dtype=torch.bfloat16, generator=g))
         ia_s, ia_q = utils.to_mx_dim1(torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g))
-        return lambda: kernels.triton_mxfp8_wgrad(go_q, go_s, ia_q, ia_s, offs)
+        return lambda cfg: ops.wgrad(go_q, go_s, ia_q, ia_s, offs, torch.bfloat16, cfg)
     raise ValueError(f"unknown pass {pass_}")
 
 

@@ -50,6 +50,29 @@ extern "C" {
 #define MXGG_FMT_E2M1 1 /* MXFP4: two e2m1 values per byte, element 2i in the low nibble */
 
 /*
+ * Per-call kernel configuration for the *_cfg entry points (no counterpart in
+ * the reference, whose Triton wrappers take BLOCK_* / GROUP_M keywords per
+ * call, forward.py:461-484).  A field left 0 takes the process default set
+ * by mxgg_set_tile_config / mxgg_set_schedule, and those default to the
+ * library's own choice.  The struct is read during the call only; two
+ * threads may issue differently configured GEMMs concurrently.
+ *   tile_m     128: one CTA per output tile; 256: a CTA pair (cta_group::2)
+ *   tile_n     128 or 256 output columns per tile
+ *   group_m    rasterisation band, in row tiles (>= 1)
+ *   schedule   MXGG_SCHED_TILES or MXGG_SCHED_SPLIT_TAIL (see mxgg_set_schedule)
+ *   split_max  most pieces per split tile (2..64)
+ *   reserved   must be zero
+ */
+typedef struct mxgg_gemm_config {
+  int32_t tile_m;
+  int32_t tile_n;
+  int32_t group_m;
+  int32_t schedule;
+  int32_t split_max;
+  int32_t reserved[3];
+} mxgg_gemm_config;
+
+/*
  * Scratch ("workspace") for one grouped-GEMM call: the row-major scales are
  * re-laid into the 128x4 atoms the tensor cores read, one atom per 128-row
  * slab and 128-element contraction stage (the reference re-lays its scales on
@@ -76,6 +99,12 @@ int64_t mxgg_wgrad_workspace_size(int64_t N, int64_t K, int64_t M, int64_t E);
 int mxgg_grouped_mm(const void* a, const void* b, const void* a_scale, const void* b_scale,
                     const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E,
                     void* out, int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+/* mxgg_grouped_mm with its own tile and schedule choice (config may be null:
+ * the process defaults).  The same workspace size serves every config. */
+int mxgg_grouped_mm_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                        const int32_t* group_end_offsets, int64_t M, int64_t N, int64_t K, int64_t E, void* out,
+                        int out_dtype, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                        void* stream);
 
 /*
  * Forward / dgrad grouped GEMM that allocates nothing and takes no workspace.
@@ -124,6 +153,11 @@ int mxgg_grouped_mm_segments(const void* a, const void* b, const void* a_scale, 
                              const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
                              int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out,
                              int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+int mxgg_grouped_mm_segments_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                                 const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M,
+                                 int64_t N, int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format,
+                                 void* out, int out_dtype, const mxgg_gemm_config* config, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
 
 /*
  * Forward with the output's MX quantisation fused into the epilogue: as
@@ -151,6 +185,11 @@ int mxgg_grouped_mm_mx(const void* a, const void* b, const void* a_scale, const 
                        int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out, int out_dtype,
                        void* q_out, void* q_scales, void* qt_out, void* qt_scales, void* workspace,
                        int64_t workspace_bytes, void* stream);
+int mxgg_grouped_mm_mx_cfg(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                           const int32_t* segment_end_offsets, const int32_t* segment_expert, int64_t M, int64_t N,
+                           int64_t K, int64_t n_segments, int64_t n_experts, int32_t b_format, void* out,
+                           int out_dtype, void* q_out, void* q_scales, void* qt_out, void* qt_scales,
+                           const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Expert-parallel forward with the combine fused into the epilogue: as
@@ -258,6 +297,10 @@ int mxgg_peer_barrier(void* const* flags, int32_t world, int32_t rank, int32_t e
 int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
                const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
                int out_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+int mxgg_wgrad_cfg(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                   const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, void* out,
+                   int out_dtype, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                   void* stream);
 
 /*
  * mxgg_wgrad, accumulating: out[g] += GO_t[:, group g] @ X_t[:, group g]^T
@@ -270,6 +313,10 @@ int mxgg_wgrad(const void* go_t, const void* go_scale, const void* ia_t, const v
 int mxgg_wgrad_accumulate(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
                           const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E, float* out,
                           void* workspace, int64_t workspace_bytes, void* stream);
+int mxgg_wgrad_accumulate_cfg(const void* go_t, const void* go_scale, const void* ia_t, const void* ia_scale,
+                              const int32_t* group_end_offsets, int64_t N, int64_t K, int64_t M, int64_t E,
+                              float* out, const mxgg_gemm_config* config, void* workspace, int64_t workspace_bytes,
+                              void* stream);
 
 /*
  * MX quantiser, FLOOR scaling, e4m3 elements, 32-element blocks.
@@ -317,12 +364,14 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
 int mxgg_build_tile_map(const int32_t* group_end_offsets, int64_t E, int64_t M, int32_t block_m, int32_t* out,
                         void* stream);
 
-/* Tile configuration for later GEMM calls on this process (0 = automatic):
- * tile_m in {128 (one CTA per tile), 256 (a CTA pair per tile)},
- * tile_n in {128, 256}, group_m >= 1 rasterisation band in m-tiles. */
+/* Process default tile configuration (0 = automatic): tile_m in {128 (one
+ * CTA per tile), 256 (a CTA pair per tile)}, tile_n in {128, 256},
+ * group_m >= 1 rasterisation band in m-tiles.  Every call takes a snapshot
+ * of the defaults under a lock; a call's own mxgg_gemm_config overrides
+ * them, which is how concurrent callers choose different configs. */
 int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m);
 
-/* Work schedule of later GEMM calls on this process.  Output tiles are
+/* Process default work schedule (a call's mxgg_gemm_config overrides it).  Output tiles are
  * dealt to the persistent CTA pairs in rounds; with SPLIT_TAIL (the default)
  * the tiles of the last, partial round are cut along the contraction into
  * pieces for the pairs that would otherwise idle, and the last piece to

@@ -40,6 +40,19 @@ def test_jagged_offsets_sequence(golden):
     np.testing.assert_array_equal(lens, golden["llama4_offs_lens"])
 
 
+def test_product_jagged_offsets_sequence(golden):
+    """The product's generate_jagged_offs (the one bench.py draws with) replays
+    the reference bench's seeded sequence: random.seed(123), then one draw per
+    Llama4 shape in the reference's order (bench.py:243-257)."""
+    import random
+
+    import utils
+    random.seed(123)
+    draws = [utils.generate_jagged_offs(e, m, 32, device="cpu").numpy() for (e, m, n, k) in O.llama4_shapes()]
+    np.testing.assert_array_equal(np.concatenate(draws), golden["llama4_offs"])
+    np.testing.assert_array_equal([len(d) for d in draws], golden["llama4_offs_lens"])
+
+
 def test_grouped_mm_emulation(golden):
     out = O.grouped_mm(golden["fwd1_a_q"], golden["fwd1_a_s"], golden["fwd1_b_q"],
                        golden["fwd1_b_s"], golden["fwd1_offs"])

@@ -1,6 +1,6 @@
-"""Autotune harness host logic (no GPU): the candidate space, applying and
-restoring a config through the C ABI, best-config selection, dealing points
-to GPUs, and the table's JSON round trip, merge and lookup."""
+"""Autotune harness host logic (no GPU): the candidate space, per-call
+configs through the C ABI, best-config selection, dealing points to GPUs,
+and the table's JSON round trip, merge and lookup."""
 import json
 import os
 import tempfile
@@ -19,63 +19,81 @@ def test_config_space_is_valid_and_distinct():
     assert not tune.Config(tile_m=192).valid() and not tune.Config(split_max=1).valid()
 
 
-def test_applied_sets_then_restores(monkeypatch):
-    calls = []
-    monkeypatch.setattr(_lib, "set_tile_config", lambda *a: calls.append(("tile",) + a))
-    monkeypatch.setattr(_lib, "set_schedule", lambda *a: calls.append(("sched",) + a))
-    cfg = tune.Config(128, 256, 4, _lib.SCHED_TILES, 0)
-    with tune.applied(cfg):
-        assert calls == [("tile", 128, 256, 4), ("sched", _lib.SCHED_TILES, 0)]
-    assert calls[2:] == [("tile", 0, 0, 0), ("sched", _lib.SCHED_DEFAULT, 0)]
-    calls.clear()
-    with tune.applied(None):
-        pass
-    assert calls == []
+def test_call_config_is_passed_per_call(monkeypatch):
+    # a tuned config travels with the call: nothing process-wide is touched
+    def boom(*a):
+        raise AssertionError("process-wide setter called")
+    monkeypatch.setattr(_lib, "set_tile_config", boom)
+    monkeypatch.setattr(_lib, "set_schedule", boom)
+    assert tune.call_config(None) is None
+    assert tune.call_config(tune.Config(128, 256, 4, _lib.SCHED_TILES, 0)) == [128, 256, 4, _lib.SCHED_TILES, 0]
     with pytest.raises(ValueError):
-        with tune.applied(tune.Config(tile_n=64)):
-            pass
+        tune.call_config(tune.Config(tile_n=64))
 
 
-def test_applied_restores_after_an_error(monkeypatch):
-    calls = []
-    monkeypatch.setattr(_lib, "set_tile_config", lambda *a: calls.append(a))
-    monkeypatch.setattr(_lib, "set_schedule", lambda *a: None)
-    with pytest.raises(RuntimeError):
-        with tune.applied(tune.Config(256, 128, 8)):
-            raise RuntimeError("call failed")
-    assert calls[-1] == (0, 0, 0)
+def test_wrappers_pass_the_installed_entry(monkeypatch):
+    import torch
+
+    import kernels
+    import mxgg
+    from kernels import backward, forward
+    seen = {}
+    monkeypatch.setattr(forward, "_mxfp8_available", True)
+    monkeypatch.setattr(backward, "_mxfp8_available", True)
+    monkeypatch.setattr(mxgg.ops, "grouped_mm", lambda *a: seen.setdefault("fwd", a[-1]))
+    monkeypatch.setattr(mxgg.ops, "wgrad", lambda *a: seen.setdefault("wgrad", a[-1]))
+    t = tune.Table()
+    t.add("fwd", 2, 256, 512, tune.Config(128, 128, 2, _lib.SCHED_TILES, 0), 1.0)
+    t.add("wgrad", 2, 256, 512, tune.Config(256, 256, 8, _lib.SCHED_SPLIT_TAIL, 3), 1.0)
+    tune.install(t)
+    try:
+        a = torch.zeros(64, 512, dtype=torch.float8_e4m3fn)
+        b = torch.zeros(2, 256, 512, dtype=torch.float8_e4m3fn)
+        offs = torch.tensor([32, 64], dtype=torch.int32)
+        kernels.triton_mxfp8_grouped_mm(a, b, torch.zeros(64, 16, dtype=torch.uint8),
+                                        torch.zeros(2, 256, 16, dtype=torch.uint8), offs)
+        kernels.triton_mxfp8_wgrad(torch.zeros(256, 64, dtype=torch.float8_e4m3fn), torch.zeros(256, 2, dtype=torch.uint8),
+                                   torch.zeros(512, 64, dtype=torch.float8_e4m3fn), torch.zeros(512, 2, dtype=torch.uint8),
+                                   offs)
+    finally:
+        tune.install(None)
+    assert seen == {"fwd": [128, 128, 2, _lib.SCHED_TILES, 0], "wgrad": [256, 256, 8, _lib.SCHED_SPLIT_TAIL, 3]}
 
 
-def test_applied_through_the_real_library():
-    # the setters need no GPU; an out-of-range value is rejected by the library
-    with tune.applied(tune.Config(128, 128, 2, _lib.SCHED_TILES, 0)):
-        pass
+def test_library_rejects_a_bad_call_config():
+    # validated before any device work, so no GPU is needed
+    lib = _lib.load()
+    for bad, word in [((64, 0, 0, 0, 0), "tile_m"), ((0, 96, 0, 0, 0), "tile_n"), ((0, 0, -1, 0, 0), "group_m"),
+                      ((0, 0, 0, 7, 0), "schedule"), ((0, 0, 0, 0, 1), "split_max")]:
+        rc = lib.mxgg_grouped_mm_cfg(None, None, None, None, None, 128, 128, 128, 1, None, _lib.DTYPE_BF16,
+                                     _lib.gemm_config(bad), None, 0, None)
+        assert rc == 1 and word in lib.mxgg_last_error().decode()
+    cfg = _lib.GemmConfig(0, 0, 0, 0, 0)
+    cfg.reserved[1] = 5
+    rc = lib.mxgg_wgrad_cfg(None, None, None, None, None, 128, 128, 128, 1, None, _lib.DTYPE_BF16,
+                            __import__("ctypes").pointer(cfg), None, 0, None)
+    assert rc == 1 and "reserved" in lib.mxgg_last_error().decode()
     with pytest.raises(_lib.MxggError):
         _lib.set_tile_config(64, 0, 0)
     _lib.set_tile_config(0, 0, 0)
 
 
-def test_tune_point_picks_the_fastest_and_skips_rejected(monkeypatch):
-    monkeypatch.setattr(_lib, "set_tile_config", lambda *a: None)
-    monkeypatch.setattr(_lib, "set_schedule", lambda *a: None)
+def test_tune_point_picks_the_fastest_and_skips_rejected():
     cfgs = tune.config_space()[:5]
-    fake = {cfgs[0]: 3.0, cfgs[1]: 1.0, cfgs[2]: 1.0, cfgs[4]: 2.0}
+    fake = {tuple(c.as_list()): t for c, t in [(cfgs[0], 3.0), (cfgs[1], 1.0), (cfgs[2], 1.0), (cfgs[4], 2.0)]}
     current = {}
 
-    def timer(run):
+    def run(cfg):
+        current["cfg"] = tuple(cfg)
+
+    def timer(fn):
+        fn()
         c = current["cfg"]
         if c not in fake:
             raise _lib.MxggError("rejected")
         return fake[c]
 
-    orig = tune.applied
-
-    def spy(cfg):
-        current["cfg"] = cfg
-        return orig(cfg)
-
-    monkeypatch.setattr(tune, "applied", spy)
-    times = tune.tune_point(lambda: None, cfgs, timer)
+    times = tune.tune_point(run, cfgs, timer)
     assert cfgs[3] not in times and len(times) == 4
     assert tune.best(times) == (cfgs[1], 1.0)      # tie with cfgs[2]: the first tried wins
 
@@ -137,14 +155,13 @@ def test_install_and_pick():
     assert tune.pick("fwd", 2, 256, 512) is None
 
 
-def test_applied_restores_the_callers_config():
-    """A config set by the caller (bench --tile-m, say) comes back after a
-    tuned call, not the library default."""
+def test_tuned_call_leaves_the_callers_defaults():
+    """A config set by the caller (bench --tile-m, say) stays in force around
+    a tuned call: the tuned entry travels with the call instead."""
     try:
         _lib.set_tile_config(128, 256, 4)
         _lib.set_schedule(_lib.SCHED_TILES, 0)
-        with tune.applied(tune.Config(256, 128, 16, _lib.SCHED_SPLIT_TAIL, 3)):
-            assert _lib.current_config() == ((256, 128, 16), (_lib.SCHED_SPLIT_TAIL, 3))
+        assert tune.call_config(tune.Config(256, 128, 16, _lib.SCHED_SPLIT_TAIL, 3)) == [256, 128, 16, 2, 3]
         assert _lib.current_config() == ((128, 256, 4), (_lib.SCHED_TILES, 0))
     finally:
         _lib.set_tile_config(0, 0, 0)
