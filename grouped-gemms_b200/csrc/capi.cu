@@ -65,6 +65,15 @@ struct GemmCfg {
   int split_max = 0;
 };
 GemmCfg g_default_cfg;   // guarded by g_mu
+// Limit of every bounded device-side wait (mbarriers, peers' flags, the
+// cross-GPU barrier), guarded by g_mu.
+constexpr unsigned long long kDefaultWaitNs = 1000000000ull;   // 1 s
+unsigned long long g_wait_ns = kDefaultWaitNs;
+
+unsigned long long wait_limit_ns() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_wait_ns;
+}
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -538,6 +547,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   p.part_slots = part_slots;
   p.part_counters = part_counters;
   p.status = st->status;
+  p.wait_ns = wait_limit_ns();
 
   Maps maps;
   if (int rc = make_tmap_2d(&maps.a, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_a, (uint64_t)C, (uint64_t)C,
@@ -1071,7 +1081,8 @@ int mxgg_peer_barrier(void* const* flags, int32_t world, int32_t rank, int32_t e
     if (!flags[i]) return fail(MXGG_ERR_INVALID, "mxgg_peer_barrier: null flag array of rank %d", i);
     f.flags[i] = static_cast<int*>(flags[i]);
   }
-  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch, st->status);
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch, st->status,
+                                                                      wait_limit_ns());
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
 }
@@ -1142,6 +1153,17 @@ int mxgg_set_schedule(int32_t schedule, int32_t split_max) {
   g_default_cfg.split_max = split_max;
   return MXGG_OK;
 }
+
+int mxgg_set_wait_limit(int64_t ns) {
+  if (ns < 0 || (ns > 0 && ns < 1000000) || ns > 60000000000ll)
+    return fail(MXGG_ERR_INVALID, "mxgg_set_wait_limit: %lld ns is outside 1 ms .. 60 s (0 restores 1 s)",
+                (long long)ns);
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_wait_ns = ns == 0 ? kDefaultWaitNs : (unsigned long long)ns;
+  return MXGG_OK;
+}
+
+int64_t mxgg_wait_limit(void) { return (int64_t)wait_limit_ns(); }
 
 int mxgg_device_status(uint32_t* status_out, int clear, void* stream_v) {
   DeviceState* st = nullptr;

@@ -15,17 +15,27 @@
 // half of the BN rows of B (plain TMA loads, no multicast), so every byte a
 // CTA pulls from L2 feeds twice the MMA work of a single-CTA tile.
 //
-// Warp roles (256 threads per CTA):
-//   warp 0      TMA producer: per stage the A and B tiles (128 B swizzle) and
-//               their scale atoms (pre-packed by pack_scales_kernel) into a
-//               STAGES ring, all completing on one transaction barrier
-//   warp 1      MMA issuer (the leader CTA's lane 0): tcgen05.cp of the scales
-//               into TMEM, then tcgen05.mma.kind::mxf8f6f4.block_scale (K=32)
-//   warp 3      builds the group table in the prologue
+// Warp roles (320 threads per CTA):
+//   warps 0-3   scale writers: per stage, the CTA's scale atoms (pre-packed by
+//               pack_scales_kernel, TMA-loaded into shared memory) go to a
+//               ring of scale slots in TMEM with tcgen05.st, warp q writing
+//               its own 32-lane quarter (the block-scaled MMA reads the same
+//               32-row atom from every quarter).  Moving the scales with
+//               tcgen05.cp instead puts three copies per stage into the
+//               tensor pipe's instruction stream, where they cost ~135 of a
+//               stage's ~490 MMA cycles (measured on B200); tcgen05.st from
+//               other warps leaves the pipe to the MMAs.  Warp 3 also builds
+//               the group table in the prologue.
 //   warps 4-7   epilogue: TMEM -> registers -> bf16/fp32 -> swizzled smem ->
 //               TMA store; ragged group edges fall back to predicated stores;
 //               on request also the MX-quantised rows and transpose (to_mx and
 //               to_mx_dim1 of the output) from the same registers
+//   warp 8      TMA producer: per stage the A and B tiles (128 B swizzle) into
+//               a STAGES ring on one transaction barrier (the pair's leader
+//               counts both CTAs' bytes), and this CTA's scale atoms on a
+//               barrier of its own
+//   warp 9      MMA issuer (the leader CTA's lane 0):
+//               tcgen05.mma.kind::mxf8f6f4.block_scale (K=32), four per stage
 //
 // Scheduling: a persistent grid (one CTA per SM) walks a device-built
 // group->tile map: every CTA reads the group end offsets once, builds the
@@ -44,7 +54,12 @@ namespace mxgg {
 
 constexpr int kBM = 128;          // rows per CTA (MMA M per CTA)
 constexpr int kBK = 128;          // contraction elements per stage (= one 128 B swizzle row of e4m3)
-constexpr int kThreads = 256;
+constexpr int kSfWarp0 = 0;       // scale writers: warps 0-3
+constexpr int kEpiWarp0 = 4;      // epilogue: warps 4-7
+constexpr int kProdWarp = 8;      // TMA producer
+constexpr int kMmaWarp = 9;       // MMA issuer
+constexpr int kThreads = 320;
+constexpr int kSfSlots = 5;       // scale slots in TMEM (stages the writers may run ahead)
 constexpr int kMaxGroups = 256;   // groups handled by the in-kernel table
 constexpr int kMaxDst = 8;        // output destinations (ranks) of an expert-parallel forward
 constexpr int kTmemCols = 512;
@@ -103,6 +118,7 @@ struct GemmParams {
   float* part_slots;         // split tiles: one fp32 128 x BN partial per CTA of the grid
   int* part_counters;        // split tiles: arrivals per (tail tile, CTA of the pair, epilogue warp), zeroed before the launch
   uint32_t* status;          // error word (device memory), 0 = ok
+  unsigned long long wait_ns;  // limit of every bounded wait (%globaltimer ns)
   // Expert-parallel output routing (fwd): group g's rows are stored to
   // destination group_dst[g] (an output buffer, possibly a peer GPU's) from
   // row group_dst_row[g] on.  Null group_dst: every group writes `out` at its
@@ -175,8 +191,11 @@ struct SmemLayout {
   alignas(1024) uint8_t epi[4][2][32 * 64];            // per epilogue warp, double buffered
   alignas(128) uint8_t sfa[STAGES][kBM * 4];
   alignas(128) uint8_t sfb[STAGES][BN * 4];             // full BN rows: each CTA's TMEM needs all of them
-  alignas(8) uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  alignas(8) uint64_t full[STAGES];   // A and B tiles landed (the leader's counts both CTAs)
+  uint64_t empty[STAGES];             // stage read by its MMAs (commit to both CTAs)
+  uint64_t sfl[STAGES];               // this CTA's scale atoms landed
+  uint64_t sft[kSfSlots];             // TMEM scale slot written (leader; every writer warp of the pair)
+  uint64_t sfe[kSfSlots];             // TMEM scale slot read by its MMAs (commit to both CTAs)
   uint64_t tfull[2];
   uint64_t tempty_ov[2];    // accumulator columns shared with the other buffer drained
   uint64_t tempty_all[2];   // whole accumulator drained
@@ -461,8 +480,8 @@ __device__ __forceinline__ void raise_error(const GemmParams& p, volatile int* a
   *abort = 1;
 }
 
-// Bounded wait (1 s of %globaltimer, or an abort) for source `src`'s rows;
-// then orders them before this thread's TMA (async-proxy) reads.
+// Bounded wait (p.wait_ns of %globaltimer, or an abort) for source `src`'s
+// rows; then orders them before this thread's TMA (async-proxy) reads.
 __device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volatile int* abort) {
   const int* flag = p.src_flags + src;
   const uint64_t t0 = ptx::globaltimer();
@@ -470,7 +489,7 @@ __device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volati
     int v;
     asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (v - p.src_epoch >= 0) break;
-    if (*abort || ptx::globaltimer() - t0 > 1000000000ull) return false;
+    if (*abort || ptx::globaltimer() - t0 > p.wait_ns) return false;
     __nanosleep(64);
   }
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -491,23 +510,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kChunks = BN / kEpiCols;       // epilogue chunks per accumulator
   constexpr int kTileM = kBM * PAIR;
   constexpr int kBRows = S::kBRows;
-  constexpr uint32_t kSfCols = 4 + BN / 32;
+  // TMEM columns of one scale slot: the A atom (4 columns: 128 rows x 4
+  // k-blocks, rows r, r+32, r+64, r+96 side by side in lane r % 32 of every
+  // quarter) and BN/128 B atoms
+  constexpr int kSfCols = 4 + BN / 32;
+  constexpr int kSfNeed = kSfSlots * kSfCols;
   // Accumulator buffers: buffer 1 starts kOv columns before the end of buffer
-  // 0 when two full buffers and the scale buffers do not fit in 512 columns
+  // 0 when two full buffers and the scale slots do not fit in 512 columns
   // (BN = 256).  The epilogue drains the shared columns first and releases
-  // them early, so the next tile's MMAs wait for one epilogue chunk, not for
-  // the whole drain.
-  constexpr int kOv = (2 * BN + 2 * kSfCols <= kTmemCols) ? 0 : kEpiCols * ((sizeof(OutT) == 4) ? 2 : 1);
+  // them early, so the next tile's MMAs wait for those epilogue chunks, not
+  // for the whole drain.
+  constexpr int kOv = (2 * BN + kSfNeed <= kTmemCols)
+                          ? 0 : (2 * BN + kSfNeed - kTmemCols + kEpiCols - 1) / kEpiCols * kEpiCols;
   constexpr int kAcc1 = BN - kOv;
-  constexpr int kSfaCol = kAcc1 + BN;          // two scale buffers follow the accumulators
-  static_assert(kSfaCol + 2 * kSfCols <= kTmemCols, "tensor memory budget");
-  // epilogue chunk drained first for each buffer (the shared columns)
+  constexpr int kSfCol0 = kAcc1 + BN;          // the scale slots follow the accumulators
+  static_assert(kSfCol0 + kSfNeed <= kTmemCols, "tensor memory budget");
+  // epilogue chunks drained first for each buffer (the shared columns)
   constexpr int kOvChunks = kOv / kEpiCols;
-  // bytes the leader's full barrier receives per stage (both CTAs' tiles and scale atoms)
-  // bytes one stage's loads deliver (the transaction count): e2m1 B tiles
-  // count their packed global bytes, half of the 8-bit-slot smem they fill
-  const uint32_t kStageBytes =
-      PAIR * (kBM * kBK + (p.b_fmt == 5 ? kBRows * kBK / 2 : kBRows * kBK) + kBM * 4 + BN * 4);
+  // bytes one stage's tile loads deliver to the leader's full barrier (the
+  // transaction count, both CTAs): e2m1 B tiles count their packed global
+  // bytes, half of the 8-bit-slot smem they fill
+  const uint32_t kStageBytes = PAIR * (kBM * kBK + (p.b_fmt == 5 ? kBRows * kBK / 2 : kBRows * kBK));
+  // bytes of this CTA's scale atoms per stage (its own barrier)
+  constexpr uint32_t kSfBytes = kBM * 4 + BN * 4;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   S* sm = reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -530,16 +555,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     else ptx::mbar_arrive(ptx::smem_u32(bar));
   };
   auto wait_leader_side = [&](const uint64_t* bar, uint32_t parity) -> bool {
-    if constexpr (PAIR == 2) return ptx::mbar_wait_cluster(ptx::smem_u32(bar), parity, abort);
-    else return ptx::mbar_wait(ptx::smem_u32(bar), parity, abort);
+    if constexpr (PAIR == 2) return ptx::mbar_wait_cluster(ptx::smem_u32(bar), parity, abort, p.wait_ns);
+    else return ptx::mbar_wait(ptx::smem_u32(bar), parity, abort, p.wait_ns);
+  };
+  // bounded wait on a barrier of this CTA
+  auto wait_local = [&](const uint64_t* bar, uint32_t parity) -> bool {
+    return ptx::mbar_wait(ptx::smem_u32(bar), parity, abort, p.wait_ns);
   };
 
   // ------------------------------------------------------------ prologue
-  if (warp == 0 && lane == 0) {
+  if (warp == kProdWarp && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       // the leader's producer arms it; every CTA's loads complete on it
       ptx::mbar_init(ptx::smem_u32(&sm->full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&sm->empty[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sm->sfl[s]), 1);
+    }
+    for (int j = 0; j < kSfSlots; ++j) {
+      ptx::mbar_init(ptx::smem_u32(&sm->sft[j]), 4 * PAIR);   // scale-writer warps of every CTA
+      ptx::mbar_init(ptx::smem_u32(&sm->sfe[j]), 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(ptx::smem_u32(&sm->tfull[a]), 1);
@@ -555,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmap_sfb);
     ptx::prefetch_tmap(&omaps.m[p.local_dst]);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     if constexpr (PAIR == 2) {
       ptx::tmem_alloc_pair(ptx::smem_u32(&sm->tmem_base), kTmemCols);
       ptx::tmem_relinquish_pair();
@@ -586,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = sm->tmem_base;
   const int num_units = sm->num_units;
 
-  if (warp == 0) {
+  if (warp == kProdWarp) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
@@ -607,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const int stage = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!ptx::mbar_wait(ptx::smem_u32(&sm->empty[stage]), ph ^ 1u, abort)) {
+          if (!wait_local(&sm->empty[stage], ph ^ 1u)) {
             raise_error(p, abort, kErrProducerWait);
             ok = false;
             break;
@@ -617,6 +651,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           // packed scale atoms: A [sub-tile][stage][512 B], B [tile][stage][BN/128 x 512 B]
           const int ya = ((u.a_sub + (int)rank) * p.stages + st) * 4;
           const int yb = (u.b_tile * p.stages + st) * 4 * (BN / 128);
+          // this CTA's scale atoms, on its own barrier (its scale writers wait there)
+          const uint32_t sb = ptx::smem_u32(&sm->sfl[stage]);
+          ptx::mbar_arrive_expect_tx(sb, kSfBytes);
+          ptx::tma_load_2d(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, sb, 0, ya);
+          ptx::tma_load_2d(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, sb, 0, yb);
           if constexpr (PAIR == 2) {
             const uint32_t fb = leader_bar(&sm->full[stage]);
             if (leader) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&sm->full[stage]), kStageBytes);
@@ -626,8 +665,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               ptx::tma_load_2d_pair(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row + kBM * (int)rank);
             ptx::tma_load_2d_pair(ptx::smem_u32(sm->b[stage]), &tmap_b, fb, x, u.b_row + kBRows * (int)rank);
-            ptx::tma_load_2d_pair(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, fb, 0, ya);
-            ptx::tma_load_2d_pair(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, fb, 0, yb);
           } else {
             const uint32_t fb = ptx::smem_u32(&sm->full[stage]);
             ptx::mbar_arrive_expect_tx(fb, kStageBytes);
@@ -636,8 +673,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row);
             ptx::tma_load_2d(ptx::smem_u32(sm->b[stage]), &tmap_b, fb, x, u.b_row);
-            ptx::tma_load_2d(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, fb, 0, ya);
-            ptx::tma_load_2d(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, fb, 0, yb);
           }
         }
       }
@@ -650,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0 && leader) {
       const uint32_t kIdesc = ptx::idesc_mxf8(kTileM, BN, 0, (uint32_t)p.b_fmt);
@@ -658,8 +693,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kBStep = (kBRows * kBK) >> 4;
       const uint64_t adesc0 = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->a[0]));
       const uint64_t bdesc0 = ptx::kmajor_sw128_desc(ptx::smem_u32(sm->b[0]));
-      const uint64_t sfadesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfa[0]));
-      const uint64_t sfbdesc0 = ptx::sf_copy_desc(ptx::smem_u32(sm->sfb[0]));
       uint32_t it = 0, ai = 0;
       bool ok = true;
       int k = 0;
@@ -683,26 +716,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < u.st_count; ++s, ++it) {
           const uint32_t stage = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!wait_leader_side(&sm->full[stage], ph)) {
+          const uint32_t slot = it % kSfSlots;
+          // the stage's tiles (both CTAs) and its scales in TMEM (every writer warp of the pair)
+          if (!wait_leader_side(&sm->full[stage], ph) ||
+              !wait_leader_side(&sm->sft[slot], (it / kSfSlots) & 1u)) {
             raise_error(p, abort, kErrMmaWait);
             ok = false;
             break;
           }
-          // scale factors of this stage -> TMEM (double-buffered so the copy
-          // never waits on the previous stage's MMAs)
-          const uint32_t sfa_t = tmem_base + kSfaCol + (it & 1u) * kSfCols;
+          ptx::tc_fence_after();
+          const uint32_t sfa_t = tmem_base + kSfCol0 + slot * kSfCols;
           const uint32_t sfb_t = sfa_t + 4;
-          const uint64_t sfa_src = sfadesc0 + (uint64_t)(stage * ((kBM * 4) >> 4));
-          const uint64_t sfb_src = sfbdesc0 + (uint64_t)(stage * ((BN * 4) >> 4));
-          if constexpr (PAIR == 2) {
-            ptx::tc_cp_32x128b_warpx4_pair(sfa_t, sfa_src);
-#pragma unroll
-            for (int b = 0; b < BN / 128; ++b) ptx::tc_cp_32x128b_warpx4_pair(sfb_t + 4 * b, sfb_src + b * (512 >> 4));
-          } else {
-            ptx::tc_cp_32x128b_warpx4(sfa_t, sfa_src);
-#pragma unroll
-            for (int b = 0; b < BN / 128; ++b) ptx::tc_cp_32x128b_warpx4(sfb_t + 4 * b, sfb_src + b * (512 >> 4));
-          }
           const uint64_t adesc = adesc0 + (uint64_t)(stage * kAStep);
           const uint64_t bdesc = bdesc0 + (uint64_t)(stage * kBStep);
           const int base = (u.st_begin + s) * kBK;
@@ -726,8 +750,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               accumulate = 1;
             }
           }
-          if constexpr (PAIR == 2) ptx::tc_commit_pair(ptx::smem_u32(&sm->empty[stage]), 0x3);
-          else ptx::tc_commit(ptx::smem_u32(&sm->empty[stage]));
+          // once these MMAs complete: the stage's buffers and the scale slot are free again
+          if constexpr (PAIR == 2) {
+            ptx::tc_commit_pair(ptx::smem_u32(&sm->empty[stage]), 0x3);
+            ptx::tc_commit_pair(ptx::smem_u32(&sm->sfe[slot]), 0x3);
+          } else {
+            ptx::tc_commit(ptx::smem_u32(&sm->empty[stage]));
+            ptx::tc_commit(ptx::smem_u32(&sm->sfe[slot]));
+          }
         }
         if (!ok) break;
         if constexpr (PAIR == 2) ptx::tc_commit_pair(ptx::smem_u32(&sm->tfull[acc]), 0x3);
@@ -737,9 +767,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (PAIR == 2) ptx::tc_commit_pair(ptx::smem_u32(&sm->drain), 0x1);
       else ptx::tc_commit(ptx::smem_u32(&sm->drain));
       volatile int never = 0;
-      if (!ptx::mbar_wait(ptx::smem_u32(&sm->drain), 0, &never)) atomicOr(p.status, kErrDrain);
+      if (!ptx::mbar_wait(ptx::smem_u32(&sm->drain), 0, &never, p.wait_ns)) atomicOr(p.status, kErrDrain);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     uint32_t ai = 0;
@@ -749,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
       const int acc = ai & 1;
       const uint32_t aph = (ai >> 1) & 1u;
-      if (!ptx::mbar_wait(ptx::smem_u32(&sm->tfull[acc]), aph, abort)) {
+      if (!wait_local(&sm->tfull[acc], aph)) {
         raise_error(p, abort, kErrEpilogueWait);
         break;
       }
@@ -1073,13 +1103,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     // expert parallel: peers read this GPU's stores after a system-scope flag
     if (p.n_dst > 1) __threadfence_system();
+  } else if (warp >= kSfWarp0 && warp < kSfWarp0 + 4) {
+    // ------------------------------------------------------- scale writers
+    // Lane l of warp q writes TMEM lane 32q + l of the stage's scale slot:
+    // row l of the A atom (4 columns) and of each B atom (4 columns each).
+    // Every quarter holds the same 32 x 16-byte atom rows, the layout the
+    // block-scaled MMA reads (rows r, r+32, r+64, r+96 in lane r % 32).
+    const int q = warp - kSfWarp0;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(32 * q) << 16) + kSfCol0;
+    uint32_t it = 0;
+    int k = 0;
+    Unit u;
+    bool ok = true;
+    while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
+      for (int s = 0; s < u.st_count; ++s, ++it) {
+        const int stage = it % STAGES;
+        const uint32_t slot = it % kSfSlots;
+        // the atoms are in shared memory, and the slot's previous MMAs are done
+        if (!wait_local(&sm->sfl[stage], (it / STAGES) & 1u) ||
+            !wait_local(&sm->sfe[slot], ((it / kSfSlots) & 1u) ^ 1u)) {
+          raise_error(p, abort, kErrScaleWait);
+          ok = false;
+          break;
+        }
+        const uint32_t taddr = lane_base + slot * kSfCols;
+        uint32_t a[4];
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                     : "r"(ptx::smem_u32(sm->sfa[stage]) + lane * 16)
+                     : "memory");
+        ptx::tmem_st_32x32b_x4(taddr, a);
+#pragma unroll
+        for (int b = 0; b < BN / 128; ++b) {
+          uint32_t w[4];
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                       : "r"(ptx::smem_u32(sm->sfb[stage]) + b * 512 + lane * 16)
+                       : "memory");
+          ptx::tmem_st_32x32b_x4(taddr + 4 + 4 * b, w);
+        }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) arrive_leader(&sm->sft[slot]);
+      }
+    }
   }
 
   // ------------------------------------------------------------ teardown
   ptx::tc_fence_before();
   __syncthreads();
   if constexpr (PAIR == 2) ptx::cluster_sync();   // the peer no longer touches this CTA's barriers or smem
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     if constexpr (PAIR == 2) ptx::tmem_dealloc_pair(tmem_base, kTmemCols);
     else ptx::tmem_dealloc(tmem_base, kTmemCols);

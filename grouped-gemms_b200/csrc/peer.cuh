@@ -5,8 +5,9 @@
 // until all `world` slots of its own array have reached `epoch` (acquire).
 // It runs as one small kernel per GPU, ordered on the stream after the work
 // it publishes (peer copies, the GEMM's peer stores) and before the work that
-// consumes what the peers published.  The wait is bounded (1 s of
-// %globaltimer); a timeout sets kErrPeerWait in the status word and returns.
+// consumes what the peers published.  The wait is bounded (wait_ns of
+// %globaltimer, 1 s by default); a timeout sets kErrPeerWait in the status
+// word and returns.
 #pragma once
 
 #include <cstdint>
@@ -23,7 +24,7 @@ struct PeerFlags {
 };
 
 __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerFlags f, int world, int rank, int epoch,
-                                                          uint32_t* status) {
+                                                          uint32_t* status, unsigned long long wait_ns) {
   const int t = threadIdx.x;
   // everything this stream did before (earlier kernels, copies) precedes the signal
   __threadfence_system();
@@ -39,7 +40,7 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerFlags f, int
       int v;
       asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(src) : "memory");
       if (v - epoch >= 0) break;   // epochs only grow
-      if (ptx::globaltimer() - t0 > 1000000000ull) {
+      if (ptx::globaltimer() - t0 > wait_ns) {
         atomicOr(status, kErrPeerWait);
         break;
       }

@@ -69,14 +69,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait on `bar` for the phase with parity `parity` to complete.
-// Returns false on timeout or when *abort becomes non-zero.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// Returns false after `limit_ns` of %globaltimer time or when *abort becomes
+// non-zero.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = MXGG_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((i & 255u) == 255u && globaltimer() - t0 > MXGG_WAIT_LIMIT_NS) return false;
+    if ((i & 255u) == 255u && globaltimer() - t0 > limit_ns) return false;
   }
 }
 
@@ -229,12 +231,6 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                : "memory");
 }
 
-// Copy a 32-row x 16-byte block of scale factors from shared memory into
-// tensor memory, replicated into the four 32-lane quarters.
-__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 // D(tmem) (+)= (A(smem) * SFA(tmem)) x (B(smem) * SFB(tmem))^T with e8m0 block
 // scales, one 32-wide K step.
 __device__ __forceinline__ void tc_mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -248,6 +244,16 @@ __device__ __forceinline__ void tc_mma_mxf8(uint32_t d_tmem, uint64_t a_desc, ui
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 4 columns of 32-bit values: thread t of the warp writes lane t.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+// every tcgen05.st this thread issued has completed
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 columns of 32-bit values: thread t of the warp gets lane t.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -315,13 +321,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 
 // Bounded wait with cluster-scope acquire (the barrier collects arrivals
 // from the peer CTA of a pair).
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                  uint64_t limit_ns = MXGG_WAIT_LIMIT_NS) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort) return false;
-    if ((i & 255u) == 255u && globaltimer() - t0 > MXGG_WAIT_LIMIT_NS) return false;
+    if ((i & 255u) == 255u && globaltimer() - t0 > limit_ns) return false;
   }
 }
 
@@ -359,10 +366,6 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
       : "memory");
 }
 
-__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 __device__ __forceinline__ void tc_mma_mxf8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                  uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(
@@ -391,9 +394,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 // pattern (as written by TMA with CU_TENSOR_MAP_SWIZZLE_128B): 8-row groups
 // are 1024 bytes apart.
 __device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) { return smem_desc(saddr, 16, 1024, 2); }
-
-// Source of a 32x128b tcgen05.cp: 32 contiguous 16-byte rows, no swizzle.
-__device__ __forceinline__ uint64_t sf_copy_desc(uint32_t saddr) { return smem_desc(saddr, 0, 128, 0); }
 
 // Instruction descriptor of kind::mxf8f6f4 with e8m0 block scales, both
 // operands K-major, fp32 accumulation.

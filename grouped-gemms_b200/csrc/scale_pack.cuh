@@ -1,9 +1,11 @@
 // Scale-factor packing for the block-scaled grouped GEMM.
 //
 // The reference's callers hand over e8m0 scales row-major, (rows,
-// contraction/32) (utils.to_mx, utils.py:67-105).  tcgen05.cp wants, per
-// 128-row slab and per 128-element contraction stage, one 512-byte atom laid
-// out as byte (r % 32) * 16 + (r / 32) * 4 + k (row r, k-block k).  This pass
+// contraction/32) (utils.to_mx, utils.py:67-105).  The GEMM's scale writers
+// want, per 128-row slab and per 128-element contraction stage, one 512-byte
+// atom laid out as byte (r % 32) * 16 + (r / 32) * 4 + k (row r, k-block k):
+// lane r % 32 of the atom is the 16 bytes that TMEM lane r % 32 of every
+// quarter holds in the block-scaled MMA's scale layout.  This pass
 // writes exactly the atoms the GEMM will read, in the order it reads them, so
 // the GEMM's producer can fetch a stage's scales with one TMA load each
 // (instead of the reference's per-call host re-layout, forward.py:537-561):

@@ -8,7 +8,7 @@ torch custom ops built on it.
 """
 
 from . import _lib, ops
-from ._lib import MxggError, device_status, set_tile_config, set_schedule
+from ._lib import MxggError, device_status, set_schedule, set_tile_config, set_wait_limit, wait_limit
 from .ops import (build_tile_map, grouped_mm_mx_op, grouped_mm_op, grouped_mm_segments_op, to_mx_fp4_op,
                   to_mx_op, wgrad_accumulate_op, wgrad_op)
 
@@ -26,5 +26,5 @@ def available() -> bool:
 
 
 __all__ = ["MxggError", "available", "build_tile_map", "device_status", "grouped_mm_mx_op", "grouped_mm_op",
-           "grouped_mm_segments_op", "ops", "set_tile_config", "set_schedule", "to_mx_fp4_op", "to_mx_op",
-           "wgrad_accumulate_op", "wgrad_op"]
+           "grouped_mm_segments_op", "ops", "set_tile_config", "set_schedule", "set_wait_limit", "to_mx_fp4_op",
+           "to_mx_op", "wait_limit", "wgrad_accumulate_op", "wgrad_op"]

@@ -108,6 +108,8 @@ SIGNATURES = {
     "mxgg_build_tile_map": (_int, [_vp, _i64, _i64, _i32, _vp, _vp]),
     "mxgg_set_tile_config": (_int, [_i32, _i32, _i32]),
     "mxgg_set_schedule": (_int, [_i32, _i32]),
+    "mxgg_set_wait_limit": (_int, [_i64]),
+    "mxgg_wait_limit": (_i64, []),
     "mxgg_device_status": (_int, [ctypes.POINTER(ctypes.c_uint32), _int, _vp]),
     "mxgg_last_error": (ctypes.c_char_p, []),
     "mxgg_version": (_i32, []),
@@ -155,6 +157,17 @@ def check(rc: int, what: str) -> None:
     if rc != MXGG_OK:
         msg = load().mxgg_last_error().decode(errors="replace")
         raise MxggError(f"{what} failed (code {rc}): {msg}")
+
+
+def set_wait_limit(ns: int = 0) -> None:
+    """Limit of every bounded device-side wait, in ns (0: the default 1 s).
+    A wait that runs out sets a device status bit and its kernel returns."""
+    check(load().mxgg_set_wait_limit(int(ns)), "mxgg_set_wait_limit")
+
+
+def wait_limit() -> int:
+    """The bounded-wait limit in ns."""
+    return int(load().mxgg_wait_limit())
 
 
 def device_status(clear: bool = True, stream=None) -> int:

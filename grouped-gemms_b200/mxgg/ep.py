@@ -369,7 +369,12 @@ class FusedExpertParallel:
         """Collective: all-gather every rank's per-expert counts and derive the
         copies, atom packing, segment tables and output heights.  The shared
         buffers do not depend on the placement, so one instance serves several
-        (`placement` overrides the constructor's for this plan)."""
+        (`placement` overrides the constructor's for this plan).
+
+        It also gathers every rank's device status word (read and cleared
+        here) and raises MxggError on all ranks alike when any of them is set:
+        the previous call's output must then be discarded.  Callers that reuse
+        one plan for many calls check with `check_status` instead."""
         from . import _lib
         dist = _dist()
         pl, world, rank = placement or self.placement, self.world, self.rank
@@ -377,12 +382,24 @@ class FusedExpertParallel:
             raise ValueError("placement and process group disagree on the world size")
         E = pl.n_experts
         dev = torch.device("cuda", torch.cuda.current_device())
-        mine = torch.tensor([int(c) for c in expert_counts], dtype=torch.int64, device=dev)
-        if mine.numel() != E or bool((mine < 0).any()):
+        counts = [int(c) for c in expert_counts]
+        if len(counts) != E or any(c < 0 for c in counts):
             raise ValueError("expert_counts must hold E non-negative counts")
-        allc = torch.empty(world, E, dtype=torch.int64, device=dev)
+        # The previous call's device-side error word travels with the counts:
+        # a bounded cross-GPU wait that gave up (a peer's rows or barrier
+        # slot never arrived: status bits 64 / 128) left stale rows in that
+        # call's output, and every rank raises here together, before the next
+        # collective, instead of carrying on with wrong numbers.
+        status = _lib.device_status(clear=True, stream=torch.cuda.current_stream().cuda_stream)
+        mine = torch.tensor(counts + [status], dtype=torch.int64, device=dev)
+        allc = torch.empty(world, E + 1, dtype=torch.int64, device=dev)
         dist.all_gather_into_tensor(allc, mine, group=self.group)
-        C = allc.tolist()                                     # C[s][e], one device sync
+        gathered = allc.tolist()                              # one device sync
+        bad = {r: row[E] for r, row in enumerate(gathered) if row[E] != 0}
+        if bad:
+            raise _lib.MxggError("fused expert parallelism: a device-side wait gave up in the previous call "
+                                 "(rank: status word) " + ", ".join(f"{r}: {v:#x}" for r, v in sorted(bad.items())))
+        C = [row[:E] for row in gathered]                     # C[s][e]
         tile_m = int(_lib.load().mxgg_query_tile_m())
         lay = fused_layout(C, pl, rank, tile_m)
         for d in range(world):
@@ -399,6 +416,22 @@ class FusedExpertParallel:
                          local_seg=_Segments(o, x, i32([rank] * len(seg["offs"])), i32(seg["local_row"]), sr),
                          dst_rows=lay["dst_rows"], tile_m=tile_m, inbox_ok=lay["inbox_ok"],
                          remote_blocks=i32(lay["remote_blocks"] if lay["inbox_ok"] else []))
+
+    def check_status(self) -> None:
+        """Collective: raise MxggError on every rank when any rank's device
+        status word is set (a bounded cross-GPU wait gave up in an earlier
+        call, so that call's output holds stale rows).  Reads and clears the
+        word; one small all-gather and a device sync."""
+        from . import _lib
+        dist = _dist()
+        st = _lib.device_status(clear=True, stream=torch.cuda.current_stream().cuda_stream)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        allst = torch.empty(self.world, dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(allst, torch.tensor([st], dtype=torch.int64, device=dev), group=self.group)
+        bad = {r: v for r, v in enumerate(allst.tolist()) if v != 0}
+        if bad:
+            raise _lib.MxggError("fused expert parallelism: a device-side wait gave up "
+                                 "(rank: status word) " + ", ".join(f"{r}: {v:#x}" for r, v in sorted(bad.items())))
 
     # ---------------------------------------------------------------- calls
     def barrier(self) -> None:

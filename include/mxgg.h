@@ -116,9 +116,14 @@ int mxgg_grouped_mm_cfg(const void* a, const void* b, const void* a_scale, const
  * synchronisation) and that cannot hold a workspace of its own.
  * Same arguments and results as mxgg_grouped_mm minus the workspace.  Its
  * scratch is one fixed 32 MiB array in device memory that every GPU loading
- * this library keeps until the process exits; problems whose scratch exceeds
- * it (mxgg_grouped_mm_workspace_size > 32 MiB) are rejected with
- * MXGG_ERR_UNSUPPORTED.  The first call on a device resolves the array's
+ * this library keeps until the process exits.  The array holds the packed
+ * scale atoms first: a problem whose packed scales alone exceed 32 MiB is
+ * rejected with MXGG_ERR_UNSUPPORTED.  The split-tail schedule's partial
+ * tiles (about 21 MB) go after them when they fit; when they do not (for
+ * example E=8, M=16640, N=K=8192), the call deals every tile whole
+ * (MXGG_SCHED_TILES), so its result equals mxgg_grouped_mm run with that
+ * schedule, and may differ from the split-tail result in the last bits of
+ * the fp32 sums.  The first call on a device resolves the array's
  * address on that device (the device must be current); make that first call
  * before any stream capture.  All calls share the array, which keeps the last
  * call's contents (nothing in it needs to start zeroed: each call rewrites
@@ -381,6 +386,15 @@ int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m);
  * 2..64).  No counterpart in the reference. */
 enum { MXGG_SCHED_DEFAULT = 0, MXGG_SCHED_TILES = 1, MXGG_SCHED_SPLIT_TAIL = 2 };
 int mxgg_set_schedule(int32_t schedule, int32_t split_max);
+
+/* Limit of every bounded device-side wait (pipeline barriers, peers' rows in
+ * mxgg_grouped_mm_ep, mxgg_peer_barrier), in ns of %globaltimer: 1 ms .. 60 s,
+ * 0 restores the default 1 s.  A wait that runs out sets its bit in the
+ * device status word and the kernel returns; the call's output is then
+ * incomplete.  Process-wide; each call reads it when it is enqueued.  No
+ * counterpart in the reference (its kernels have no device-side waits). */
+int mxgg_set_wait_limit(int64_t ns);
+int64_t mxgg_wait_limit(void);
 
 /* Error bits raised by device-side bounded waits since the last clear
  * (0 = none; bit 256: a transposed quantised output met a group off the

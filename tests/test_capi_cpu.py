@@ -108,6 +108,18 @@ def test_schedule_validation():
     assert lib.mxgg_set_schedule(_lib.SCHED_DEFAULT, 0) == 0
 
 
+def test_wait_limit_validation():
+    # the bounded-wait limit is a host setting: 1 ms .. 60 s, 0 restores 1 s
+    assert _lib.wait_limit() == 1_000_000_000
+    for bad in (-1, 999_999, 61_000_000_000):
+        with pytest.raises(_lib.MxggError):
+            _lib.set_wait_limit(bad)
+    _lib.set_wait_limit(5_000_000)
+    assert _lib.wait_limit() == 5_000_000
+    _lib.set_wait_limit(0)
+    assert _lib.wait_limit() == 1_000_000_000
+
+
 def test_workspace_holds_split_tail_partials():
     # one fp32 128 x 256 partial tile for each of up to 160 CTAs, on top of
     # the packed scales, whatever the problem

@@ -198,6 +198,50 @@ def test_full_size_sampled_rows(K_, U):
     assert O.rel_l2(got, bf16_round(ref)) <= REL_BF16
 
 
+@pytest.mark.parametrize("E,N,K,passname", [(8, 5120, 2048, "fwd"), (4, 2048, 8192, "fwd"), (8, 2048, 5120, "dgrad")])
+def test_full_size_mult16_sampled_rows(K_, U, E, N, K, passname):
+    """BASELINE config 2/3 group sizes: multiples of 16 (so group edges fall
+    mid 32-row block) at the sweep's full M, checked on sampled rows that
+    include every group's first and last row."""
+    import random
+    M = 16640
+    random.seed(1600 + E)
+    offs = U.generate_jagged_offs(E, M, multiple_of=16, device="cpu").tolist()
+    assert any(o % 32 for o in offs[:-1]), "the draw must put a group edge off the 32-row grid"
+    torch.manual_seed(16)
+    if passname == "fwd":
+        A = torch.randn(M, K, dtype=torch.bfloat16, device="cuda")
+        B = torch.randn(E, N, K, dtype=torch.bfloat16, device="cuda")
+        a_s, a_q = U.to_mx(A)
+        b_s, b_q = U.to_mx(B)
+    else:
+        # dgrad: grad_out (M, N) and W^T (E, K, N), both quantised along N
+        A = torch.randn(M, N, dtype=torch.bfloat16, device="cuda")
+        B = torch.randn(E, N, K, dtype=torch.bfloat16, device="cuda")
+        a_s, a_q = U.to_mx(A)
+        wt = [U.to_mx_dim1(B[e]) for e in range(E)]
+        b_s = torch.stack([s_ for s_, _ in wt])
+        b_q = torch.stack([q for _, q in wt])
+    del A, B
+    o = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    out = K_.triton_mxfp8_grouped_mm(a_q, b_q, a_s, b_s, o)
+    torch.cuda.synchronize()
+    starts = [0] + offs[:-1]
+    edges = sorted({r for a, b in zip(starts, offs) if b > a for r in (a, b - 1)})
+    rng = np.random.default_rng(1)
+    rows = np.array(sorted(set(edges) | set(rng.choice(M, 32, replace=False).tolist())))
+    groups = np.searchsorted(np.asarray(offs), rows, side="right")
+    rt = torch.from_numpy(rows).cuda()
+    A_d = O.dequant(u8(a_q[rt]), u8(a_s[rt])).astype(np.float32)
+    got = f32(out[rt])
+    ref = np.empty_like(got)
+    for g in np.unique(groups):
+        Bd = O.dequant(u8(b_q[g]), u8(b_s[g])).astype(np.float32)
+        sel = groups == g
+        ref[sel] = A_d[sel] @ Bd.T
+    assert O.rel_l2(got, bf16_round(ref)) <= REL_BF16
+
+
 def test_dgrad_pass(K_, U):
     """dgrad = the same op with grad_out (M, N) and W^T (E, K, N), both
     quantised along N (the contraction)."""
