@@ -97,8 +97,11 @@ def mxfp8_grouped_mm_to_mx(
     epilogue also writes ``utils.to_mx_dim1`` of the output -- the transpose
     quantised along tokens, ``(scales_t (N, M//32), data_t (N, M))``, the
     operand layout of the next ``triton_mxfp8_wgrad`` -- appended after
-    ``data``; it needs ``M % 32 == 0`` and group ends on multiples of 32 (a
-    group off that grid sets device status bit 256).  Rows at or past
+    ``data``; it needs ``M % 32 == 0`` and group ends on multiples of 32.  A
+    group off that grid sets device status bit 256 and its transposed blocks
+    are left unwritten (the buffers are not zeroed), so a caller whose offsets
+    may be off the grid must check ``mxgg.device_status()`` before using
+    them.  Rows at or past
     ``group_end_offsets[-1]`` are left unwritten.  The reference runs the GEMM
     (kernels/forward.py:461-606) and ``to_mx`` (utils.py:67-105) separately.
     """
