@@ -153,7 +153,7 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
 constexpr int kMaxGridCtas = 160;
 
 struct Maps {
-  CUtensorMap a, a_self, b, sfa, sfb;
+  CUtensorMap a, a_self, b;
   OutMaps out;
 };
 
@@ -185,7 +185,7 @@ int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, lon
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.a_self, m.b, m.sfa, m.sfb, m.out, p));
+  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.a_self, m.b, m.out, p));
   return MXGG_OK;
 }
 
@@ -572,14 +572,10 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                      : make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C,
                                     (uint64_t)C, kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (int rc = make_tmap_2d(&maps.sfa, (route && route->a_atoms) ? route->a_atoms : ws_a,
-                            CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
-                            (uint64_t)(ws.a_subtiles * ws.stages * 4), 128, 128, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return rc;
-  if (int rc = make_tmap_2d(&maps.sfb, ws_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
-                            (uint64_t)(ws.b_tiles * ws.stages * 4 * (bn / 128)), 128, 128, 128, 4 * (bn / 128),
-                            CU_TENSOR_MAP_SWIZZLE_NONE))
-    return rc;
+  // the scale writers read the packed atoms directly; every index they form
+  // stays inside the a_subtiles x stages and b_tiles x stages atoms packed
+  p.sfa_atoms = static_cast<const uint8_t*>((route && route->a_atoms) ? route->a_atoms : ws_a);
+  p.sfb_atoms = ws_b;
   std::memset(&maps.out, 0, sizeof(maps.out));
   if (route) {
     // one map per destination with rows (the peers' outputs take TMA stores too)

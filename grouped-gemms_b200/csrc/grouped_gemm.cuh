@@ -17,25 +17,27 @@
 //
 // Warp roles (320 threads per CTA):
 //   warps 0-3   scale writers: per stage, the CTA's scale atoms (pre-packed by
-//               pack_scales_kernel, TMA-loaded into shared memory) go to a
-//               ring of scale slots in TMEM with tcgen05.st, warp q writing
-//               its own 32-lane quarter (the block-scaled MMA reads the same
-//               32-row atom from every quarter).  Moving the scales with
-//               tcgen05.cp instead puts three copies per stage into the
-//               tensor pipe's instruction stream, where they cost ~135 of a
-//               stage's ~490 MMA cycles (measured on B200); tcgen05.st from
-//               other warps leaves the pipe to the MMAs.  Warp 3 also builds
-//               the group table in the prologue.
+//               pack_scales_kernel) go from global memory, through a register
+//               ring loaded kSfRing stages ahead, to a ring of kSfSlots scale
+//               slots in TMEM with tcgen05.st, warp q writing its own 32-lane
+//               quarter (the block-scaled MMA reads the same 32-row atom from
+//               every quarter); then they arrive on the stage's full barrier.
+//               Moving the scales with tcgen05.cp instead puts three copies
+//               per stage into the tensor pipe's instruction stream, where
+//               they cost ~135 of a stage's ~490 MMA cycles (measured on
+//               B200); tcgen05.st from other warps leaves the pipe to the
+//               MMAs.  Warp 3 also builds the group table in the prologue.
 //   warps 4-7   epilogue: TMEM -> registers -> bf16/fp32 -> swizzled smem ->
 //               TMA store; ragged group edges fall back to predicated stores;
 //               on request also the MX-quantised rows and transpose (to_mx and
 //               to_mx_dim1 of the output) from the same registers
 //   warp 8      TMA producer: per stage the A and B tiles (128 B swizzle) into
 //               a STAGES ring on one transaction barrier (the pair's leader
-//               counts both CTAs' bytes), and this CTA's scale atoms on a
-//               barrier of its own
-//   warp 9      MMA issuer (the leader CTA's lane 0):
-//               tcgen05.mma.kind::mxf8f6f4.block_scale (K=32), four per stage
+//               counts both CTAs' bytes and the scale writers' arrivals)
+//   warp 9      MMA issuer (the leader CTA's lane 0): one wait per stage (its
+//               full barrier), four tcgen05.mma.kind::mxf8f6f4.block_scale
+//               (K=32), one commit.  A second per-stage wait, on a barrier of
+//               the scale writers' own, measured ~10 % slower.
 //
 // Scheduling: a persistent grid (one CTA per SM) walks a device-built
 // group->tile map: every CTA reads the group end offsets once, builds the
@@ -59,7 +61,8 @@ constexpr int kEpiWarp0 = 4;      // epilogue: warps 4-7
 constexpr int kProdWarp = 8;      // TMA producer
 constexpr int kMmaWarp = 9;       // MMA issuer
 constexpr int kThreads = 320;
-constexpr int kSfSlots = 5;       // scale slots in TMEM (stages the writers may run ahead)
+constexpr int kSfSlots = 2;       // scale slots in TMEM (stages the writers may run ahead)
+constexpr int kSfRing = 4;        // stages of scale atoms the writers hold in registers
 constexpr int kMaxGroups = 256;   // groups handled by the in-kernel table
 constexpr int kMaxDst = 8;        // output destinations (ranks) of an expert-parallel forward
 constexpr int kTmemCols = 512;
@@ -117,6 +120,10 @@ struct GemmParams {
   int split_max;             // most pieces per split tile (0: about sqrt(stages))
   float* part_slots;         // split tiles: one fp32 128 x BN partial per CTA of the grid
   int* part_counters;        // split tiles: arrivals per (tail tile, CTA of the pair, epilogue warp), zeroed before the launch
+  // Packed scale atoms (pack_scales_kernel's layout): A [sub-tile][stage][512 B],
+  // B [tile][stage][BN/128][512 B].  The scale writers read them directly.
+  const uint8_t* sfa_atoms;
+  const uint8_t* sfb_atoms;
   uint32_t* status;          // error word (device memory), 0 = ok
   unsigned long long wait_ns;  // limit of every bounded wait (%globaltimer ns)
   // Expert-parallel output routing (fwd): group g's rows are stored to
@@ -189,13 +196,10 @@ struct SmemLayout {
   alignas(1024) uint8_t a[STAGES][kBM * kBK];
   alignas(1024) uint8_t b[STAGES][kBRows * kBK];
   alignas(1024) uint8_t epi[4][2][32 * 64];            // per epilogue warp, double buffered
-  alignas(128) uint8_t sfa[STAGES][kBM * 4];
-  alignas(128) uint8_t sfb[STAGES][BN * 4];             // full BN rows: each CTA's TMEM needs all of them
-  alignas(8) uint64_t full[STAGES];   // A and B tiles landed (the leader's counts both CTAs)
+  // full: the stage's A and B tiles landed (the leader's barrier counts both
+  // CTAs' bytes) and every scale writer of the pair has put its scales in TMEM
+  alignas(8) uint64_t full[STAGES];
   uint64_t empty[STAGES];             // stage read by its MMAs (commit to both CTAs)
-  uint64_t sfl[STAGES];               // this CTA's scale atoms landed
-  uint64_t sft[kSfSlots];             // TMEM scale slot written (leader; every writer warp of the pair)
-  uint64_t sfe[kSfSlots];             // TMEM scale slot read by its MMAs (commit to both CTAs)
   uint64_t tfull[2];
   uint64_t tempty_ov[2];    // accumulator columns shared with the other buffer drained
   uint64_t tempty_all[2];   // whole accumulator drained
@@ -499,12 +503,12 @@ __device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volati
 template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_self,
-                        const __grid_constant__ CUtensorMap tmap_b,
-                        const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                        const __grid_constant__ OutMaps omaps, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ OutMaps omaps,
+                        const GemmParams p) {
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
   static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
   static_assert(ACC == 2, "two accumulator buffers (overlapping when 2*BN does not fit)");
+  static_assert(kSfSlots < STAGES, "a scale writer waits on the empty barrier kSfSlots stages back");
   using S = SmemLayout<BN, STAGES, PAIR, OutT>;
   constexpr int kEpiCols = S::kEpiCols;
   constexpr int kChunks = BN / kEpiCols;       // epilogue chunks per accumulator
@@ -531,8 +535,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // transaction count, both CTAs): e2m1 B tiles count their packed global
   // bytes, half of the 8-bit-slot smem they fill
   const uint32_t kStageBytes = PAIR * (kBM * kBK + (p.b_fmt == 5 ? kBRows * kBK / 2 : kBRows * kBK));
-  // bytes of this CTA's scale atoms per stage (its own barrier)
-  constexpr uint32_t kSfBytes = kBM * 4 + BN * 4;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   S* sm = reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -566,14 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------------------------------------ prologue
   if (warp == kProdWarp && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      // the leader's producer arms it; every CTA's loads complete on it
-      ptx::mbar_init(ptx::smem_u32(&sm->full[s]), 1);
+      // the leader's producer arms it, every CTA's tile loads complete on it,
+      // and every scale-writer warp of the pair arrives on it
+      ptx::mbar_init(ptx::smem_u32(&sm->full[s]), 1 + 4 * PAIR);
       ptx::mbar_init(ptx::smem_u32(&sm->empty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sm->sfl[s]), 1);
-    }
-    for (int j = 0; j < kSfSlots; ++j) {
-      ptx::mbar_init(ptx::smem_u32(&sm->sft[j]), 4 * PAIR);   // scale-writer warps of every CTA
-      ptx::mbar_init(ptx::smem_u32(&sm->sfe[j]), 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(ptx::smem_u32(&sm->tfull[a]), 1);
@@ -585,8 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
-    ptx::prefetch_tmap(&tmap_sfa);
-    ptx::prefetch_tmap(&tmap_sfb);
     ptx::prefetch_tmap(&omaps.m[p.local_dst]);
   }
   if (warp == kMmaWarp) {
@@ -648,14 +644,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int st = u.st_begin + s;
           const int x = st * kBK;
-          // packed scale atoms: A [sub-tile][stage][512 B], B [tile][stage][BN/128 x 512 B]
-          const int ya = ((u.a_sub + (int)rank) * p.stages + st) * 4;
-          const int yb = (u.b_tile * p.stages + st) * 4 * (BN / 128);
-          // this CTA's scale atoms, on its own barrier (its scale writers wait there)
-          const uint32_t sb = ptx::smem_u32(&sm->sfl[stage]);
-          ptx::mbar_arrive_expect_tx(sb, kSfBytes);
-          ptx::tma_load_2d(ptx::smem_u32(sm->sfa[stage]), &tmap_sfa, sb, 0, ya);
-          ptx::tma_load_2d(ptx::smem_u32(sm->sfb[stage]), &tmap_sfb, sb, 0, yb);
           if constexpr (PAIR == 2) {
             const uint32_t fb = leader_bar(&sm->full[stage]);
             if (leader) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&sm->full[stage]), kStageBytes);
@@ -718,8 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ph = (it / STAGES) & 1u;
           const uint32_t slot = it % kSfSlots;
           // the stage's tiles (both CTAs) and its scales in TMEM (every writer warp of the pair)
-          if (!wait_leader_side(&sm->full[stage], ph) ||
-              !wait_leader_side(&sm->sft[slot], (it / kSfSlots) & 1u)) {
+          if (!wait_leader_side(&sm->full[stage], ph)) {
             raise_error(p, abort, kErrMmaWait);
             ok = false;
             break;
@@ -750,14 +737,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               accumulate = 1;
             }
           }
-          // once these MMAs complete: the stage's buffers and the scale slot are free again
-          if constexpr (PAIR == 2) {
-            ptx::tc_commit_pair(ptx::smem_u32(&sm->empty[stage]), 0x3);
-            ptx::tc_commit_pair(ptx::smem_u32(&sm->sfe[slot]), 0x3);
-          } else {
-            ptx::tc_commit(ptx::smem_u32(&sm->empty[stage]));
-            ptx::tc_commit(ptx::smem_u32(&sm->sfe[slot]));
-          }
+          // once these MMAs complete: the stage's buffers and its scale slot are free again
+          if constexpr (PAIR == 2) ptx::tc_commit_pair(ptx::smem_u32(&sm->empty[stage]), 0x3);
+          else ptx::tc_commit(ptx::smem_u32(&sm->empty[stage]));
         }
         if (!ok) break;
         if constexpr (PAIR == 2) ptx::tc_commit_pair(ptx::smem_u32(&sm->tfull[acc]), 0x3);
@@ -1109,43 +1091,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     // row l of the A atom (4 columns) and of each B atom (4 columns each).
     // Every quarter holds the same 32 x 16-byte atom rows, the layout the
     // block-scaled MMA reads (rows r, r+32, r+64, r+96 in lane r % 32).
+    //
+    // Stage it's scales go to slot it % kSfSlots once the MMAs of stage
+    // it - kSfSlots, the slot's last reader, have completed (that stage's
+    // empty barrier).  The stage's tiles were only requested once the MMAs
+    // STAGES back completed and then cross L2, so with the atoms already in
+    // registers (loaded kSfRing stages earlier) the scales are in TMEM before
+    // the tiles land, and the writers' arrivals do not hold the full barrier.
+    // The arrival for stage it always lands in that stage's phase of full:
+    // the phase before it completed before the MMAs of stage it - STAGES were
+    // issued, which precedes the completion the writer waited for.
     const int q = warp - kSfWarp0;
     const uint32_t lane_base = tmem_base + ((uint32_t)(32 * q) << 16) + kSfCol0;
-    uint32_t it = 0;
-    int k = 0;
-    Unit u;
+    constexpr int kB = BN / 128;                  // B atoms per stage
+    // load cursor over the (unit, stage) sequence every role walks
+    int lk = 0, ls = 0;
+    Unit lu;
+    bool lhas = false;
+    auto advance = [&]() -> bool {
+      while (true) {
+        if (lhas && ls + 1 < lu.st_count) {
+          ++ls;
+          return true;
+        }
+        if (!next_unit<BN, kTileM>(sm, p, lk, unit0, unit_stride, num_units, lu)) return false;
+        lhas = true;
+        ls = -1;
+      }
+    };
     bool ok = true;
-    while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
-      for (int s = 0; s < u.st_count; ++s, ++it) {
-        const int stage = it % STAGES;
-        const uint32_t slot = it % kSfSlots;
-        // the atoms are in shared memory, and the slot's previous MMAs are done
-        if (!wait_local(&sm->sfl[stage], (it / STAGES) & 1u) ||
-            !wait_local(&sm->sfe[slot], ((it / kSfSlots) & 1u) ^ 1u)) {
-          raise_error(p, abort, kErrScaleWait);
+    // sources whose atoms may be read (streaming dispatch: a sender packs its
+    // rows' atoms before it raises its flag); rows read in place are always there
+    uint32_t ready = (p.self_src >= 0) ? (1u << p.self_src) : 0u;
+    auto load = [&](uint4 (&r)[3]) {
+      if (p.src_flags && !((ready >> lu.src) & 1u)) {
+        int got = 1;
+        if (lane == 0) {
+          got = wait_source(p, lu.src, abort) ? 1 : 0;
+          if (!got) raise_error(p, abort, kErrSourceWait);
+        }
+        __syncwarp();
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
           ok = false;
+          return;
+        }
+        int f;   // every lane's own acquire of the raised flag
+        asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(f) : "l"(p.src_flags + lu.src) : "memory");
+        ready |= 1u << lu.src;
+      }
+      const long long st = lu.st_begin + ls;
+      r[0] = __ldg(reinterpret_cast<const uint4*>(p.sfa_atoms + ((long long)(lu.a_sub + (int)rank) * p.stages + st) * 512) +
+                   lane);
+#pragma unroll
+      for (int b = 0; b < kB; ++b)
+        r[1 + b] = __ldg(reinterpret_cast<const uint4*>(p.sfb_atoms + (((long long)lu.b_tile * p.stages + st) * kB + b) * 512) +
+                         lane);
+    };
+    uint4 ring[kSfRing][3];
+    int loaded = 0;
+#pragma unroll
+    for (int r = 0; r < kSfRing; ++r) {
+      if (ok && advance()) {
+        load(ring[r]);
+        ++loaded;
+      }
+    }
+    uint32_t it = 0;
+    bool done = false;
+    while (!done) {
+#pragma unroll
+      for (int r = 0; r < kSfRing; ++r) {   // stage it sits in ring[it % kSfRing] == ring[r]
+        if (!ok || (int)it >= loaded) {
+          done = true;
           break;
         }
-        const uint32_t taddr = lane_base + slot * kSfCols;
-        uint32_t a[4];
-        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-                     : "r"(ptx::smem_u32(sm->sfa[stage]) + lane * 16)
-                     : "memory");
-        ptx::tmem_st_32x32b_x4(taddr, a);
-#pragma unroll
-        for (int b = 0; b < BN / 128; ++b) {
-          uint32_t w[4];
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
-                       : "r"(ptx::smem_u32(sm->sfb[stage]) + b * 512 + lane * 16)
-                       : "memory");
-          ptx::tmem_st_32x32b_x4(taddr + 4 + 4 * b, w);
+        if (it >= (uint32_t)kSfSlots) {
+          // the slot's last reader, stage it - kSfSlots, has completed
+          const uint32_t j = it - kSfSlots;
+          if (!wait_local(&sm->empty[j % STAGES], (j / STAGES) & 1u)) {
+            raise_error(p, abort, kErrScaleWait);
+            ok = false;
+            done = true;
+            break;
+          }
         }
+        const uint32_t taddr = lane_base + (it % kSfSlots) * kSfCols;
+        ptx::tmem_st_32x32b_x4(taddr, reinterpret_cast<const uint32_t(&)[4]>(ring[r][0]));
+#pragma unroll
+        for (int b = 0; b < kB; ++b)
+          ptx::tmem_st_32x32b_x4(taddr + 4 + 4 * b, reinterpret_cast<const uint32_t(&)[4]>(ring[r][1 + b]));
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) arrive_leader(&sm->sft[slot]);
+        if (lane == 0) arrive_leader(&sm->full[it % STAGES]);
+        ++it;
+        if (ok && advance()) {
+          load(ring[r]);
+          ++loaded;
+        }
       }
     }
   }

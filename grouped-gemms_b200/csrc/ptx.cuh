@@ -16,6 +16,13 @@
 #define MXGG_WAIT_LIMIT_NS 1000000000ull   // 1 s
 #endif
 
+// A waiting thread is suspended in hardware until the barrier's phase
+// completes or this many ns pass (the try_wait suspend-time hint), instead of
+// re-polling: polling warps take issue slots from the warps sharing their SM
+// sub-partition, the MMA issuer among them (measured on B200: hinted waits made
+// the GEMM 2-4 % faster).
+#define MXGG_WAIT_SUSPEND_NS 20000
+
 namespace mxgg {
 namespace ptx {
 
@@ -60,10 +67,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "n"(MXGG_WAIT_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
@@ -75,10 +82,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           uint64_t limit_ns = MXGG_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((i & 255u) == 255u && globaltimer() - t0 > limit_ns) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 
@@ -311,10 +318,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "n"(MXGG_WAIT_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
@@ -325,10 +332,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
                                                   uint64_t limit_ns = MXGG_WAIT_LIMIT_NS) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
+  while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort) return false;
-    if ((i & 255u) == 255u && globaltimer() - t0 > limit_ns) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 
