@@ -178,13 +178,19 @@ int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, lon
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = PAIR;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: the GEMM may start while the scale-pack
+  // kernel that precedes it still runs (that kernel lets it go at once); its
+  // roles that read what the pack writes wait for it with griddepcontrol.wait.
+  // After any other kernel, which never lets it go early, this changes nothing.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.a_self, m.b, m.out, p));
   return MXGG_OK;
 }

@@ -61,7 +61,7 @@ constexpr int kEpiWarp0 = 4;      // epilogue: warps 4-7
 constexpr int kProdWarp = 8;      // TMA producer
 constexpr int kMmaWarp = 9;       // MMA issuer
 constexpr int kThreads = 320;
-constexpr int kSfSlots = 2;       // scale slots in TMEM (stages the writers may run ahead)
+constexpr int kSfSlotsMax = 5;    // scale slots in TMEM (stages the writers may run ahead), at most
 constexpr int kSfRing = 4;        // stages of scale atoms the writers hold in registers
 constexpr int kMaxGroups = 256;   // groups handled by the in-kernel table
 constexpr int kMaxDst = 8;        // output destinations (ranks) of an expert-parallel forward
@@ -508,7 +508,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
   static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
   static_assert(ACC == 2, "two accumulator buffers (overlapping when 2*BN does not fit)");
-  static_assert(kSfSlots < STAGES, "a scale writer waits on the empty barrier kSfSlots stages back");
+  // a scale writer waits on the empty barrier kSfSlots stages back, which must
+  // be a barrier the producer has not re-armed yet
+  constexpr int kSfSlots = (STAGES - 1 < kSfSlotsMax) ? STAGES - 1 : kSfSlotsMax;
   using S = SmemLayout<BN, STAGES, PAIR, OutT>;
   constexpr int kEpiCols = S::kEpiCols;
   constexpr int kChunks = BN / kEpiCols;       // epilogue chunks per accumulator
@@ -754,6 +756,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lane quarter this warp may access
+    // the split-tail arrival counters are zeroed by the scale-pack kernel
+    // that precedes this grid (which may have launched early, see capi.cu)
+    ptx::griddep_wait();
     uint32_t ai = 0;
     int buf = 0;
     int k = 0;
@@ -972,8 +977,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if (!u.split) {
+        int ci0 = 0;
+        if constexpr (kOvChunks > 1) {
+          if (!zero) {
+            // the shared chunks leave TMEM together, so the next tile's MMAs
+            // wait for one TMEM read, not for their conversion and stores
+            const int c0 = (acc == 0) ? c_first : 0;
+            uint32_t vs[kOvChunks][kEpiCols];
+#pragma unroll
+            for (int i = 0; i < kOvChunks; ++i) {
+              if constexpr (kEpiCols == 32)
+                ptx::tmem_ld_32x32b_x32(t_row + (c0 + i) * kEpiCols, reinterpret_cast<uint32_t(&)[32]>(vs[i]));
+              else
+                ptx::tmem_ld_32x32b_x16(t_row + (c0 + i) * kEpiCols, reinterpret_cast<uint32_t(&)[16]>(vs[i]));
+            }
+            ptx::tmem_wait_ld();
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_leader(&sm->tempty_ov[acc]);
+#pragma unroll
+            for (int i = 0; i < kOvChunks; ++i) emit(c0 + i, vs[i]);
+            ci0 = kOvChunks;
+          }
+        }
 #pragma unroll 1
-        for (int ci = 0; ci < kChunks; ++ci) {
+        for (int ci = ci0; ci < kChunks; ++ci) {
           const int c = (acc == 0) ? (ci < kOvChunks ? c_first + ci : ci - kOvChunks) : ci;
           uint32_t v[kEpiCols];
           load_chunk(ci, c, v);
@@ -1148,6 +1176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         r[1 + b] = __ldg(reinterpret_cast<const uint4*>(p.sfb_atoms + (((long long)lu.b_tile * p.stages + st) * kB + b) * 512) +
                          lane);
     };
+    // the atoms are written by the scale-pack kernel that precedes this grid
+    ptx::griddep_wait();
     uint4 ring[kSfRing][3];
     int loaded = 0;
 #pragma unroll

@@ -89,6 +89,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Let the next kernel on the stream (launched with programmatic stream
+// serialisation) start once every CTA of this grid has executed this.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Wait until the preceding grid on the stream has completed and its memory
+// operations are visible (a no-op when this grid was launched normally).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // --------------------------------------------------------------- proxies
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -80,6 +80,10 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
   __shared__ int s_start[kMaxGroups];
   __shared__ int s_cum[kMaxGroups + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The GEMM that follows may launch now: its prologue and first tile loads
+  // need nothing from this kernel, and the roles that read the atoms and
+  // counters written here wait for this grid to finish (griddepcontrol.wait).
+  ptx::griddep_launch_dependents();
   if (p.mode == kFwd) {
     if (warp == 0) {
       // same group table as the GEMM: clamped, monotone starts; tile prefix
