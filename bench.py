@@ -124,9 +124,12 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ inputs
-def build_problems(device, shapes, passes, seed=123, multiple_of=32):
+def build_problems(device, shapes, passes, seed=123, multiple_of=32, scale_layout="row_major"):
     """Quantised operands for every (shape, pass); offsets as the reference draws them
-    (group sizes multiples of `multiple_of`; wgrad needs 32)."""
+    (group sizes multiples of `multiple_of`; wgrad needs 32).  scale_layout
+    "blocked": the scales come from the quantisers' blocked outputs
+    (utils.to_mx_grouped_blocked / to_mx_dim1_blocked) and the GEMMs take them
+    in place; the e4m3 data and every result are the same bits."""
     import torch
     import utils
 
@@ -138,28 +141,34 @@ def build_problems(device, shapes, passes, seed=123, multiple_of=32):
         A = torch.randn(M, K, device=device, dtype=torch.bfloat16, generator=gen)
         W = torch.randn(E, N, K, device=device, dtype=torch.bfloat16, generator=gen)
         G = torch.randn(M, N, device=device, dtype=torch.bfloat16, generator=gen)
+        blk = scale_layout == "blocked"
         if "fwd" in passes:
-            a_s, a_q = utils.to_mx(A)
-            b_s, b_q = utils.to_mx(W)
+            a_s, a_q = utils.to_mx_grouped_blocked(A, offs) if blk else utils.to_mx(A)
+            b_s, b_q = utils.to_mx_grouped_blocked(W) if blk else utils.to_mx(W)
             probs.append(dict(pass_="fwd", shape=(E, M, N, K), flops=2.0 * M * N * K,
-                              args=(a_q, b_q, a_s, b_s, offs)))
+                              args=(a_q, b_q, a_s, b_s, offs), layout=scale_layout))
         if "fwd4" in passes:
             a_s, a_q = utils.to_mx(A)
             w4_s, w4_q = utils.to_mx(W, elem_dtype=torch.float4_e2m1fn_x2)
             probs.append(dict(pass_="fwd4", shape=(E, M, N, K), flops=2.0 * M * N * K,
                               args=(a_q, w4_q, a_s, w4_s, offs)))
         if "dgrad" in passes:
-            g_s, g_q = utils.to_mx(G)                                  # along N
-            wt = [utils.to_mx_dim1(W[e]) for e in range(E)]            # W[e]^T (K, N), along N
-            wt_s = torch.stack([s for s, _ in wt])
-            wt_q = torch.stack([q for _, q in wt])
+            if blk:
+                g_s, g_q = utils.to_mx_grouped_blocked(G, offs)        # along N, per group
+                wt_s, wt_q = utils.to_mx_grouped_blocked(W.transpose(-2, -1).contiguous())   # (E, K, N), per expert
+            else:
+                g_s, g_q = utils.to_mx(G)                              # along N
+                wt = [utils.to_mx_dim1(W[e]) for e in range(E)]        # W[e]^T (K, N), along N
+                wt_s = torch.stack([s for s, _ in wt])
+                wt_q = torch.stack([q for _, q in wt])
             probs.append(dict(pass_="dgrad", shape=(E, M, N, K), flops=2.0 * M * N * K,
-                              args=(g_q, wt_q, g_s, wt_s, offs)))
+                              args=(g_q, wt_q, g_s, wt_s, offs), layout=scale_layout))
         if "wgrad" in passes:
-            go_s, go_q = utils.to_mx_dim1(G)                           # (N, M), along tokens
-            ia_s, ia_q = utils.to_mx_dim1(A)                           # (K, M), along tokens
+            dim1 = utils.to_mx_dim1_blocked if blk else utils.to_mx_dim1
+            go_s, go_q = dim1(G)                                       # (N, M), along tokens
+            ia_s, ia_q = dim1(A)                                       # (K, M), along tokens
             probs.append(dict(pass_="wgrad", shape=(E, M, N, K), flops=2.0 * M * N * K,
-                              args=(go_q, go_s, ia_q, ia_s, offs)))
+                              args=(go_q, go_s, ia_q, ia_s, offs), layout=scale_layout))
         del A, W, G
     torch.cuda.synchronize()
     return probs
@@ -449,9 +458,10 @@ def run_problem(p):
     import kernels
     if "plan" in p:
         return run_ep_problem(p)
+    layout = p.get("layout", "row_major")
     if p["pass_"] == "wgrad":
-        return kernels.triton_mxfp8_wgrad(*p["args"])
-    return kernels.triton_mxfp8_grouped_mm(*p["args"])
+        return kernels.triton_mxfp8_wgrad(*p["args"], scale_layout=layout)
+    return kernels.triton_mxfp8_grouped_mm(*p["args"], scale_layout=layout)
 
 
 def _blocked_scales(s2d):
@@ -1014,6 +1024,21 @@ def main():
         fp4 = {"fwd_geomean_tflops": round(geomean([p["flops"] / t / 1e12 for p, t in zip(p4, per4)]), 1),
                "note": "e2m1 weights (two per byte, TMA-unpacked) x e4m3 activations on kind::mxf8f6f4"}
         del p4
+    blocked = None
+    if world == 1 and not args.no_extras:
+        # the same sweep with the scales quantised straight into the blocked
+        # layout the GEMM reads (no pack launch per call)
+        pb = build_problems(dev, [shapes[i] for i in idx], passes, scale_layout="blocked")
+        perb, _ = time_problems(pb, max(1, min(args.steps, 3)), 1, world, flush)
+        tfb = [p["flops"] / t / 1e12 for p, t in zip(pb, perb)]
+        blocked = {"geomean_tflops": round(geomean(tfb), 1),
+                   "per_pass_geomean": {ps: round(geomean([x for x, p in zip(tfb, pb) if p["pass_"] == ps]), 1)
+                                        for ps in passes},
+                   "over_row_major": round(geomean(tfb) / gm, 4),
+                   "launches_per_call": 1,
+                   "scales": "utils.to_mx_grouped_blocked / to_mx_dim1_blocked outside the timed region; "
+                             "scale_layout='blocked'"}
+        del pb
     mult16 = None
     if world == 1 and not args.no_extras and any(ps in passes for ps in ("fwd", "dgrad")):
         # BASELINE config 2's group sizes: multiples of 16 (fwd and dgrad;
@@ -1075,6 +1100,8 @@ def main():
             line["mxfp4_weights"] = fp4
         if mult16:
             line["fwd_dgrad_mult16"] = mult16
+        if blocked:
+            line["blocked_scales"] = blocked
         if vendor:
             line["vs_vendor"] = vendor
         if args.torch_arm and world == 1:

@@ -63,6 +63,7 @@ struct GemmCfg {
   int group_m = 0;
   int schedule = MXGG_SCHED_DEFAULT;
   int split_max = 0;
+  int scale_layout = MXGG_SCALE_ROW_MAJOR;   // per call only (it describes the caller's tensors)
 };
 GemmCfg g_default_cfg;   // guarded by g_mu
 // Limit of every bounded device-side wait (mbarriers, peers' flags, the
@@ -205,11 +206,12 @@ int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, l
   }
 }
 
-// Packed-scale workspace of one GEMM call: [A atoms | B atoms], each part
-// 1 KiB aligned.  Sized for the larger of the two tile heights so a size
-// query does not depend on the tile configuration chosen at launch.
+// Workspace of one GEMM call: [A atoms | B atoms | split-tail partials |
+// arrival counters], each part 1 KiB aligned.  The atoms (the blocked scale
+// layout, scale_pack.cuh) do not depend on the tile shape; the partials do,
+// so a size query takes the larger tile width.
 struct WsPlan {
-  long long a_subtiles, b_tiles, stages, a_bytes, b_bytes;
+  long long a_slabs, b_slabs, stages, a_bytes, b_bytes;
   long long part_bytes, counter_bytes;   // split tail: one fp32 partial tile per CTA, arrival counters
   long long total;                       // with the split-tail scratch
   long long base;                        // without it
@@ -222,15 +224,17 @@ WsPlan plan_workspace(int mode, int64_t M, int64_t N, int64_t K, int64_t E, int6
   WsPlan w{};
   const int64_t C = mode == kFwd ? K : M;
   w.stages = (C + kBK - 1) / kBK;
+  (void)tile_m;
   if (mode == kFwd) {
-    w.a_subtiles = ((M + tile_m - 1) / tile_m + (E - 1)) * (tile_m / kBM);
-    w.b_tiles = n_experts * ((N + tile_n - 1) / tile_n);
+    // sum over groups of ceil(rows_g / 128) <= ceil(M / 128) + E - 1
+    w.a_slabs = (M + kBM - 1) / kBM + (E - 1);
+    w.b_slabs = n_experts * ((N + kBM - 1) / kBM);
   } else {
-    w.a_subtiles = ((N + tile_m - 1) / tile_m) * (tile_m / kBM);
-    w.b_tiles = (K + tile_n - 1) / tile_n;
+    w.a_slabs = (N + kBM - 1) / kBM;
+    w.b_slabs = (K + kBM - 1) / kBM;
   }
-  w.a_bytes = (w.a_subtiles * w.stages * 512 + 1023) / 1024 * 1024;
-  w.b_bytes = (w.b_tiles * w.stages * (tile_n / 128) * 512 + 1023) / 1024 * 1024;
+  w.a_bytes = (w.a_slabs * w.stages * 512 + 1023) / 1024 * 1024;
+  w.b_bytes = (w.b_slabs * w.stages * 512 + 1023) / 1024 * 1024;
   // one fp32 128 x tile_n partial per CTA; one counter per (tail tile, CTA
   // of the pair, epilogue warp), fewer tail tiles than pairs
   w.part_bytes = (long long)kMaxGridCtas * kBM * tile_n * 4;
@@ -293,8 +297,11 @@ int resolve_cfg(const mxgg_gemm_config* user, GemmCfg* out, const char* what) {
     *out = g_default_cfg;
   }
   if (!user) return MXGG_OK;
-  if (user->reserved[0] || user->reserved[1] || user->reserved[2])
+  if (user->reserved[0] || user->reserved[1])
     return fail(MXGG_ERR_INVALID, "%s: mxgg_gemm_config.reserved must be zero", what);
+  if (user->scale_layout != MXGG_SCALE_ROW_MAJOR && user->scale_layout != MXGG_SCALE_BLOCKED)
+    return fail(MXGG_ERR_INVALID, "%s: unknown scale_layout %d", what, user->scale_layout);
+  out->scale_layout = user->scale_layout;
   if (int rc = check_cfg_fields(user->tile_m, user->tile_n, user->group_m, user->schedule, user->split_max, what))
     return rc;
   if (user->tile_m) out->tile_m = user->tile_m;
@@ -453,18 +460,25 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   uint8_t* ws_b = ws_a + ws.a_bytes;
   float* part_slots = reinterpret_cast<float*>(ws_b + ws.b_bytes);
   int* part_counters = reinterpret_cast<int*>(ws_b + ws.b_bytes + ws.part_bytes);
-  const bool split_tail = split_ok && cfg.schedule != MXGG_SCHED_TILES;
+  // A tile splits only if it has enough stages (the kernel's split_ways: at
+  // least 2 with a split_max, else at least 24): when none can, the split
+  // machinery -- and the zeroing of its counters -- stays off.
+  const long long max_stages = mode == kFwd ? ws.stages : ws.stages + 1;   // a group's tokens may straddle one more
+  const bool split_tail = split_ok && cfg.schedule != MXGG_SCHED_TILES &&
+                          (cfg.split_max > 0 ? max_stages >= 2 : max_stages >= 24);
+  const bool blocked = cfg.scale_layout == MXGG_SCALE_BLOCKED;
+  if (blocked && (route || !aligned(a_scale, 16) || !aligned(b_scale, 16)))
+    return fail(MXGG_ERR_INVALID, "%s: blocked scales must be 16-byte aligned (and are not taken by the "
+                "expert-parallel call)", what);
 
-  // 1) pack the row-major scales into the atoms the GEMM loads
-  {
+  if (blocked) {
+    // the scales are laid out already; only the split-tail counters need zeros
+    if (split_tail) MXGG_CUDA_TRY(cudaMemsetAsync(part_counters, 0, (size_t)ws.counter_bytes, stream));
+  } else {
+    // 1) pack the row-major scales into the blocked atoms the GEMM reads
     PackParams pp{};
     pp.mode = mode;
     pp.E = (int)E;
-    pp.M = (int)M;
-    pp.N = (int)N;
-    pp.K = (int)K;
-    pp.tile_m = tc.tile_m;
-    pp.tile_n = bn;
     pp.stages = (int)ws.stages;
     pp.offs = offs;
     pp.sfa = static_cast<const uint8_t*>(a_scale);
@@ -477,8 +491,9 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     else if (ld % 4 == 0 && aligned(a_scale, 4) && aligned(b_scale, 4)) pp.vec = 1;
     else pp.vec = 0;
     // A atoms the senders packed already: pack only B here
-    pp.a_subtiles = (route && route->a_atoms) ? 0 : (int)ws.a_subtiles;
-    pp.b_tiles = (int)ws.b_tiles;
+    pp.a_slabs = (route && route->a_atoms) ? 0 : (int)ws.a_slabs;
+    pp.b_slabs = (int)ws.b_slabs;
+    pp.b_height = (int)(mode == kFwd ? N : K);
     pp.a_out = ws_a;
     pp.b_out = ws_b;
     if (split_tail) {
@@ -486,7 +501,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
       pp.zero_count = ws.counter_bytes / 4;
     }
     const long long chunks = (ws.stages + 3) / 4;
-    const long long warps = ((long long)pp.a_subtiles + ws.b_tiles * (bn / 128)) * chunks;
+    const long long warps = ((long long)pp.a_slabs + pp.b_slabs) * chunks;
     const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
     pack_scales_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pp);
     MXGG_CUDA_TRY(cudaGetLastError());
@@ -578,10 +593,15 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
                      : make_tmap_2d(&maps.b, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)rows_b, (uint64_t)C,
                                     (uint64_t)C, kBK, (uint32_t)(bn / pair), CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  // the scale writers read the packed atoms directly; every index they form
-  // stays inside the a_subtiles x stages and b_tiles x stages atoms packed
-  p.sfa_atoms = static_cast<const uint8_t*>((route && route->a_atoms) ? route->a_atoms : ws_a);
-  p.sfb_atoms = ws_b;
+  // the scale writers read the packed atoms directly; every slab index they
+  // form is clamped inside the a_slabs x stages and b_slabs x stages atoms
+  if (blocked) {
+    p.sfa_atoms = static_cast<const uint8_t*>(a_scale);
+    p.sfb_atoms = static_cast<const uint8_t*>(b_scale);
+  } else {
+    p.sfa_atoms = static_cast<const uint8_t*>((route && route->a_atoms) ? route->a_atoms : ws_a);
+    p.sfb_atoms = ws_b;
+  }
   std::memset(&maps.out, 0, sizeof(maps.out));
   if (route) {
     // one map per destination with rows (the peers' outputs take TMA stores too)
@@ -825,15 +845,15 @@ int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols,
   switch (x_dtype) {
     case MXGG_DTYPE_BF16:
       quantize_rows_e4m3<__nv_bfloat16, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(x), rows, cols, qq, ss, scale_layout);
+          static_cast<const __nv_bfloat16*>(x), rows, cols, qq, ss, scale_layout, ScaleSegs{});
       break;
     case MXGG_DTYPE_F16:
       quantize_rows_e4m3<__half, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
-          static_cast<const __half*>(x), rows, cols, qq, ss, scale_layout);
+          static_cast<const __half*>(x), rows, cols, qq, ss, scale_layout, ScaleSegs{});
       break;
     default:
       quantize_rows_e4m3<float, true><<<(unsigned)blocks, nthreads, 0, stream>>>(
-          static_cast<const float*>(x), rows, cols, qq, ss, scale_layout);
+          static_cast<const float*>(x), rows, cols, qq, ss, scale_layout, ScaleSegs{});
   }
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
@@ -884,15 +904,18 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
     switch (x_dtype) {
       case MXGG_DTYPE_BF16:
         quantize_rows_e4m3<__nv_bfloat16><<<(unsigned)blocks, nthreads, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+            static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout,
+            ScaleSegs{});
         break;
       case MXGG_DTYPE_F16:
         quantize_rows_e4m3<__half><<<(unsigned)blocks, nthreads, 0, stream>>>(
-            static_cast<const __half*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+            static_cast<const __half*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout,
+            ScaleSegs{});
         break;
       default:
         quantize_rows_e4m3<float><<<(unsigned)blocks, nthreads, 0, stream>>>(
-            static_cast<const float*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout);
+            static_cast<const float*>(x), rows, cols, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales), scale_layout,
+            ScaleSegs{});
     }
   } else if (mode == MXGG_QUANT_COLS) {
     if (rows % 32 != 0) return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: rows=%lld not a multiple of 32", (long long)rows);
@@ -914,6 +937,56 @@ int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, voi
     }
   } else {
     return fail(MXGG_ERR_INVALID, "mxgg_quantize_mx: unknown mode %d", mode);
+  }
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int64_t mxgg_blocked_scale_bytes(int64_t rows, int64_t contraction, int64_t n_segments) {
+  if (rows < 0 || contraction < 0 || n_segments < 1) return -1;
+  const int64_t slabs = (rows + 127) / 128 + (n_segments - 1);
+  return slabs * ((contraction + 127) / 128) * 512;
+}
+
+int mxgg_quantize_mx_blocked(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
+                             const int32_t* segment_end_offsets, int64_t n_segments, int64_t segment_rows,
+                             void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const char* what = "mxgg_quantize_mx_blocked";
+  if (rows < 0 || cols < 0) return fail(MXGG_ERR_INVALID, "%s: negative size", what);
+  if (n_segments < 1 || n_segments > kMaxScaleSegments)
+    return fail(MXGG_ERR_INVALID, "%s: n_segments=%lld outside 1..%d", what, (long long)n_segments,
+                kMaxScaleSegments);
+  if (!segment_end_offsets && segment_rows < 1)
+    return fail(MXGG_ERR_INVALID, "%s: uniform segments need segment_rows >= 1", what);
+  if (rows == 0 || cols == 0) return MXGG_OK;
+  if (!x || !q || !scales) return fail(MXGG_ERR_INVALID, "%s: null pointer", what);
+  if (x_dtype != MXGG_DTYPE_BF16 && x_dtype != MXGG_DTYPE_F16 && x_dtype != MXGG_DTYPE_F32)
+    return fail(MXGG_ERR_INVALID, "%s: unknown x_dtype %d", what, x_dtype);
+  if (cols % 32 != 0) return fail(MXGG_ERR_INVALID, "%s: cols=%lld not a multiple of 32", what, (long long)cols);
+  if (!aligned(x, 16) || !aligned(q, 8))
+    return fail(MXGG_ERR_INVALID, "%s: x must be 16-byte and q 8-byte aligned", what);
+  if (rows >= ((int64_t)1 << 31)) return fail(MXGG_ERR_UNSUPPORTED, "%s: rows beyond 2^31", what);
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const ScaleSegs segs{segment_end_offsets, (int)n_segments, segment_end_offsets ? 0 : (long long)segment_rows};
+  const int nthreads = 256;
+  const long long work = rows * cols / 8;
+  const long long blocks = std::max(1LL, std::min<long long>((work + nthreads - 1) / nthreads, (long long)st->num_sms * 8));
+  uint8_t* qq = static_cast<uint8_t*>(q);
+  uint8_t* ss = static_cast<uint8_t*>(scales);
+  switch (x_dtype) {
+    case MXGG_DTYPE_BF16:
+      quantize_rows_e4m3<__nv_bfloat16><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), rows, cols, qq, ss, kScaleBlockedSeg, segs);
+      break;
+    case MXGG_DTYPE_F16:
+      quantize_rows_e4m3<__half><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const __half*>(x), rows, cols, qq, ss, kScaleBlockedSeg, segs);
+      break;
+    default:
+      quantize_rows_e4m3<float><<<(unsigned)blocks, nthreads, 0, stream>>>(
+          static_cast<const float*>(x), rows, cols, qq, ss, kScaleBlockedSeg, segs);
   }
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
@@ -972,17 +1045,14 @@ int32_t mxgg_query_tile_m(void) {
 
 int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments) {
   if (M < 0 || K < 0 || n_segments < 1) return -1;
-  int64_t best = 0;
-  for (int tm : {128, 256}) best = std::max<int64_t>(best, plan_workspace(kFwd, M, 128, K, n_segments, 1, tm, 128).a_bytes);
-  return best;
+  return plan_workspace(kFwd, M, 128, K, n_segments, 1, 256, 256).a_bytes;
 }
 
 int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
-                      int64_t n_segments, int32_t tile_m, void* out, void* stream) {
-  if (rows < 0 || K <= 0 || K % 32 != 0 || n_segments < 1 || n_segments > kMaxGroups ||
-      (tile_m != 128 && tile_m != 256))
-    return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: bad sizes (rows %lld, K %lld, segments %lld, tile_m %d)",
-                (long long)rows, (long long)K, (long long)n_segments, (int)tile_m);
+                      int64_t n_segments, void* out, void* stream) {
+  if (rows < 0 || K <= 0 || K % 32 != 0 || n_segments < 1 || n_segments > kMaxGroups)
+    return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: bad sizes (rows %lld, K %lld, segments %lld)",
+                (long long)rows, (long long)K, (long long)n_segments);
   if (rows == 0) return MXGG_OK;
   if (!a_scale || !segment_end_offsets || !out) return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: null pointer");
   DeviceState* st = nullptr;
@@ -990,11 +1060,6 @@ int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, i
   PackParams pp{};
   pp.mode = kFwd;
   pp.E = (int)n_segments;
-  pp.M = (int)rows;
-  pp.N = 128;
-  pp.K = (int)K;
-  pp.tile_m = tile_m;
-  pp.tile_n = 128;
   pp.stages = (int)((K + kBK - 1) / kBK);
   pp.offs = segment_end_offsets;
   pp.sfa = static_cast<const uint8_t*>(a_scale);
@@ -1004,12 +1069,13 @@ int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, i
   pp.sf_ld = K / 32;
   const int64_t ld = K / 32;
   pp.vec = (ld % 16 == 0 && aligned(a_scale, 16)) ? 4 : ((ld % 4 == 0 && aligned(a_scale, 4)) ? 1 : 0);
-  pp.a_subtiles = (int)(((rows + tile_m - 1) / tile_m + (n_segments - 1)) * (tile_m / kBM));
-  pp.b_tiles = 0;
+  pp.a_slabs = (int)((rows + kBM - 1) / kBM + (n_segments - 1));
+  pp.b_slabs = 0;
+  pp.b_height = 1;
   pp.a_out = static_cast<uint8_t*>(out);
   pp.b_out = nullptr;
   const long long chunks = (pp.stages + 3) / 4;
-  const long long warps = (long long)pp.a_subtiles * chunks;
+  const long long warps = (long long)pp.a_slabs * chunks;
   const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
   pack_scales_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pp);
   MXGG_CUDA_TRY(cudaGetLastError());

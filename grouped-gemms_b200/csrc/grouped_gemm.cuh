@@ -120,8 +120,11 @@ struct GemmParams {
   int split_max;             // most pieces per split tile (0: about sqrt(stages))
   float* part_slots;         // split tiles: one fp32 128 x BN partial per CTA of the grid
   int* part_counters;        // split tiles: arrivals per (tail tile, CTA of the pair, epilogue warp), zeroed before the launch
-  // Packed scale atoms (pack_scales_kernel's layout): A [sub-tile][stage][512 B],
-  // B [tile][stage][BN/128][512 B].  The scale writers read them directly.
+  // Scale atoms in the blocked layout (scale_pack.cuh): [slab][stage][512 B],
+  // one slab per 128 rows -- fwd A: the slabs of each group in turn, every
+  // group starting a new slab; fwd B: ceil(N / 128) slabs per expert; wgrad:
+  // ceil(rows / 128) slabs of each operand.  The scale writers read them
+  // directly.
   const uint8_t* sfa_atoms;
   const uint8_t* sfb_atoms;
   uint32_t* status;          // error word (device memory), 0 = ok
@@ -172,8 +175,9 @@ struct Unit {
   int st_count;      // number of stages (0 = the output tile is all zeros)
   int c_begin;       // contraction range [c_begin, c_end), multiples of 32
   int c_end;
-  int a_sub;         // packed A-scale sub-tile of the tile's first 128 rows
-  int b_tile;        // packed B-scale tile
+  int a_sub;         // A scale slab of the tile's first 128 rows (the pair's second CTA: a_sub + 1)
+  int b_tile;        // B scale slab of the tile's first 128 columns
+  int b_last;        // last B scale slab of the tile's expert (fwd) or operand (wgrad)
   int dst;           // output destination (0 unless expert-parallel routing)
   int src;           // rank the rows come from (streaming dispatch)
   // a stage range of a tail tile that other CTA pairs share
@@ -210,6 +214,7 @@ struct SmemLayout {
   int g_start[kMaxGroups];
   int g_end[kMaxGroups];
   int g_cum[kMaxGroups + 1];
+  int g_cum128[kMaxGroups + 1];   // fwd: exclusive prefix of 128-row scale slabs per group
   int g_order[kMaxGroups];   // wgrad: groups by decreasing token count
   int g_expert[kMaxGroups];  // fwd: B slice of each group
   int g_dst[kMaxGroups];     // fwd, expert parallel: output destination of each group
@@ -222,14 +227,15 @@ struct SmemLayout {
 
 __device__ __forceinline__ int cdiv_i(int a, int b) { return (a + b - 1) / b; }
 
-// Group table: start/end rows (fwd) or token ranges (wgrad) per group and an
-// exclusive prefix of tile rows (of `tile_m` rows each).  Offsets are clamped
+// Group table: start/end rows (fwd) or token ranges (wgrad) per group, an
+// exclusive prefix of tile rows (of `tile_m` rows each) and one of 128-row
+// scale slabs.  Offsets are clamped
 // into [0, R] and made monotone so that out-of-range or decreasing offsets can
 // never address memory outside the operands.
 template <class S>
 __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, int R, int tile_m) {
   const int lane = ptx::lane_id();
-  int carry_max = 0, carry_sum = 0;
+  int carry_max = 0, carry_sum = 0, carry_sum128 = 0;
   for (int base = 0; base < p.E; base += 32) {
     const int i = base + lane;
     int c = 0;
@@ -244,21 +250,31 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
     if (lane == 0) prev = carry_max;
     const int start = prev, end = v;
     int t = (i < p.E) ? cdiv_i(end - start, tile_m) : 0;
-    int incl = t;
+    int t128 = (i < p.E) ? cdiv_i(end - start, kBM) : 0;
+    int incl = t, incl128 = t128;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       int u = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += u;
+      int u128 = __shfl_up_sync(0xffffffffu, incl128, o);
+      if (lane >= o) {
+        incl += u;
+        incl128 += u128;
+      }
     }
     if (i < p.E) {
       sm->g_start[i] = start;
       sm->g_end[i] = end;
       sm->g_cum[i] = carry_sum + incl - t;
+      sm->g_cum128[i] = carry_sum128 + incl128 - t128;
     }
     carry_max = __shfl_sync(0xffffffffu, v, 31);
     carry_sum += __shfl_sync(0xffffffffu, incl, 31);
+    carry_sum128 += __shfl_sync(0xffffffffu, incl128, 31);
   }
-  if (lane == 0) sm->g_cum[p.E] = carry_sum;
+  if (lane == 0) {
+    sm->g_cum[p.E] = carry_sum;
+    sm->g_cum128[p.E] = carry_sum128;
+  }
   // fwd: which B slice each group multiplies (clamped, so a bad index can
   // never address memory outside B)
   for (int i = lane; i < p.E; i += 32) {
@@ -337,8 +353,10 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     u.st_count = cdiv_i(p.K, kBK);
     u.c_begin = 0;
     u.c_end = p.K;
-    u.a_sub = m * (TILE_M / kBM);
-    u.b_tile = ge * NT + n;
+    u.a_sub = sm->g_cum128[g] + (m - sm->g_cum[g]) * (TILE_M / kBM);
+    const int NB = cdiv_i(p.N, kBM);
+    u.b_tile = ge * NB + n * (BN / kBM);
+    u.b_last = ge * NB + NB - 1;
   } else {
     const int NT = cdiv_i(p.N, TILE_M);
     const int KT = cdiv_i(p.K, BN);
@@ -370,7 +388,8 @@ __device__ __forceinline__ Unit decode_unit(const S* sm, const GemmParams& p, in
     u.c_begin = s;
     u.c_end = e;
     u.a_sub = nt * (TILE_M / kBM);
-    u.b_tile = kt;
+    u.b_tile = kt * (BN / kBM);
+    u.b_last = cdiv_i(p.K, kBM) - 1;
   }
   return u;
 }
@@ -1132,6 +1151,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp - kSfWarp0;
     const uint32_t lane_base = tmem_base + ((uint32_t)(32 * q) << 16) + kSfCol0;
     constexpr int kB = BN / 128;                  // B atoms per stage
+    // last A slab: the groups' slabs end at g_cum128[E] (the exact size of a
+    // blocked scale tensor the caller laid out, e.g. with the quantiser)
+    const int a_last = (p.mode == kFwd) ? sm->g_cum128[p.E] - 1 : cdiv_i(p.N, kBM) - 1;
     // load cursor over the (unit, stage) sequence every role walks
     int lk = 0, ls = 0;
     Unit lu;
@@ -1168,13 +1190,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(f) : "l"(p.src_flags + lu.src) : "memory");
         ready |= 1u << lu.src;
       }
+      // slabs past a group's or an expert's rows hold other rows' scales (or
+      // are clamped to the last slab): they only feed rows that are never stored
       const long long st = lu.st_begin + ls;
-      r[0] = __ldg(reinterpret_cast<const uint4*>(p.sfa_atoms + ((long long)(lu.a_sub + (int)rank) * p.stages + st) * 512) +
-                   lane);
+      const int sa = min(lu.a_sub + (int)rank, a_last);
+      r[0] = __ldg(reinterpret_cast<const uint4*>(p.sfa_atoms + ((long long)sa * p.stages + st) * 512) + lane);
 #pragma unroll
-      for (int b = 0; b < kB; ++b)
-        r[1 + b] = __ldg(reinterpret_cast<const uint4*>(p.sfb_atoms + (((long long)lu.b_tile * p.stages + st) * kB + b) * 512) +
-                         lane);
+      for (int b = 0; b < kB; ++b) {
+        const int sb = min(lu.b_tile + b, lu.b_last);
+        r[1 + b] = __ldg(reinterpret_cast<const uint4*>(p.sfb_atoms + ((long long)sb * p.stages + st) * 512) + lane);
+      }
     };
     // the atoms are written by the scale-pack kernel that precedes this grid
     ptx::griddep_wait();

@@ -21,7 +21,10 @@
 //           (to_mx(x.t().contiguous()) fused into one pass) -- the operand
 //           layout the wgrad pass consumes (scales along tokens).
 // Scales are written row-major (the reference layout) or, on request, in the
-// 128x4 blocked scale-factor atom layout used by Blackwell block-scaled MMAs.
+// 128x4 blocked scale-factor atom layout used by Blackwell block-scaled MMAs:
+// over the whole matrix (kScaleBlocked), or per row segment (kScaleBlockedSeg:
+// every segment starts a new 128-row slab -- the layout the grouped GEMM
+// reads for forward A (segments = groups) and B (segments = experts)).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -34,7 +37,25 @@
 namespace mxgg {
 
 enum : int { kInBF16 = 0, kInF16 = 1, kInF32 = 2 };
-enum : int { kScaleRowMajor = 0, kScaleBlocked = 1 };
+enum : int { kScaleRowMajor = 0, kScaleBlocked = 1, kScaleBlockedSeg = 2 };
+constexpr int kMaxScaleSegments = 256;
+
+// Row segments of a kScaleBlockedSeg scale tensor: device cumulative ends
+// (offs, n segments) or, with offs null, uniform segments of seg_rows rows.
+struct ScaleSegs {
+  const int32_t* offs;
+  int n;
+  long long seg_rows;
+};
+
+// Per-CTA table of a ScaleSegs with device offsets: clamped, monotone
+// segment starts, the end of the last segment and the exclusive prefix of the
+// segments' 128-row slabs.
+struct SegTable {
+  int start[kMaxScaleSegments];
+  int cum[kMaxScaleSegments + 1];
+  int end;
+};
 
 __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
@@ -136,6 +157,70 @@ __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c,
   return atom * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
 }
 
+// one warp fills `t` from segs.offs (rows: the scale matrix height)
+__device__ __forceinline__ void build_seg_table(SegTable& t, const ScaleSegs& segs, long long rows) {
+  const int lane = threadIdx.x & 31;
+  int carry_max = 0, carry_sum = 0;
+  for (int base = 0; base < segs.n; base += 32) {
+    const int i = base + lane;
+    int c = 0;
+    if (i < segs.n) c = (int)min(max((long long)__ldg(segs.offs + i), 0LL), rows);
+    int v = (i < segs.n) ? max(c, carry_max) : carry_max;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v = max(v, u);
+    }
+    int prev = __shfl_up_sync(0xffffffffu, v, 1);
+    if (lane == 0) prev = carry_max;
+    const int n128 = (i < segs.n) ? (v - prev + 127) / 128 : 0;
+    int incl = n128;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (i < segs.n) {
+      t.start[i] = prev;
+      t.cum[i] = carry_sum + incl - n128;
+    }
+    carry_max = __shfl_sync(0xffffffffu, v, 31);
+    carry_sum += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) {
+    t.cum[segs.n] = carry_sum;
+    t.end = carry_max;
+  }
+}
+
+// Offset of scale (r, c) of a (R, C) scale matrix in the per-segment blocked
+// layout, or -1 for a row no segment holds (at or past the last segment's
+// end).  Segment g's rows fill slabs cum[g], cum[g] + 1, ...: row r of the
+// segment is row r % 128 of slab cum[g] + r / 128.
+__device__ __forceinline__ long long blocked_seg_sf_offset(long long r, long long c, long long C, const ScaleSegs& segs,
+                                                           const SegTable& t) {
+  long long slab, rr;
+  if (!segs.offs) {
+    const long long g = r / segs.seg_rows;
+    if (g >= segs.n) return -1;
+    rr = r - g * segs.seg_rows;
+    slab = g * ((segs.seg_rows + 127) / 128) + rr / 128;
+  } else {
+    if (r >= t.end) return -1;
+    // the segment holding r: the last one starting at or before it (an empty
+    // segment shares its start with the next one)
+    int lo = 0, hi = segs.n - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (t.start[mid] <= r) lo = mid; else hi = mid - 1;
+    }
+    rr = r - t.start[lo];
+    slab = t.cum[lo] + rr / 128;
+  }
+  const long long cb = (C + 3) / 4;
+  return (slab * cb + c / 4) * 512 + (rr % 32) * 16 + ((rr % 128) / 32) * 4 + (c % 4);
+}
+
 // -------------------------------------------------------------- row mode
 // x: (R, C) contiguous, C % 32 == 0.  q: (R, C) e4m3.  s: scales.
 // Each thread handles kUnroll 8-element slots a grid-stride apart and issues
@@ -144,8 +229,13 @@ __device__ __forceinline__ long long blocked_sf_offset(long long r, long long c,
 template <typename T, bool kFp4 = false>
 __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ x, long long R, long long C,
                                                           uint8_t* __restrict__ q, uint8_t* __restrict__ s,
-                                                          int scale_layout) {
+                                                          int scale_layout, const ScaleSegs segs) {
   constexpr int kUnroll = 4;
+  __shared__ SegTable seg_table;
+  if (scale_layout == kScaleBlockedSeg && segs.offs) {
+    if (threadIdx.x < 32) build_seg_table(seg_table, segs, R);
+    __syncthreads();
+  }
   const long long total8 = R * C / 8;                  // a multiple of 4: a 32-block never straddles slots
   const long long stride = (long long)gridDim.x * blockDim.x;
   const int lane = threadIdx.x & 31;
@@ -189,9 +279,13 @@ __global__ void __launch_bounds__(256) quantize_rows_e4m3(const T* __restrict__ 
         const long long blk = i / 4;
         if (scale_layout == kScaleRowMajor) {
           s[blk] = (uint8_t)sc;
-        } else {
+        } else if (scale_layout == kScaleBlocked) {
           const long long r = blk / SC, c = blk - r * SC;
           s[blocked_sf_offset(r, c, SC)] = (uint8_t)sc;
+        } else {
+          const long long r = blk / SC, c = blk - r * SC;
+          const long long o = blocked_seg_sf_offset(r, c, SC, segs, seg_table);
+          if (o >= 0) s[o] = (uint8_t)sc;
         }
       }
     }

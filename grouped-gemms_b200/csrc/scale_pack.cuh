@@ -2,21 +2,25 @@
 //
 // The reference's callers hand over e8m0 scales row-major, (rows,
 // contraction/32) (utils.to_mx, utils.py:67-105).  The GEMM's scale writers
-// want, per 128-row slab and per 128-element contraction stage, one 512-byte
-// atom laid out as byte (r % 32) * 16 + (r / 32) * 4 + k (row r, k-block k):
-// lane r % 32 of the atom is the 16 bytes that TMEM lane r % 32 of every
-// quarter holds in the block-scaled MMA's scale layout.  This pass
-// writes exactly the atoms the GEMM will read, in the order it reads them, so
-// the GEMM's producer can fetch a stage's scales with one TMA load each
-// (instead of the reference's per-call host re-layout, forward.py:537-561):
+// read them in the blocked layout: per 128-row slab and per 128-element
+// contraction stage one 512-byte atom, byte (r % 32) * 16 + (r / 32) * 4 + k
+// for row r of the slab and k-block k of the stage -- lane r % 32 of the atom
+// is the 16 bytes TMEM lane r % 32 of every quarter holds in the block-scaled
+// MMA's scale layout.  Atoms are stored [slab][stage][512 B], slabs in order:
 //
-//   A side  [sub-tile][stage][512 B]        sub-tile = 128 rows of a tile
-//   B side  [tile][stage][BN/128][512 B]    all BN rows of an n-tile
+//   forward / dgrad A   each group's rows in 128-row slabs, a new slab at
+//                       every group start (group g's slabs follow those of
+//                       groups 0 .. g-1)
+//   forward / dgrad B   ceil(N / 128) slabs per expert
+//   wgrad A and B       ceil(rows / 128) slabs over the whole operand
 //
-// Forward tiles follow the group boundaries (a tile never spans two groups),
-// so the A-side sub-tile of (group g, tile mt, half h) starts at row
-// start_g + mt * tile_m + 128 h.  Rows past the operand are clamped: their
-// scales only feed output rows that are never stored.
+// This is torch's blocked scale layout for grouped MXFP8 GEMMs (to_blocked of
+// each group's / expert's scale rows, concatenated); it depends on neither
+// the tile shape nor the schedule, so a quantiser can write it once
+// (mxgg_quantize_mx's blocked modes) and the GEMM takes it as is.  This pass
+// converts row-major scales into it (the reference instead re-lays scales on
+// the host for every call, forward.py:537-561).  Rows past the operand are
+// clamped: their scales only feed output rows that are never stored.
 #pragma once
 
 #include <cstdint>
@@ -27,22 +31,20 @@ namespace mxgg {
 
 struct PackParams {
   int mode;              // kFwd / kWgrad
-  int E;
-  int M, N, K;           // as GemmParams
-  int tile_m;            // 128 * PAIR
-  int tile_n;            // BN
+  int E;                 // fwd: groups of A rows
   int stages;            // ceil(contraction / 128)
-  const int32_t* offs;
+  const int32_t* offs;   // fwd: group end offsets of the A rows
   const uint8_t* sfa;    // (rows_a, sf_ld) row-major
   const uint8_t* sfb;    // (rows_b, sf_ld) row-major
   int rows_a, rows_b;
   long long sf_ld;       // bytes per scale row
   int vec;               // 4: 16-byte row loads are aligned, 1: 4-byte, 0: bytes
-  int a_subtiles;        // A-side sub-tiles provisioned in the workspace
-  int b_tiles;           // B-side tiles (fwd: experts x n-tiles)
+  int a_slabs;           // A slabs to write (fwd: an upper bound; slabs past the groups' are skipped)
+  int b_slabs;           // B slabs to write
+  int b_height;          // rows per B matrix (fwd: N, one matrix per expert; wgrad: K)
   uint8_t* a_out;
   uint8_t* b_out;
-  int* zero;             // stream-K arrival counters to clear (or null)
+  int* zero;             // split-tail arrival counters to clear (or null)
   long long zero_count;
 };
 
@@ -65,7 +67,7 @@ __device__ __forceinline__ void load_row_words(const uint8_t* row, const PackPar
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const long long cc = cw + b;
-        const uint32_t v = (cc < p.sf_ld) ? (uint32_t)__ldg(row + cc) : 127u;
+        const uint32_t v = (cc < p.sf_ld) ? (uint32_t)__ldg(row + cc) : 0u;
         x |= v << (8 * b);
       }
       w[j] = x;
@@ -84,14 +86,14 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
   // need nothing from this kernel, and the roles that read the atoms and
   // counters written here wait for this grid to finish (griddepcontrol.wait).
   ptx::griddep_launch_dependents();
-  if (p.mode == kFwd) {
+  if (p.mode == kFwd && p.a_slabs > 0) {
     if (warp == 0) {
-      // same group table as the GEMM: clamped, monotone starts; tile prefix
+      // the GEMM's group table: clamped, monotone starts; 128-row slab prefix
       int carry_max = 0, carry_sum = 0;
       for (int base = 0; base < p.E; base += 32) {
         const int i = base + lane;
         int c = 0;
-        if (i < p.E) c = min(max(__ldg(p.offs + i), 0), p.M);
+        if (i < p.E) c = min(max(__ldg(p.offs + i), 0), p.rows_a);
         int v = (i < p.E) ? max(c, carry_max) : carry_max;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -100,7 +102,7 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
         }
         int prev = __shfl_up_sync(0xffffffffu, v, 1);
         if (lane == 0) prev = carry_max;
-        int t = (i < p.E) ? cdiv_i(v - prev, p.tile_m) : 0;
+        int t = (i < p.E) ? cdiv_i(v - prev, 128) : 0;
         int incl = t;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -123,53 +125,39 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
          i += (long long)gridDim.x * blockDim.x)
       p.zero[i] = 0;
   }
-  const int halves = p.tile_m / 128;
-  const int bsub = p.tile_n / 128;
   const int chunks = (p.stages + 3) / 4;
-  const int a_work = p.a_subtiles * chunks;
-  const int b_work = p.b_tiles * bsub * chunks;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
-  for (int wi = blockIdx.x * (blockDim.x >> 5) + warp; wi < a_work + b_work; wi += nwarps) {
+  const long long a_work = (long long)p.a_slabs * chunks;
+  const long long b_work = (long long)p.b_slabs * chunks;
+  const int nb = cdiv_i(max(p.b_height, 1), 128);
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + warp; wi < a_work + b_work; wi += nwarps) {
     const bool side_a = wi < a_work;
-    const int idx = side_a ? wi : wi - a_work;
-    const int q = idx % chunks;
-    const int slab = idx / chunks;      // A: sub-tile; B: tile * bsub + b
+    const long long idx = side_a ? wi : wi - a_work;
+    const int q = (int)(idx % chunks);
+    const int slab = (int)(idx / chunks);
     long long row0;
     const uint8_t* sf;
     int rows_total;
-    uint8_t* dst0;
-    long long dst_stage_stride;
     if (side_a) {
       sf = p.sfa;
       rows_total = p.rows_a;
-      const int m = slab / halves, h = slab % halves;
       if (p.mode == kFwd) {
-        if (m >= s_cum[p.E]) continue;   // beyond the tiles this call produces
+        if (slab >= s_cum[p.E]) continue;   // beyond the slabs of this call's groups
         int lo = 0, hi = p.E - 1;
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
-          if (s_cum[mid] <= m) lo = mid; else hi = mid - 1;
+          if (s_cum[mid] <= slab) lo = mid; else hi = mid - 1;
         }
-        row0 = (long long)s_start[lo] + (long long)(m - s_cum[lo]) * p.tile_m + 128LL * h;
+        row0 = (long long)s_start[lo] + 128LL * (slab - s_cum[lo]);
       } else {
         row0 = 128LL * slab;
       }
-      dst0 = p.a_out + (long long)slab * p.stages * 512;
-      dst_stage_stride = 512;
     } else {
       sf = p.sfb;
       rows_total = p.rows_b;
-      const int tile = slab / bsub, b = slab % bsub;
-      if (p.mode == kFwd) {
-        const int NT = cdiv_i(p.N, p.tile_n);
-        const int g = tile / NT, nt = tile % NT;
-        row0 = (long long)g * p.N + (long long)nt * p.tile_n + 128LL * b;
-      } else {
-        row0 = (long long)tile * p.tile_n + 128LL * b;
-      }
-      dst0 = p.b_out + ((long long)tile * p.stages * bsub + b) * 512;
-      dst_stage_stride = 512LL * bsub;
+      row0 = (long long)(slab / nb) * p.b_height + 128LL * (slab % nb);
     }
+    uint8_t* dst0 = (side_a ? p.a_out : p.b_out) + (long long)slab * p.stages * 512;
     uint32_t w[4][4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -180,7 +168,7 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
     for (int j = 0; j < 4; ++j) {
       const int st = 4 * q + j;
       if (st < p.stages) {
-        uint4* d = reinterpret_cast<uint4*>(dst0 + (long long)st * dst_stage_stride + lane * 16);
+        uint4* d = reinterpret_cast<uint4*>(dst0 + (long long)st * 512 + lane * 16);
         *d = make_uint4(w[0][j], w[1][j], w[2][j], w[3][j]);
       }
     }

@@ -12,3 +12,12 @@ _UNAVAILABLE_MSG = "MXFP8 grouped-GEMM kernels require an sm_100 (B200) GPU and 
 
 _mxfp8_available = mxgg.available()
 _rocm_mxfp8_available = _mxfp8_available
+
+
+def _scale_layout(name: str) -> int:
+    """``scale_layout`` keyword -> the library's constant."""
+    from mxgg import _lib
+    layouts = {"row_major": _lib.SCALE_ROW_MAJOR, "blocked": _lib.SCALE_BLOCKED}
+    if name not in layouts:
+        raise ValueError(f"scale_layout must be 'row_major' or 'blocked', got {name!r}")
+    return layouts[name]

@@ -14,7 +14,7 @@ import torch
 import mxgg
 from mxgg import tune as _tune
 
-from ._common import _UNAVAILABLE_MSG, _mxfp8_available
+from ._common import _UNAVAILABLE_MSG, _mxfp8_available, _scale_layout
 
 
 def triton_mxfp8_wgrad(
@@ -30,6 +30,7 @@ def triton_mxfp8_wgrad(
     num_warps: int = 8,
     num_stages: int = 2,
     out: torch.Tensor = None,
+    scale_layout: str = "row_major",
 ) -> torch.Tensor:
     """MXFP8 weight gradient: ``grad_W[g] = grad_output[group_g]^T @ input_act[group_g]``.
 
@@ -43,12 +44,17 @@ def triton_mxfp8_wgrad(
     ``out`` (not in the reference): an existing fp32 ``(E, N, K)`` gradient
     buffer to accumulate into (``out += grad_W``, one deterministic add per
     element); it is returned.
+
+    ``scale_layout`` (not in the reference): ``"blocked"`` takes both scale
+    tensors in the blocked layout ``utils.to_mx_dim1_blocked`` writes (one
+    re-layout launch fewer; bit-identical results).
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
+    layout = _scale_layout(scale_layout)
     # a tuned config for this call shape (mxgg.tune), passed with the call
     cfg = _tune.call_config(_tune.pick("wgrad", group_end_offsets.shape[0], go_t.shape[0], ia_t.shape[0]))
     if out is not None:
-        mxgg.ops.wgrad_accumulate(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out, cfg)
+        mxgg.ops.wgrad_accumulate(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out, cfg, layout)
         return out
-    return mxgg.ops.wgrad(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype, cfg)
+    return mxgg.ops.wgrad(go_t, go_scale, ia_t, ia_scale, group_end_offsets, out_dtype, cfg, layout)

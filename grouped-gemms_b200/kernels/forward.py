@@ -19,7 +19,7 @@ import torch
 import mxgg
 from mxgg import tune as _tune
 
-from ._common import _UNAVAILABLE_MSG, _mxfp8_available
+from ._common import _UNAVAILABLE_MSG, _mxfp8_available, _scale_layout
 
 
 def triton_mxfp8_grouped_mm(
@@ -41,6 +41,7 @@ def triton_mxfp8_grouped_mm(
     kpack: int = 1,
     w_cache_modifier: str = None,
     x_evict_policy: str = None,
+    scale_layout: str = "row_major",
 ) -> torch.Tensor:
     """MXFP8 grouped GEMM: ``output[g] = input_act[group_g] @ weight[g]^T``.
 
@@ -58,9 +59,17 @@ def triton_mxfp8_grouped_mm(
     e2m1 values per byte, from ``utils.to_mx(w, elem_dtype=torch.float4_e2m1fn_x2)``)
     with the same ``(E, N, K//32)`` scales; the product runs on the same
     block-scaled tensor-core path.  The reference has no MXFP4 path.
+
+    ``scale_layout`` (not in the reference): ``"row_major"`` takes the
+    reference's scale matrices, re-laid on the GPU for the tensor cores on
+    every call (one extra launch); ``"blocked"`` takes them already in that
+    layout, as ``utils.to_mx_grouped_blocked`` writes them (activation scales
+    per group of ``group_end_offsets``, weight scales per expert), and the
+    call is the GEMM launch alone.  The results are bit-identical.
     """
     if not _mxfp8_available:
         raise NotImplementedError(_UNAVAILABLE_MSG)
+    layout = _scale_layout(scale_layout)
     M, K = input_act.shape
     E, N, K2 = weight.shape
     if weight.dtype == torch.float4_e2m1fn_x2:
@@ -68,12 +77,12 @@ def triton_mxfp8_grouped_mm(
         experts = torch.arange(E, dtype=torch.int32, device=weight.device)
         return mxgg.ops.grouped_mm_segments(input_act, weight, input_act_scales, weight_scales,
                                             group_end_offsets, experts, out_dtype,
-                                            _tune.call_config(_tune.pick("fwd", E, N, K)))
+                                            _tune.call_config(_tune.pick("fwd", E, N, K)), layout)
     assert K == K2, f"K mismatch: A={K}, B={K2}"
     # a tuned config for this call shape (mxgg.tune), passed with the call;
     # None: the library's choice
     return mxgg.ops.grouped_mm(input_act, weight, input_act_scales, weight_scales, group_end_offsets, out_dtype,
-                               _tune.call_config(_tune.pick("fwd", E, N, K)))
+                               _tune.call_config(_tune.pick("fwd", E, N, K)), layout)
 
 
 def mxfp8_grouped_mm_to_mx(

@@ -47,17 +47,22 @@ FMT_E4M3, FMT_E2M1 = 0, 1
 
 class GemmConfig(ctypes.Structure):
     """``mxgg_gemm_config``: a call's tile and schedule choice (0 = the
-    process default, which defaults to the library's heuristic)."""
+    process default, which defaults to the library's heuristic) and the
+    layout of the scales it is given (SCALE_ROW_MAJOR or SCALE_BLOCKED)."""
     _fields_ = [("tile_m", ctypes.c_int32), ("tile_n", ctypes.c_int32), ("group_m", ctypes.c_int32),
-                ("schedule", ctypes.c_int32), ("split_max", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+                ("schedule", ctypes.c_int32), ("split_max", ctypes.c_int32), ("scale_layout", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 2)]
 
 
-def gemm_config(cfg):
+def gemm_config(cfg, scale_layout: int = SCALE_ROW_MAJOR):
     """A pointer to a GemmConfig for `cfg` -- a (tile_m, tile_n, group_m,
-    schedule, split_max) sequence -- or None for the process defaults."""
-    if cfg is None:
+    schedule, split_max) sequence, or None for the process defaults -- and
+    `scale_layout`; None when both are defaults."""
+    if cfg is None and scale_layout == SCALE_ROW_MAJOR:
         return None
-    return ctypes.pointer(GemmConfig(*[int(v) for v in cfg]))
+    vals = [int(v) for v in (cfg if cfg is not None else ())]
+    vals += [0] * (5 - len(vals))
+    return ctypes.pointer(GemmConfig(*vals[:5], int(scale_layout)))
 
 
 # every symbol include/mxgg.h declares, with (restype, argtypes)
@@ -90,7 +95,7 @@ SIGNATURES = {
                                   _i32, _vp, _vp, _i64, _i32, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "mxgg_query_tile_m": (_i32, []),
     "mxgg_ep_atom_bytes": (_i64, [_i64, _i64, _i64]),
-    "mxgg_pack_a_atoms": (_int, [_vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "mxgg_pack_a_atoms": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "mxgg_peer_signal": (_int, [_vp, _i32, _vp]),
     "mxgg_inbox_unpack": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "mxgg_ipc_alloc": (_int, [_i64, ctypes.POINTER(_vp), ctypes.c_char_p]),
@@ -102,6 +107,8 @@ SIGNATURES = {
     "mxgg_wgrad_accumulate": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
     "mxgg_grouped_mm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),
+    "mxgg_blocked_scale_bytes": (_i64, [_i64, _i64, _i64]),
+    "mxgg_quantize_mx_blocked": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp]),
     "mxgg_quantize_mx_fp4": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _vp]),
     "mxgg_quantize_mx_gather": (_int, [_vp, _int, _i64, _vp, _i64, _i64, _vp, _vp, _vp]),
     "mxgg_combine_topk": (_int, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _vp]),

@@ -223,25 +223,25 @@ class FusedPlan:
     rows_local: int
     rows_recv: int               # all rows this rank multiplies (its own included)
     copies: List[tuple]          # (dest rank, first row there, first local row, rows) to peers, in sending order
-    pack: List[tuple]            # (dest rank, cumulative segment ends (device), first m-tile there,
-                                 #  first local row, rows), this rank included
+    pack: List[tuple]            # (dest rank, cumulative segment ends (device), first 128-row scale slab
+                                 #  there, first local row, rows), this rank included
     self_base: int               # local row of the first row this rank routes to itself
     seg: _Segments               # world * L segments over the receive buffer
     local_seg: _Segments         # the same segments with every row kept here, in receive order
     dst_rows: List[int]          # local rows of every rank (the output buffers' heights)
-    tile_m: int
     inbox_ok: bool               # every segment starts on a 32-row boundary: peers' blocks go by inbox
     remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
 
 
-def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int, tile_m: int) -> dict:
+def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int) -> dict:
     """The fused path's routing arithmetic for `rank`, from every rank's
     per-expert row counts C[s][e] (rows sorted by expert on each rank).
 
     Receiver d's layout: sources in arrival order d, d-1, d-2, ..., each
     source's rows grouped by d's local experts.  Returns plain lists:
       copies   (dest, first row there, first local row, rows), to peers, in sending order d+1, d+2, ...
-      pack     (dest, cumulative segment ends, first m-tile there, first local row, rows), this rank included
+      pack     (dest, cumulative segment ends, first 128-row scale slab there, first local row, rows),
+               this rank included
       seg      offs / expert / src / dst_row / local_row of this rank's receive segments
       self_base, rows_recv, rows_local, dst_rows, need_recv, inbox_ok, remote_blocks
     """
@@ -264,7 +264,7 @@ def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int, tile_m: int
     def seg_rows(s, d):
         return [C[s][e] if pl.dest(s, e) == d else 0 for e in pl.experts_of(d)]
 
-    # where each source's rows and atoms start at each receiver
+    # where each source's rows and scale slabs start at each receiver
     recv_off = [[0] * world for _ in range(world)]
     m0 = [[0] * world for _ in range(world)]
     for d in range(world):
@@ -272,7 +272,7 @@ def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int, tile_m: int
         for s in order(d):
             recv_off[s][d], m0[s][d] = r, m
             r += send[s][d]
-            m += sum((c + tile_m - 1) // tile_m for c in seg_rows(s, d))
+            m += sum((c + 127) // 128 for c in seg_rows(s, d))   # 128-row scale slabs
     copies, pack = [], []
     for j in range(world):
         d = (rank + j) % world
@@ -400,8 +400,7 @@ class FusedExpertParallel:
             raise _lib.MxggError("fused expert parallelism: a device-side wait gave up in the previous call "
                                  "(rank: status word) " + ", ".join(f"{r}: {v:#x}" for r, v in sorted(bad.items())))
         C = [row[:E] for row in gathered]                     # C[s][e]
-        tile_m = int(_lib.load().mxgg_query_tile_m())
-        lay = fused_layout(C, pl, rank, tile_m)
+        lay = fused_layout(C, pl, rank)
         for d in range(world):
             if lay["need_recv"][d] > self._caps[d][0] or lay["dst_rows"][d] > self._caps[d][1]:
                 raise ValueError(f"fused EP buffers of rank {d} too small: {lay['need_recv'][d]} received / "
@@ -414,7 +413,7 @@ class FusedExpertParallel:
                          self_base=lay["self_base"],
                          seg=_Segments(o, x, sr, i32(seg["dst_row"]), sr),
                          local_seg=_Segments(o, x, i32([rank] * len(seg["offs"])), i32(seg["local_row"]), sr),
-                         dst_rows=lay["dst_rows"], tile_m=tile_m, inbox_ok=lay["inbox_ok"],
+                         dst_rows=lay["dst_rows"], inbox_ok=lay["inbox_ok"],
                          remote_blocks=i32(lay["remote_blocks"] if lay["inbox_ok"] else []))
 
     def check_status(self) -> None:
@@ -459,12 +458,11 @@ class FusedExpertParallel:
         self.src_epoch += 1
         cur = torch.cuda.current_stream()
         sp = ctypes.c_void_p(cur.cuda_stream)
-        stages = (K + 127) // 128
-        atom_bytes_per_mtile = (plan.tile_m // 128) * stages * 512
+        atom_bytes_per_slab = (K + 127) // 128 * 512
         for (d, cum, m0, src_row, rows) in plan.pack:
             _lib.check(lib.mxgg_pack_a_atoms(ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)),
-                                             ctypes.c_void_p(cum.data_ptr()), rows, K, cum.numel(), plan.tile_m,
-                                             ctypes.c_void_p(self.atoms.ptrs[d] + m0 * atom_bytes_per_mtile), sp),
+                                             ctypes.c_void_p(cum.data_ptr()), rows, K, cum.numel(),
+                                             ctypes.c_void_p(self.atoms.ptrs[d] + m0 * atom_bytes_per_slab), sp),
                        "mxgg_pack_a_atoms")
         side = self._side
         side.wait_stream(cur)

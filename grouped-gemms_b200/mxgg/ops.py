@@ -120,6 +120,46 @@ def _(x, mode, scale_layout):
     return s, q
 
 
+def _to_mx_blocked_impl(x: Tensor, offs: Optional[Tensor], n_segments: int) -> Tuple[Tensor, Tensor]:
+    """to_mx along the last dim of a 2-D x, with the scales in the segmented
+    blocked layout the grouped GEMM reads when called with SCALE_BLOCKED:
+    segments are the groups (offs, cumulative row ends) or, with offs None,
+    n_segments equal row blocks (the experts of a flattened (E * N, K)
+    weight).  Returns (scales, a flat zero-padded uint8 tensor, q (R, C))."""
+    _require_cuda(x, what="mxgg::to_mx_blocked")
+    if x.dtype not in _IN_DTYPES:
+        raise TypeError(f"mxgg::to_mx_blocked: unsupported input dtype {x.dtype}")
+    x = x.contiguous()
+    R, C = x.shape
+    lib = _lib.load()
+    S = offs.shape[0] if offs is not None else int(n_segments)
+    if offs is None and (S < 1 or R % S != 0):
+        raise ValueError(f"mxgg::to_mx_blocked: {R} rows do not split into {S} equal segments")
+    with torch.cuda.device(x.device):
+        q = torch.empty((R, C), dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.zeros(max(int(lib.mxgg_blocked_scale_bytes(R, C, S)), 0), dtype=torch.uint8, device=x.device)
+        if offs is not None:
+            _require_cuda(offs, what="mxgg::to_mx_blocked")
+            offs = offs.to(torch.int32).contiguous()
+        _lib.check(lib.mxgg_quantize_mx_blocked(_ptr(x), _IN_DTYPES[x.dtype], R, C, _ptr(q), _ptr(s),
+                                                _ptr(offs) if offs is not None else None, S,
+                                                0 if offs is not None else R // S, _stream(x.device)),
+                   "mxgg_quantize_mx_blocked")
+    return s, q
+
+
+to_mx_blocked_op = torch.library.custom_op("mxgg::to_mx_blocked", _to_mx_blocked_impl, mutates_args=())
+to_mx_blocked = _fast(to_mx_blocked_op, _to_mx_blocked_impl)
+
+
+@to_mx_blocked_op.register_fake
+def _(x, offs, n_segments):
+    R, C = x.shape
+    S = offs.shape[0] if offs is not None else int(n_segments)
+    nbytes = ((R + 127) // 128 + S - 1) * ((C + 127) // 128) * 512
+    return x.new_empty((nbytes,), dtype=torch.uint8), x.new_empty((R, C), dtype=torch.float8_e4m3fn)
+
+
 def _to_mx_fp4_impl(x: Tensor, scale_layout: int) -> Tuple[Tensor, Tensor]:
     """MXFP4 along the last dim: (scales (R, C/32) u8, q (R, C/2) float4_e2m1fn_x2)."""
     _require_cuda(x, what="mxgg::to_mx_fp4")
@@ -155,9 +195,12 @@ def _(x, scale_layout):
 
 # ---------------------------------------------------------------- grouped_mm
 def _grouped_mm_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, offs: Tensor,
-                  out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
+                  out_dtype: torch.dtype, cfg: Optional[List[int]] = None, scale_layout: int = 0) -> Tensor:
     """cfg: this call's (tile_m, tile_n, group_m, schedule, split_max), zeros
-    for the process defaults (mxgg_gemm_config); None: all defaults."""
+    for the process defaults (mxgg_gemm_config); None: all defaults.
+    scale_layout: SCALE_ROW_MAJOR (the reference's (rows, K/32) scales) or
+    SCALE_BLOCKED (the blocked layout to_mx_blocked writes: A per group, B
+    per expert; no re-layout launch)."""
     _require_cuda(a, b, a_scale, b_scale, offs, what="mxgg::grouped_mm")
     if out_dtype not in _OUT_DTYPES:
         raise TypeError(f"mxgg::grouped_mm: unsupported out_dtype {out_dtype}")
@@ -173,7 +216,7 @@ def _grouped_mm_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, off
     ws = _workspace(lib.mxgg_grouped_mm_workspace_size(M, N, K, E), a.device)
     with torch.cuda.device(a.device):
         _lib.check(lib.mxgg_grouped_mm_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(offs),
-                                           M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                           M, N, K, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg, scale_layout),
                                            _ptr(ws), ws.numel(), _stream(a.device)), "mxgg_grouped_mm")
     return out
 
@@ -183,13 +226,14 @@ grouped_mm = _fast(grouped_mm_op, _grouped_mm_impl)
 
 
 @grouped_mm_op.register_fake
-def _(a, b, a_scale, b_scale, offs, out_dtype, cfg=None):
+def _(a, b, a_scale, b_scale, offs, out_dtype, cfg=None, scale_layout=0):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
 # ------------------------------------------------------- grouped_mm_segments
 def _grouped_mm_segments_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
-                           seg_expert: Tensor, out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
+                           seg_expert: Tensor, out_dtype: torch.dtype, cfg: Optional[List[int]] = None,
+                           scale_layout: int = 0) -> Tensor:
     """Rows of segment s times B[seg_expert[s]]: the layout an expert-parallel
     all-to-all delivers (source-major, then expert)."""
     _require_cuda(a, b, a_scale, b_scale, seg_offs, seg_expert, what="mxgg::grouped_mm_segments")
@@ -211,7 +255,7 @@ def _grouped_mm_segments_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Te
     with torch.cuda.device(a.device):
         _lib.check(lib.mxgg_grouped_mm_segments_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale),
                                                     _ptr(seg_offs), _ptr(seg_expert), M, N, K, S, E, b_format,
-                                                    _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                                    _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg, scale_layout),
                                                     _ptr(ws), ws.numel(), _stream(a.device)),
                    "mxgg_grouped_mm_segments")
     return out
@@ -223,14 +267,14 @@ grouped_mm_segments = _fast(grouped_mm_segments_op, _grouped_mm_segments_impl)
 
 
 @grouped_mm_segments_op.register_fake
-def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, cfg=None):
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, cfg=None, scale_layout=0):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
 
 
 def _grouped_mm_mx_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, seg_offs: Tensor,
                      seg_expert: Optional[Tensor], out_dtype: torch.dtype, keep_out: bool, rows: bool = True,
-                     cols: bool = False, cfg: Optional[List[int]] = None) -> Tuple[Tensor, Tensor, Tensor, Tensor,
-                                                                                  Tensor]:
+                     cols: bool = False, cfg: Optional[List[int]] = None,
+                     scale_layout: int = 0) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The forward (segments as in grouped_mm_segments_op; seg_expert None:
     segment s uses expert s) with MX quantisation of its output fused into
     the epilogue.  Returns (scales, data, scales_t, data_t, out):
@@ -275,7 +319,7 @@ def _grouped_mm_mx_impl(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, 
         _lib.check(lib.mxgg_grouped_mm_mx_cfg(_ptr(a), _ptr(b), _ptr(a_scale), _ptr(b_scale), _ptr(seg_offs),
                                               _ptr(seg_expert) if seg_expert is not None else None, M, N, K, S, E,
                                               b_format, opt(out, keep_out), _OUT_DTYPES[out_dtype], opt(q, rows),
-                                              opt(s, rows), opt(qt, cols), opt(st, cols), _lib.gemm_config(cfg),
+                                              opt(s, rows), opt(qt, cols), opt(st, cols), _lib.gemm_config(cfg, scale_layout),
                                               _ptr(ws), ws.numel(), _stream(dev)),
                    "mxgg_grouped_mm_mx")
     return s, q, st, qt, out
@@ -286,7 +330,8 @@ grouped_mm_mx = _fast(grouped_mm_mx_op, _grouped_mm_mx_impl)
 
 
 @grouped_mm_mx_op.register_fake
-def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False, cfg=None):
+def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=True, cols=False, cfg=None,
+      scale_layout=0):
     M, N = a.shape[0], b.shape[1]
     e = lambda shape, on, dt: a.new_empty(shape if on else (0,), dtype=dt)  # noqa: E731
     return (e((M, N // 32), rows, torch.uint8), e((M, N), rows, torch.float8_e4m3fn),
@@ -296,7 +341,9 @@ def _(a, b, a_scale, b_scale, seg_offs, seg_expert, out_dtype, keep_out, rows=Tr
 
 # --------------------------------------------------------------------- wgrad
 def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
-             out_dtype: torch.dtype, cfg: Optional[List[int]] = None) -> Tensor:
+             out_dtype: torch.dtype, cfg: Optional[List[int]] = None, scale_layout: int = 0) -> Tensor:
+    """scale_layout SCALE_BLOCKED: go_scale / ia_scale in the one-segment
+    blocked layout (to_mx_dim1 with blocked scales)."""
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, what="mxgg::wgrad")
     if out_dtype not in _OUT_DTYPES:
         raise TypeError(f"mxgg::wgrad: unsupported out_dtype {out_dtype}")
@@ -313,7 +360,7 @@ def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, 
     ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
         _lib.check(lib.mxgg_wgrad_cfg(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
-                                      N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg),
+                                      N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg, scale_layout),
                                       _ptr(ws), ws.numel(), _stream(go_t.device)), "mxgg_wgrad")
     return out
 
@@ -323,12 +370,12 @@ wgrad = _fast(wgrad_op, _wgrad_impl)
 
 
 @wgrad_op.register_fake
-def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype, cfg=None):
+def _(go_t, go_scale, ia_t, ia_scale, offs, out_dtype, cfg=None, scale_layout=0):
     return go_t.new_empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype)
 
 
 def _wgrad_accumulate_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor,
-                        out: Tensor, cfg: Optional[List[int]] = None) -> None:
+                        out: Tensor, cfg: Optional[List[int]] = None, scale_layout: int = 0) -> None:
     """out[g] += the group's weight gradient, in place (fp32 out)."""
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, out, what="mxgg::wgrad_accumulate_")
     N, M = go_t.shape
@@ -345,7 +392,7 @@ def _wgrad_accumulate_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scal
     ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
         _lib.check(lib.mxgg_wgrad_accumulate_cfg(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale),
-                                                 _ptr(offs), N, K, M, E, _ptr(out), _lib.gemm_config(cfg),
+                                                 _ptr(offs), N, K, M, E, _ptr(out), _lib.gemm_config(cfg, scale_layout),
                                                  _ptr(ws), ws.numel(), _stream(go_t.device)),
                    "mxgg_wgrad_accumulate")
 
@@ -356,7 +403,7 @@ wgrad_accumulate = _fast(wgrad_accumulate_op, _wgrad_accumulate_impl)
 
 
 @wgrad_accumulate_op.register_fake
-def _(go_t, go_scale, ia_t, ia_scale, offs, out, cfg=None):
+def _(go_t, go_scale, ia_t, ia_scale, offs, out, cfg=None, scale_layout=0):
     return None
 
 

@@ -69,6 +69,33 @@ def to_mx_blocked_scales(data: torch.Tensor):
     return mxgg.ops.to_mx(data, _lib.QUANT_ROWS, _lib.SCALE_BLOCKED)
 
 
+def to_mx_grouped_blocked(data: torch.Tensor, group_end_offsets: torch.Tensor = None):
+    """``to_mx`` with the scales written once, in the blocked layout the
+    grouped GEMMs read with ``scale_layout="blocked"``: a 2-D ``data`` (M, K)
+    with ``group_end_offsets`` is an activation (each group's scale rows start
+    a new 128-row slab), a 3-D ``data`` (E, N, K) a weight (each expert's).
+    Returns ``(scales, data_fp8)``: the scales as one flat uint8 tensor
+    (zero padding), the data in ``data``'s shape.  No reference counterpart.
+    """
+    if data.dim() == 3:
+        E, N, K = data.shape
+        s, q = mxgg.ops.to_mx_blocked(data.reshape(E * N, K), None, E)
+        return s, q.reshape(E, N, K)
+    assert data.dim() == 2 and group_end_offsets is not None, \
+        "a 2-D activation needs its group_end_offsets"
+    return mxgg.ops.to_mx_blocked(data, group_end_offsets, 0)
+
+
+def to_mx_dim1_blocked(data: torch.Tensor):
+    """``to_mx_dim1`` with the scales in the one-segment blocked layout
+    (the weight-gradient operands' layout for ``scale_layout="blocked"``).
+    Returns ``(scales flat uint8, data_fp8 (C, R))``.
+    """
+    assert data.dim() == 2, "to_mx_dim1_blocked takes a 2-D tensor"
+    _check_to_mx_args(data.t(), torch.float8_e4m3fn, 32)
+    return mxgg.ops.to_mx(data, _lib.QUANT_COLS, _lib.SCALE_BLOCKED)
+
+
 def generate_jagged_offs(E: int, M: int, multiple_of: int = 32, dtype=torch.int32, device="cuda") -> torch.Tensor:
     """Random sorted cumulative offsets summing to M, each a multiple of
     ``multiple_of``; the last value is M.  Same draw as utils.py:35-50

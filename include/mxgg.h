@@ -44,6 +44,19 @@ extern "C" {
 /* scale layouts */
 #define MXGG_SCALE_ROW_MAJOR 0 /* (rows, cols/32), the reference layout */
 #define MXGG_SCALE_BLOCKED 1   /* 128x4 atoms (rows padded to 128, cols/32 to 4) */
+/*
+ * The blocked scale layout the grouped GEMMs read (torch's layout for its
+ * grouped MXFP8 GEMMs).  A scale matrix of R rows and C/32 columns (C the
+ * contraction) is stored as 512-byte atoms [slab][ceil(C/128)][512 B], one
+ * slab per 128 rows, byte (r % 32) * 16 + ((r % 128) / 32) * 4 + k % 4 of
+ * atom (slab, k / 4) holding row r, k-block k of the slab.  Rows are cut into
+ * segments and every segment starts a new slab:
+ *   forward / dgrad A   segments = the groups (group_end_offsets)
+ *   forward / dgrad B   segments = the experts (N rows each)
+ *   wgrad A and B       one segment (the whole operand: MXGG_SCALE_BLOCKED)
+ * mxgg_quantize_mx_blocked writes the segmented form, mxgg_quantize_mx with
+ * MXGG_SCALE_BLOCKED the one-segment form.  Padding (rows past a segment's
+ * end in its last slab, k-blocks past C/32) feeds no stored output. */
 
 /* element formats of a GEMM operand */
 #define MXGG_FMT_E4M3 0 /* MXFP8: one e4m3 byte per element */
@@ -61,6 +74,17 @@ extern "C" {
  *   group_m    rasterisation band, in row tiles (>= 1)
  *   schedule   MXGG_SCHED_TILES or MXGG_SCHED_SPLIT_TAIL (see mxgg_set_schedule)
  *   split_max  most pieces per split tile (2..64)
+ *   scale_layout  MXGG_SCALE_ROW_MAJOR (0): a_scale / b_scale are the
+ *              reference's row-major e8m0 matrices, re-laid into the
+ *              workspace by a pack launch before the GEMM.
+ *              MXGG_SCALE_BLOCKED: they are already in the blocked layout
+ *              (see MXGG_SCALE_BLOCKED; 16-byte aligned, A at least the sum
+ *              over groups of ceil(rows_g / 128) slabs -- at most
+ *              mxgg_blocked_scale_bytes(M, K, E) bytes -- B n_experts *
+ *              ceil(N / 128) slabs); the GEMM reads them in place and
+ *              launches nothing else.  Results are bit-identical.
+ *              Forward, dgrad and wgrad entry points; not the expert-parallel
+ *              one.
  *   reserved   must be zero
  */
 typedef struct mxgg_gemm_config {
@@ -69,7 +93,8 @@ typedef struct mxgg_gemm_config {
   int32_t group_m;
   int32_t schedule;
   int32_t split_max;
-  int32_t reserved[3];
+  int32_t scale_layout;
+  int32_t reserved[2];
 } mxgg_gemm_config;
 
 /*
@@ -249,11 +274,13 @@ int32_t mxgg_query_tile_m(void);
 int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments);
 /* Packs the scales of `rows` rows (a_scale (rows, K/32) row-major) grouped
  * in n_segments segments (device cumulative ends, relative to the first row)
- * into atoms numbered from 0, for GEMM tiles of tile_m rows, at `out`
- * (typically inside a peer's atom buffer, at the m-tile where this sender's
- * segments start in the receiver's order). */
+ * into the blocked layout of forward A scales -- 128-row slabs, a new slab at
+ * every segment start, [slab][ceil(K/128)][512 B] -- numbered from 0, at
+ * `out` (typically inside a peer's atom buffer, at the slab where this
+ * sender's segments start in the receiver's order: the sum of
+ * ceil(rows / 128) over the receiver's earlier segments). */
 int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
-                      int64_t n_segments, int32_t tile_m, void* out, void* stream);
+                      int64_t n_segments, void* out, void* stream);
 /* Writes `epoch` into `slot` (usually a peer's flag array) once everything
  * earlier on `stream` is done, as a stream memory operation
  * (cuStreamWriteValue32, with its memory barrier): no kernel, so no SM is
@@ -359,6 +386,20 @@ int mxgg_quantize_mx_fp4(const void* x, int x_dtype, int64_t rows, int64_t cols,
 
 int mxgg_quantize_mx(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
                      int mode, int scale_layout, void* stream);
+
+/* The rows mode of mxgg_quantize_mx with the scales written in the segmented
+ * blocked layout (see MXGG_SCALE_BLOCKED), ready for a grouped GEMM called
+ * with scale_layout MXGG_SCALE_BLOCKED: the segments are the groups
+ * (segment_end_offsets, device int32 cumulative ends, n_segments <= 256) or,
+ * with segment_end_offsets null, n_segments uniform segments of segment_rows
+ * rows (a weight tensor's experts).  scales holds at least
+ * mxgg_blocked_scale_bytes(rows, cols, n_segments) bytes; entries no row
+ * fills are left as they are (zero-fill them for a bit-for-bit comparison
+ * with torch's to_blocked).  No counterpart in the reference. */
+int64_t mxgg_blocked_scale_bytes(int64_t rows, int64_t contraction, int64_t n_segments);
+int mxgg_quantize_mx_blocked(const void* x, int x_dtype, int64_t rows, int64_t cols, void* q, void* scales,
+                             const int32_t* segment_end_offsets, int64_t n_segments, int64_t segment_rows,
+                             void* stream);
 
 /*
  * Routing tables of the reference's _build_expt_data (forward.py:340-365),

@@ -78,3 +78,29 @@ def run_ranks(worker, world, *args, timeout=300):
                 p.kill()
         shutil.rmtree(d, ignore_errors=True)
     return results
+
+
+def blocked_scales_ref(s: np.ndarray, segments) -> np.ndarray:
+    """CPU restatement of the blocked scale layout: the (R, C32) row-major
+    e8m0 matrix `s` cut into row segments [(start, end), ...]; each segment's
+    rows fill 128-row slabs of their own, slab j of a segment holding its rows
+    128 j .. 128 j + 127; a slab is ceil(C32 / 4) atoms of 512 bytes, atom k4
+    holding k-blocks 4 k4 .. 4 k4 + 3 of the slab's rows, row r, k-block k at
+    byte (r % 32) * 16 + (r // 32) * 4 + k % 4.  Padding bytes are zero (as
+    torch's to_blocked pads)."""
+    R, C32 = s.shape
+    cb = (C32 + 3) // 4
+    slabs = sum((e - b + 127) // 128 for b, e in segments)
+    out = np.zeros(slabs * cb * 512, dtype=np.uint8)
+    slab0 = 0
+    cols = np.arange(C32)
+    for b, e in segments:
+        rr = np.arange(e - b)
+        if rr.size:
+            slab = slab0 + rr // 128
+            r128 = rr % 128
+            idx = ((slab[:, None] * cb + cols[None, :] // 4) * 512 + (r128[:, None] % 32) * 16
+                   + (r128[:, None] // 32) * 4 + cols[None, :] % 4)
+            out[idx] = s[b:e]
+        slab0 += (e - b + 127) // 128
+    return out

@@ -26,10 +26,9 @@ def _cases():
 
 
 @pytest.mark.parametrize("world,E,align,C", _cases())
-@pytest.mark.parametrize("tile_m", [256, 128])
-def test_fused_layout_moves_every_row(world, E, align, C, tile_m):
+def test_fused_layout_moves_every_row(world, E, align, C):
     pl = ExpertPlacement(world, E)
-    lays = [fused_layout(C, pl, r, tile_m) for r in range(world)]
+    lays = [fused_layout(C, pl, r) for r in range(world)]
     # each rank's local rows, tagged (owner, local row, expert)
     local = []
     for s in range(world):
@@ -48,12 +47,12 @@ def test_fused_layout_moves_every_row(world, E, align, C, tile_m):
         seg = lay["seg"]
         assert lay["rows_recv"] == lay["need_recv"][d]
         lo = 0
-        g_cum = 0
-        first_tile = {}
+        g_cum = 0          # 128-row scale slabs of the segments so far
+        first_slab = {}
         for i, hi in enumerate(seg["offs"]):
             src, le = seg["src"][i], seg["expert"][i]
             e = pl.experts_of(d)[le]
-            first_tile.setdefault(src, g_cum)
+            first_slab.setdefault(src, g_cum)
             for k, r in enumerate(range(lo, hi)):
                 row = local[d][lay["self_base"] + r] if src == d else recv[d][r]
                 assert row is not None, "a received row was never copied"
@@ -62,7 +61,7 @@ def test_fused_layout_moves_every_row(world, E, align, C, tile_m):
                 # the output row goes back to its owner's exact position
                 assert seg["dst_row"][i] + k == lrow
                 assert seg["local_row"][i] == lo
-            g_cum += (hi - lo + tile_m - 1) // tile_m
+            g_cum += (hi - lo + 127) // 128
             lo = hi
         # every row routed to d arrived exactly once
         want = sorted(r for s in range(world) for r in local[s] if pl.dest(s, r[2]) == d)
@@ -70,11 +69,11 @@ def test_fused_layout_moves_every_row(world, E, align, C, tile_m):
                      for i, hi in enumerate(seg["offs"])
                      for r in range(seg["offs"][i - 1] if i else 0, hi))
         assert got == want
-        # senders pack their scale atoms where d's tile numbering puts their first segment
+        # senders pack their scale atoms where d's slab numbering puts their first segment
         for s in range(world):
             for (dd, cum, m0, src_row, rows) in lays[s]["pack"]:
                 if dd == d:
-                    assert m0 == first_tile[s]
+                    assert m0 == first_slab[s]
                     assert cum[-1] == rows
     # inbox blocks: exactly the 32-row blocks of rows computed by other ranks
     for r in range(world):

@@ -40,8 +40,9 @@ def test_wrappers_pass_the_installed_entry(monkeypatch):
     seen = {}
     monkeypatch.setattr(forward, "_mxfp8_available", True)
     monkeypatch.setattr(backward, "_mxfp8_available", True)
-    monkeypatch.setattr(mxgg.ops, "grouped_mm", lambda *a: seen.setdefault("fwd", a[-1]))
-    monkeypatch.setattr(mxgg.ops, "wgrad", lambda *a: seen.setdefault("wgrad", a[-1]))
+    # the wrappers pass (..., cfg, scale_layout)
+    monkeypatch.setattr(mxgg.ops, "grouped_mm", lambda *a: seen.setdefault("fwd", a[-2:]))
+    monkeypatch.setattr(mxgg.ops, "wgrad", lambda *a: seen.setdefault("wgrad", a[-2:]))
     t = tune.Table()
     t.add("fwd", 2, 256, 512, tune.Config(128, 128, 2, _lib.SCHED_TILES, 0), 1.0)
     t.add("wgrad", 2, 256, 512, tune.Config(256, 256, 8, _lib.SCHED_SPLIT_TAIL, 3), 1.0)
@@ -57,7 +58,33 @@ def test_wrappers_pass_the_installed_entry(monkeypatch):
                                    offs)
     finally:
         tune.install(None)
-    assert seen == {"fwd": [128, 128, 2, _lib.SCHED_TILES, 0], "wgrad": [256, 256, 8, _lib.SCHED_SPLIT_TAIL, 3]}
+    assert seen == {"fwd": ([128, 128, 2, _lib.SCHED_TILES, 0], _lib.SCALE_ROW_MAJOR),
+                    "wgrad": ([256, 256, 8, _lib.SCHED_SPLIT_TAIL, 3], _lib.SCALE_ROW_MAJOR)}
+
+
+def test_wrappers_pass_the_scale_layout(monkeypatch):
+    import torch
+
+    import kernels
+    import mxgg
+    from kernels import backward, forward
+    seen = {}
+    monkeypatch.setattr(forward, "_mxfp8_available", True)
+    monkeypatch.setattr(backward, "_mxfp8_available", True)
+    monkeypatch.setattr(mxgg.ops, "grouped_mm", lambda *a: seen.setdefault("fwd", a[-1]))
+    monkeypatch.setattr(mxgg.ops, "wgrad", lambda *a: seen.setdefault("wgrad", a[-1]))
+    a = torch.zeros(64, 512, dtype=torch.float8_e4m3fn)
+    b = torch.zeros(2, 256, 512, dtype=torch.float8_e4m3fn)
+    offs = torch.tensor([32, 64], dtype=torch.int32)
+    kernels.triton_mxfp8_grouped_mm(a, b, torch.zeros(1, dtype=torch.uint8), torch.zeros(1, dtype=torch.uint8), offs,
+                                    scale_layout="blocked")
+    kernels.triton_mxfp8_wgrad(torch.zeros(256, 64, dtype=torch.float8_e4m3fn), torch.zeros(1, dtype=torch.uint8),
+                               torch.zeros(512, 64, dtype=torch.float8_e4m3fn), torch.zeros(1, dtype=torch.uint8),
+                               offs, scale_layout="blocked")
+    assert seen == {"fwd": _lib.SCALE_BLOCKED, "wgrad": _lib.SCALE_BLOCKED}
+    with pytest.raises(ValueError, match="scale_layout"):
+        kernels.triton_mxfp8_grouped_mm(a, b, torch.zeros(1, dtype=torch.uint8), torch.zeros(1, dtype=torch.uint8),
+                                        offs, scale_layout="swizzled")
 
 
 def test_library_rejects_a_bad_call_config():
@@ -68,6 +95,9 @@ def test_library_rejects_a_bad_call_config():
         rc = lib.mxgg_grouped_mm_cfg(None, None, None, None, None, 128, 128, 128, 1, None, _lib.DTYPE_BF16,
                                      _lib.gemm_config(bad), None, 0, None)
         assert rc == 1 and word in lib.mxgg_last_error().decode()
+    rc = lib.mxgg_grouped_mm_cfg(None, None, None, None, None, 128, 128, 128, 1, None, _lib.DTYPE_BF16,
+                                 _lib.gemm_config(None, 7), None, 0, None)
+    assert rc == 1 and "scale_layout" in lib.mxgg_last_error().decode()
     cfg = _lib.GemmConfig(0, 0, 0, 0, 0)
     cfg.reserved[1] = 5
     rc = lib.mxgg_wgrad_cfg(None, None, None, None, None, 128, 128, 128, 1, None, _lib.DTYPE_BF16,
