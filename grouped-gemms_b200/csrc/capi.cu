@@ -158,13 +158,13 @@ struct Maps {
   OutMaps out;
 };
 
-template <int BN, int STAGES, int ACC, int PAIR, typename OutT>
+template <int BN, int STAGES, int ACC, int PAIR, typename OutT, bool kFull>
 int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units,
                   cudaStream_t stream) {
   using S = SmemLayout<BN, STAGES, PAIR, OutT>;
   constexpr size_t kSmem = sizeof(S) + 1024;
   static_assert(kSmem <= 232448, "shared memory budget");
-  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, PAIR, OutT>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, PAIR, OutT, kFull>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   MXGG_CUDA_TRY(cudaGetDevice(&dev));
@@ -196,14 +196,23 @@ int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, lon
   return MXGG_OK;
 }
 
-template <int BN, int STAGES, int ACC, int PAIR>
-int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
+template <int BN, int STAGES, int ACC, int PAIR, bool kFull>
+int launch_gemm_out(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
                     cudaStream_t stream) {
   switch (out_dtype) {
-    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, PAIR, __half>(st, m, p, max_units, stream);
-    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, PAIR, float>(st, m, p, max_units, stream);
-    default: return launch_gemm_t<BN, STAGES, ACC, PAIR, __nv_bfloat16>(st, m, p, max_units, stream);
+    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, PAIR, __half, kFull>(st, m, p, max_units, stream);
+    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, PAIR, float, kFull>(st, m, p, max_units, stream);
+    default: return launch_gemm_t<BN, STAGES, ACC, PAIR, __nv_bfloat16, kFull>(st, m, p, max_units, stream);
   }
+}
+
+// full: the call needs the expert-parallel, quantised-output or accumulating
+// paths; every other call runs the plain kernel (see grouped_gemm_kernel)
+template <int BN, int STAGES, int ACC, int PAIR>
+int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
+                    bool full, cudaStream_t stream) {
+  return full ? launch_gemm_out<BN, STAGES, ACC, PAIR, true>(st, m, p, max_units, out_dtype, stream)
+              : launch_gemm_out<BN, STAGES, ACC, PAIR, false>(st, m, p, max_units, out_dtype, stream);
 }
 
 // Workspace of one GEMM call: [A atoms | B atoms | split-tail partials |
@@ -618,6 +627,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
       return rc;
   }
 
+  const bool full = route != nullptr || quant != nullptr || accumulate;
   long long max_units;
   const int tile_m = tc.tile_m;
   if (mode == kFwd) {
@@ -627,11 +637,11 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
     max_units = E * ((N + tile_m - 1) / tile_m) * ((K + bn - 1) / bn);
   }
   if (pair == 2) {
-    if (bn == 256) return launch_gemm_cfg<256, 6, 2, 2>(*st, maps, p, max_units, out_dtype, stream);
-    return launch_gemm_cfg<128, 8, 2, 2>(*st, maps, p, max_units, out_dtype, stream);
+    if (bn == 256) return launch_gemm_cfg<256, 6, 2, 2>(*st, maps, p, max_units, out_dtype, full, stream);
+    return launch_gemm_cfg<128, 8, 2, 2>(*st, maps, p, max_units, out_dtype, full, stream);
   }
-  if (bn == 256) return launch_gemm_cfg<256, 4, 2, 1>(*st, maps, p, max_units, out_dtype, stream);
-  return launch_gemm_cfg<128, 6, 2, 1>(*st, maps, p, max_units, out_dtype, stream);
+  if (bn == 256) return launch_gemm_cfg<256, 4, 2, 1>(*st, maps, p, max_units, out_dtype, full, stream);
+  return launch_gemm_cfg<128, 6, 2, 1>(*st, maps, p, max_units, out_dtype, full, stream);
 }
 
 // Scratch of mxgg_grouped_mm_noalloc: a fixed array in device memory that
