@@ -927,6 +927,10 @@ def main():
     import utils
     dev = torch.device("cuda", torch.cuda.current_device())
     mxgg.device_status(clear=True)
+    if args.tile_m or args.tile_n or args.schedule != "default" or args.split_max:
+        # an explicit configuration on the command line wins over the packaged tuned table
+        from mxgg import tune as _tune
+        _tune.install(None)
     mxgg.set_tile_config(args.tile_m, args.tile_n, 0)
     mxgg.set_schedule({"default": mxgg._lib.SCHED_DEFAULT, "tiles": mxgg._lib.SCHED_TILES,
                        "split_tail": mxgg._lib.SCHED_SPLIT_TAIL}[args.schedule], args.split_max)

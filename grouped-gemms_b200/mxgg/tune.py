@@ -25,8 +25,13 @@ weight (E, N, K) -- dgrad included, as the forward call with N and K swapped
 -- and ("wgrad", E, N, K) for ``triton_mxfp8_wgrad`` with output (E, N, K).
 ``install(table)`` makes those entry points look up their call and pass the
 entry's config with the call itself (``mxgg_gemm_config``): no process-wide
-setting changes, so threads issuing differently tuned GEMMs do not race.  The environment variable ``MXGG_TUNE_TABLE``
-names a table to install at import.  Without an entry, the library's own
+setting changes, so threads issuing differently tuned GEMMs do not race.
+
+At import the package installs its own table, ``tables/b200_llama4.json``:
+the 36 Llama4 sweep shapes x {fwd, wgrad} (dgrad shapes are among the
+forward ones), tuned on a B200 at M = 16640.  The environment variable
+``MXGG_TUNE_TABLE`` names another table to install instead, or, set to
+``none``, installs none.  Without an entry for a call, the library's own
 heuristic applies.
 
     python -m mxgg.tune --shapes 0,4,8 --passes fwd,wgrad --gpus 8 --out table.json
@@ -166,8 +171,22 @@ def pick(pass_: str, E: int, N: int, K: int) -> Optional[Config]:
     return _installed.lookup(pass_, E, N, K) if _installed is not None else None
 
 
-if os.environ.get("MXGG_TUNE_TABLE"):
-    install(os.environ["MXGG_TUNE_TABLE"])
+DEFAULT_TABLE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tables", "b200_llama4.json")
+
+
+def install_default() -> None:
+    """The import-time choice: ``MXGG_TUNE_TABLE`` (a path, or ``none``), else
+    the packaged B200 table."""
+    env = os.environ.get("MXGG_TUNE_TABLE")
+    if env is None:
+        install(DEFAULT_TABLE if os.path.exists(DEFAULT_TABLE) else None)
+    elif env.strip().lower() in ("", "none", "off", "0"):
+        install(None)
+    else:
+        install(env)
+
+
+install_default()
 
 
 # ------------------------------------------------------------------ timing

@@ -173,6 +173,27 @@ def test_table_round_trip_merge_and_lookup():
                                            "config": {"tile_m": 96}}]})
 
 
+def test_packaged_default_table(monkeypatch):
+    # the packaged table covers every sweep shape x {fwd, wgrad} with valid configs
+    t = tune.Table.load(tune.DEFAULT_TABLE)
+    shapes = tune.llama4_shapes()
+    for (E, M, N, K) in shapes:
+        for ps in ("fwd", "wgrad"):
+            cfg = t.lookup(ps, E, N, K)
+            assert cfg is not None and cfg.valid(), (ps, E, N, K)
+    # installed at import unless MXGG_TUNE_TABLE says otherwise
+    monkeypatch.delenv("MXGG_TUNE_TABLE", raising=False)
+    try:
+        tune.install_default()
+        assert tune.pick("fwd", *shapes[0][:1], *shapes[0][2:]) == t.lookup("fwd", shapes[0][0], shapes[0][2],
+                                                                            shapes[0][3])
+        monkeypatch.setenv("MXGG_TUNE_TABLE", "none")
+        tune.install_default()
+        assert tune.pick("fwd", shapes[0][0], shapes[0][2], shapes[0][3]) is None
+    finally:
+        tune.install(None)
+
+
 def test_install_and_pick():
     t = tune.Table()
     t.add("fwd", 2, 256, 512, tune.Config(128, 128, 2), 1.0)
