@@ -872,8 +872,8 @@ def main():
     ap.add_argument("--tile-m", type=int, default=0, help="GEMM tile rows: 128 (one CTA) or 256 (CTA pair); 0 = auto")
     ap.add_argument("--tile-n", type=int, default=0, help="GEMM tile columns: 128 or 256; 0 = auto")
     ap.add_argument("--schedule", default="default", choices=["default", "tiles", "split_tail"],
-                    help="GEMM work schedule: split the last partial round's tiles (split_tail, the default) "
-                         "or deal whole tiles")
+                    help="GEMM work schedule: deal whole tiles (tiles, the default) or split the last "
+                         "partial round's tiles along the contraction (split_tail)")
     ap.add_argument("--split-max", type=int, default=0, help="most pieces per split tile (0 = automatic)")
     ap.add_argument("--torch-arm", action="store_true",
                     help="also time torch._scaled_grouped_mm (MXFP8) on the same forward shapes (1 GPU)")

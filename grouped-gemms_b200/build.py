@@ -9,8 +9,11 @@ Python package that loads it, so it travels with a copy of the source tree.
 import argparse
 import ctypes
 import os
+import shutil
 import subprocess
 import sys
+import tempfile
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
@@ -22,9 +25,15 @@ ROOT = os.path.dirname(HERE)
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared",
+    "-Xcompiler", "-fPIC",
     "--expt-relaxed-constexpr",
 ]
+
+
+def units():
+    """The translation units: the C ABI and one per GEMM kernel build
+    (compiled in parallel, then linked into one shared library)."""
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith(".cu")]
 
 
 def built_id(path: str) -> str:
@@ -51,12 +60,27 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return OUT
     nvcc = os.environ.get("NVCC", "nvcc")
-    cmd = [nvcc, *NVCC_FLAGS, f'-DMXGG_BUILD_ID="{source_digest()}"', "-o", OUT + ".tmp",
-           os.path.join(CSRC, "capi.cu")]
-    if verbose:
-        print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
-    os.replace(OUT + ".tmp", OUT)
+    tmp = tempfile.mkdtemp(prefix="mxgg_build_")
+    try:
+        def compile_one(src):
+            obj = os.path.join(tmp, os.path.basename(src) + ".o")
+            cmd = [nvcc, *NVCC_FLAGS, f'-DMXGG_BUILD_ID="{source_digest()}"', "-c", "-o", obj, src]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            # each nvcc its own scratch directory: parallel runs must not share temporaries
+            env = dict(os.environ, TMPDIR=tempfile.mkdtemp(dir=tmp))
+            subprocess.run(cmd, check=True, env=env)
+            return obj
+        srcs = units()
+        with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 1)) as ex:
+            objs = list(ex.map(compile_one, srcs))
+        cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT + ".tmp", *objs]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        os.replace(OUT + ".tmp", OUT)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
     return OUT
 
 

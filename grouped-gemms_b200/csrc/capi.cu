@@ -12,6 +12,7 @@
 #include <string>
 
 #include "../../include/mxgg.h"
+#include "gemm_launch.cuh"
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
 #include "scale_pack.cuh"
@@ -147,72 +148,6 @@ CUtensorMapDataType out_tmap_dtype(int out_dtype) {
     case MXGG_DTYPE_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   }
-}
-
-// The grid never holds more CTAs than this (B200: 148 SMs); it bounds the
-// split-tail scratch, which is therefore independent of the problem.
-constexpr int kMaxGridCtas = 160;
-
-struct Maps {
-  CUtensorMap a, a_self, b;
-  OutMaps out;
-};
-
-template <int BN, int STAGES, int ACC, int PAIR, typename OutT, bool kFull>
-int launch_gemm_t(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units,
-                  cudaStream_t stream) {
-  using S = SmemLayout<BN, STAGES, PAIR, OutT>;
-  constexpr size_t kSmem = sizeof(S) + 1024;
-  static_assert(kSmem <= 232448, "shared memory budget");
-  auto kern = grouped_gemm_kernel<BN, STAGES, ACC, PAIR, OutT, kFull>;
-  static bool attr_done[kMaxDevices] = {};
-  int dev = 0;
-  MXGG_CUDA_TRY(cudaGetDevice(&dev));
-  if (!attr_done[dev]) {
-    MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-    if (PAIR > 1) MXGG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
-    attr_done[dev] = true;
-  }
-  const long long units = std::max(1LL, std::min<long long>(std::min(st.num_sms, kMaxGridCtas) / PAIR, max_units));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(units * PAIR), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = PAIR;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  // Programmatic dependent launch: the GEMM may start while the scale-pack
-  // kernel that precedes it still runs (that kernel lets it go at once); its
-  // roles that read what the pack writes wait for it with griddepcontrol.wait.
-  // After any other kernel, which never lets it go early, this changes nothing.
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  MXGG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.a_self, m.b, m.out, p));
-  return MXGG_OK;
-}
-
-template <int BN, int STAGES, int ACC, int PAIR, bool kFull>
-int launch_gemm_out(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
-                    cudaStream_t stream) {
-  switch (out_dtype) {
-    case MXGG_DTYPE_F16: return launch_gemm_t<BN, STAGES, ACC, PAIR, __half, kFull>(st, m, p, max_units, stream);
-    case MXGG_DTYPE_F32: return launch_gemm_t<BN, STAGES, ACC, PAIR, float, kFull>(st, m, p, max_units, stream);
-    default: return launch_gemm_t<BN, STAGES, ACC, PAIR, __nv_bfloat16, kFull>(st, m, p, max_units, stream);
-  }
-}
-
-// full: the call needs the expert-parallel, quantised-output or accumulating
-// paths; every other call runs the plain kernel (see grouped_gemm_kernel)
-template <int BN, int STAGES, int ACC, int PAIR>
-int launch_gemm_cfg(const DeviceState& st, const Maps& m, const GemmParams& p, long long max_units, int out_dtype,
-                    bool full, cudaStream_t stream) {
-  return full ? launch_gemm_out<BN, STAGES, ACC, PAIR, true>(st, m, p, max_units, out_dtype, stream)
-              : launch_gemm_out<BN, STAGES, ACC, PAIR, false>(st, m, p, max_units, out_dtype, stream);
 }
 
 // Workspace of one GEMM call: [A atoms | B atoms | split-tail partials |
@@ -473,7 +408,7 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   // least 2 with a split_max, else at least 24): when none can, the split
   // machinery -- and the zeroing of its counters -- stays off.
   const long long max_stages = mode == kFwd ? ws.stages : ws.stages + 1;   // a group's tokens may straddle one more
-  const bool split_tail = split_ok && cfg.schedule != MXGG_SCHED_TILES &&
+  const bool split_tail = split_ok && cfg.schedule == MXGG_SCHED_SPLIT_TAIL &&
                           (cfg.split_max > 0 ? max_stages >= 2 : max_stages >= 24);
   const bool blocked = cfg.scale_layout == MXGG_SCALE_BLOCKED;
   if (blocked && (route || !aligned(a_scale, 16) || !aligned(b_scale, 16)))
@@ -627,7 +562,6 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
       return rc;
   }
 
-  const bool full = route != nullptr || quant != nullptr || accumulate;
   long long max_units;
   const int tile_m = tc.tile_m;
   if (mode == kFwd) {
@@ -636,12 +570,23 @@ int run_gemm(int mode, const void* a, const void* b, const void* a_scale, const 
   } else {
     max_units = E * ((N + tile_m - 1) / tile_m) * ((K + bn - 1) / bn);
   }
-  if (pair == 2) {
-    if (bn == 256) return launch_gemm_cfg<256, 6, 2, 2>(*st, maps, p, max_units, out_dtype, full, stream);
-    return launch_gemm_cfg<128, 8, 2, 2>(*st, maps, p, max_units, out_dtype, full, stream);
-  }
-  if (bn == 256) return launch_gemm_cfg<256, 4, 2, 1>(*st, maps, p, max_units, out_dtype, full, stream);
-  return launch_gemm_cfg<128, 6, 2, 1>(*st, maps, p, max_units, out_dtype, full, stream);
+  // the kernel build with the optional paths this call uses (the plain
+  // build, whole tiles, for the reference's calls)
+  int feat = 0;
+  if (split_tail) feat |= kFeatSplit;
+  if (route) feat |= kFeatEp;
+  if (quant) feat |= kFeatQuant;
+  if (accumulate) feat |= kFeatAcc;
+  int dev = 0;
+  MXGG_CUDA_TRY(cudaGetDevice(&dev));
+  const GemmLaunch l{dev, st->num_sms, &maps, &p, max_units, out_dtype, bn, pair, stream};
+  cudaError_t e;
+  if (feat == 0) e = launch_gemm_plain(l);
+  else if (feat == kFeatSplit) e = launch_gemm_split(l);
+  else if (feat == kFeatEp) e = launch_gemm_ep(l);
+  else e = launch_gemm_full(l);
+  if (e != cudaSuccess) return fail(MXGG_ERR_CUDA, "%s: GEMM launch: %s", what, cudaGetErrorString(e));
+  return MXGG_OK;
 }
 
 // Scratch of mxgg_grouped_mm_noalloc: a fixed array in device memory that

@@ -69,6 +69,15 @@ constexpr int kTmemCols = 512;
 
 enum : int { kFwd = 0, kWgrad = 1 };
 
+// Optional paths of the GEMM kernel, compiled into a build only when its
+// calls need them (a build's template argument kFeat is a mask of these):
+enum : int {
+  kFeatSplit = 1,   // split-tail schedule: pieces, fp32 partials, their reduction
+  kFeatEp = 2,      // expert parallel: peer outputs and inboxes, streamed sources, rows read in place
+  kFeatQuant = 4,   // MX-quantised outputs (rows and transposed) from the epilogue
+  kFeatAcc = 8,     // accumulate into an fp32 output
+};
+
 // error bits written to GemmParams::status
 enum : uint32_t {
   kErrProducerWait = 1u,
@@ -415,12 +424,12 @@ __device__ __forceinline__ int split_ways(const GemmParams& p, int C, int s, int
 // the L < P tiles of the last, partial round are instead cut along the
 // contraction into pieces, one per otherwise idle pair: pair i takes piece
 // i % s of tail tile i / s (s = P / L).  `k` counts the pair's rounds.
-template <int BN, int TILE_M, class S>
+template <int BN, int TILE_M, bool kSplit, class S>
 __device__ __forceinline__ bool next_unit(const S* sm, const GemmParams& p, int& k, int pair, int P, int num_units,
                                           Unit& u) {
   const int F = num_units / P;
   const int L = num_units - F * P;
-  const int s = (p.split_tail && L > 0) ? P / L : 1;
+  const int s = (kSplit && p.split_tail && L > 0) ? P / L : 1;
   if (s < 2 || k < F) {
     const int t = unit_at(k, pair, P);
     if (t >= num_units) return false;
@@ -519,13 +528,13 @@ __device__ __forceinline__ bool wait_source(const GemmParams& p, int src, volati
   return true;
 }
 
-// kFull: the expert-parallel (peer outputs, streamed sources, in-place
-// rows), quantised-output and accumulating paths are compiled in.  Without
-// them the kernel is the plain single-GPU GEMM: measured on B200, that build
-// of the same source ran the Llama4 sweep points 2-20 % faster (geomean +9 %
-// on eight points x fwd/wgrad, the small-K points most), its hot loops
-// fitting the instruction caches of the four sub-partitions.
-template <int BN, int STAGES, int ACC, int PAIR, typename OutT, bool kFull>
+// kFeat: the optional paths compiled in (kFeat* bits).  With none, the
+// kernel is the plain single-GPU GEMM: measured on B200, that build of the
+// same source ran the Llama4 sweep points 2-20 % faster than the one with
+// every path (geomean +9 % on eight points x fwd/wgrad, the small-K points
+// most), its hot loops fitting the instruction caches of the four
+// sub-partitions; without the split tail, whole tiles ran another 3 % faster.
+template <int BN, int STAGES, int ACC, int PAIR, typename OutT, int kFeat>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_self,
                         const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ OutMaps omaps,
@@ -533,6 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
   static_assert(PAIR == 1 || PAIR == 2, "one CTA or a CTA pair per tile");
   static_assert(ACC == 2, "two accumulator buffers (overlapping when 2*BN does not fit)");
+  constexpr bool kSplit = (kFeat & kFeatSplit) != 0;
+  constexpr bool kEp = (kFeat & kFeatEp) != 0;
+  constexpr bool kQuant = (kFeat & kFeatQuant) != 0;
+  constexpr bool kAcc = (kFeat & kFeatAcc) != 0;
   // a scale writer waits on the empty barrier kSfSlots stages back, which must
   // be a barrier the producer has not re-armed yet
   constexpr int kSfSlots = (STAGES - 1 < kSfSlotsMax) ? STAGES - 1 : kSfSlotsMax;
@@ -652,8 +665,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       Unit u;
       // sources whose rows have arrived (streaming dispatch); rows read in place are always there
       uint32_t ready = (p.self_src >= 0) ? (1u << p.self_src) : 0u;
-      while (ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u)) {
-        if (kFull && p.src_flags && u.st_count > 0 && !((ready >> u.src) & 1u)) {
+      while (ok && next_unit<BN, kTileM, kSplit>(sm, p, k, unit0, unit_stride, num_units, u)) {
+        if (kEp && p.src_flags && u.st_count > 0 && !((ready >> u.src) & 1u)) {
           if (!wait_source(p, u.src, abort)) {
             raise_error(p, abort, kErrSourceWait);
             ok = false;
@@ -674,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (PAIR == 2) {
             const uint32_t fb = leader_bar(&sm->full[stage]);
             if (leader) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&sm->full[stage]), kStageBytes);
-            if (kFull && u.src == p.self_src)
+            if (kEp && u.src == p.self_src)
               ptx::tma_load_2d_pair(ptx::smem_u32(sm->a[stage]), &tmap_a_self, fb, x,
                                     u.a_row + p.self_row_base + kBM * (int)rank);
             else
@@ -683,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             const uint32_t fb = ptx::smem_u32(&sm->full[stage]);
             ptx::mbar_arrive_expect_tx(fb, kStageBytes);
-            if (kFull && u.src == p.self_src)
+            if (kEp && u.src == p.self_src)
               ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a_self, fb, x, u.a_row + p.self_row_base);
             else
               ptx::tma_load_2d(ptx::smem_u32(sm->a[stage]), &tmap_a, fb, x, u.a_row);
@@ -712,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int k = 0;
       Unit u;
-      for (; ok && next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
+      for (; ok && next_unit<BN, kTileM, kSplit>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
         const int acc = ai & 1;
         const uint32_t aph = (ai >> 1) & 1u;
         // this buffer fully drained (tile ai - 2) ...
@@ -788,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int buf = 0;
     int k = 0;
     Unit u;
-    for (; next_unit<BN, kTileM>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
+    for (; next_unit<BN, kTileM, kSplit>(sm, p, k, unit0, unit_stride, num_units, u); ++ai) {
       const int acc = ai & 1;
       const uint32_t aph = (ai >> 1) & 1u;
       if (!wait_local(&sm->tfull[acc], aph)) {
@@ -846,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = pack2<OutT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-          if (kFull && p.qt_data != nullptr) {
+          if (kQuant && p.qt_data != nullptr) {
             // to_mx of the transposed 32 x 32 block: stage the warp's rows
             // (64-byte swizzle, as for a TMA store), then lane j reads column
             // j down the 32 rows and quantises it as one block of row col0 + j
@@ -886,14 +899,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) atomicOr(p.status, kErrQtRows);
             }
           }
-          if (kFull && p.q_data != nullptr) {
+          if (kQuant && p.q_data != nullptr) {
             // to_mx of this row's 32 output columns (host: out_cols % 32 == 0)
             if (lane < rows_here && grow < p.out_rows)
               quantize_block32<OutT>(w, p.q_data + grow * p.out_ld + col0, p.q_scale + grow * (p.out_ld / 32) + col0 / 32);
           }
-          if (kFull && p.q_only) return;
+          if (kQuant && p.q_only) return;
         }
-        if (kFull && u.dst != p.local_dst && rows_here < 32) {
+        if (kEp && u.dst != p.local_dst && rows_here < 32) {
           // A peer GPU's output, rows cut by the group edge: stage the warp's
           // rows x 64 B, then store them with 4 lanes per row, so each row's
           // 64 bytes cross NVLink as one contiguous run.  Output rows are
@@ -931,7 +944,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           buf ^= 1;
           return;
         }
-        if (kFull && u.dst != p.local_dst && p.inbox_chunks > 0) {
+        if (kEp && u.dst != p.local_dst && p.inbox_chunks > 0) {
           uint8_t* stg = sm->epi[q][buf];
           if (lane == 0) ptx::bulk_wait_read<1>();   // the copy that last used this buffer has read it
           __syncwarp();
@@ -953,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           buf ^= 1;
           return;
         }
-        if (use_tma || (kFull && u.dst != p.local_dst)) {
+        if (use_tma || (kEp && u.dst != p.local_dst)) {
           uint8_t* stg = sm->epi[q][buf];
           if (lane == 0) ptx::bulk_wait_read<1>();   // the store that last used this buffer has read it
           __syncwarp();
@@ -968,7 +981,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (kFull && p.accumulate)
+            if (kAcc && p.accumulate)
               ptx::tma_reduce_add_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
             else
               ptx::tma_store_2d(&omaps.m[u.dst], ptx::smem_u32(stg), col0, (int)(u.out_row + my_row0));
@@ -978,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (lane < rows_here && grow < p.out_rows) {
           OutT* dst = reinterpret_cast<OutT*>(p.out) + grow * p.out_ld + col0;
           const int ncols = min(kEpiCols, p.out_cols - col0);
-          if (kFull && sizeof(OutT) == 4 && p.accumulate) {
+          if (kAcc && sizeof(OutT) == 4 && p.accumulate) {
             // read-add-write; every element belongs to exactly one tile
             float* d = reinterpret_cast<float*>(dst);
 #pragma unroll
@@ -1001,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      if (!u.split) {
+      if (!kSplit || !u.split) {
         int ci0 = 0;
         if constexpr (kOvChunks > 1) {
           if (!zero) {
@@ -1137,7 +1150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) ptx::bulk_wait<0>();
     __syncwarp();
     // expert parallel: peers read this GPU's stores after a system-scope flag
-    if (kFull && p.n_dst > 1) __threadfence_system();
+    if (kEp && p.n_dst > 1) __threadfence_system();
   } else if (warp >= kSfWarp0 && warp < kSfWarp0 + 4) {
     // ------------------------------------------------------- scale writers
     // Lane l of warp q writes TMEM lane 32q + l of the stage's scale slot:
@@ -1170,7 +1183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++ls;
           return true;
         }
-        if (!next_unit<BN, kTileM>(sm, p, lk, unit0, unit_stride, num_units, lu)) return false;
+        if (!next_unit<BN, kTileM, kSplit>(sm, p, lk, unit0, unit_stride, num_units, lu)) return false;
         lhas = true;
         ls = -1;
       }
@@ -1180,7 +1193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows' atoms before it raises its flag); rows read in place are always there
     uint32_t ready = (p.self_src >= 0) ? (1u << p.self_src) : 0u;
     auto load = [&](uint4 (&r)[3]) {
-      if (kFull && p.src_flags && !((ready >> lu.src) & 1u)) {
+      if (kEp && p.src_flags && !((ready >> lu.src) & 1u)) {
         int got = 1;
         if (lane == 0) {
           got = wait_source(p, lu.src, abort) ? 1 : 0;

@@ -418,13 +418,15 @@ int mxgg_build_tile_map(const int32_t* group_end_offsets, int64_t E, int64_t M, 
 int mxgg_set_tile_config(int32_t tile_m, int32_t tile_n, int32_t group_m);
 
 /* Process default work schedule (a call's mxgg_gemm_config overrides it).  Output tiles are
- * dealt to the persistent CTA pairs in rounds; with SPLIT_TAIL (the default)
- * the tiles of the last, partial round are cut along the contraction into
- * pieces for the pairs that would otherwise idle, and the last piece to
- * finish sums the fp32 partials in a fixed order (results do not depend on
- * timing).  TILES deals every tile whole.  split_max caps the pieces per
- * tile (0: about the square root of the tile's 128-element stages; else
- * 2..64).  No counterpart in the reference. */
+ * dealt to the persistent CTA pairs in rounds.  TILES (what DEFAULT means)
+ * deals every tile whole.  With SPLIT_TAIL the tiles of the last, partial
+ * round are cut along the contraction into pieces for the pairs that would
+ * otherwise idle, and the last piece to finish sums the fp32 partials in a
+ * fixed order (results do not depend on timing); that schedule runs a
+ * kernel build with the split machinery compiled in, which measured ~3 %
+ * slower per stage, so it pays only where the tail round is long.
+ * split_max caps the pieces per tile (0: about the square root of the
+ * tile's 128-element stages; else 2..64).  No counterpart in the reference. */
 enum { MXGG_SCHED_DEFAULT = 0, MXGG_SCHED_TILES = 1, MXGG_SCHED_SPLIT_TAIL = 2 };
 int mxgg_set_schedule(int32_t schedule, int32_t split_max);
 

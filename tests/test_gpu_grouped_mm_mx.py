@@ -109,7 +109,7 @@ def test_fused_to_mx_schedules(schedule):
         offs = offsets(2, 2048, 32, seed=5)
         _check(_make(2, 2048, 2048, 4096, offs, seed=5))
     finally:
-        mxgg.set_schedule(mxgg._lib.SCHED_SPLIT_TAIL, 0)
+        mxgg.set_schedule(mxgg._lib.SCHED_DEFAULT, 0)
 
 
 def test_fused_to_mx_empty_contraction_and_errors():

@@ -174,24 +174,36 @@ def test_table_round_trip_merge_and_lookup():
 
 
 def test_packaged_default_table(monkeypatch):
-    # the packaged table covers every sweep shape x {fwd, wgrad} with valid configs
+    # the packaged table: valid configs for sweep shapes only (points where
+    # the library's own choice was not beaten carry no entry)
     t = tune.Table.load(tune.DEFAULT_TABLE)
-    shapes = tune.llama4_shapes()
-    for (E, M, N, K) in shapes:
-        for ps in ("fwd", "wgrad"):
-            cfg = t.lookup(ps, E, N, K)
-            assert cfg is not None and cfg.valid(), (ps, E, N, K)
+    sweep = {(E, N, K) for (E, M, N, K) in tune.llama4_shapes()}
+    assert t.entries
+    for (ps, E, N, K), (cfg, us, M) in t.entries.items():
+        assert ps in ("fwd", "wgrad") and (E, N, K) in sweep and cfg.valid() and us > 0
+    (ps, E, N, K), (cfg, _, _) = sorted(t.entries.items())[0]
     # installed at import unless MXGG_TUNE_TABLE says otherwise
     monkeypatch.delenv("MXGG_TUNE_TABLE", raising=False)
     try:
         tune.install_default()
-        assert tune.pick("fwd", *shapes[0][:1], *shapes[0][2:]) == t.lookup("fwd", shapes[0][0], shapes[0][2],
-                                                                            shapes[0][3])
+        assert tune.pick(ps, E, N, K) == cfg
         monkeypatch.setenv("MXGG_TUNE_TABLE", "none")
         tune.install_default()
-        assert tune.pick("fwd", shapes[0][0], shapes[0][2], shapes[0][3]) is None
+        assert tune.pick(ps, E, N, K) is None
     finally:
         tune.install(None)
+
+
+def test_worth_keeping_needs_a_confirmed_margin():
+    a, b = tune.Config(128, 256, 2, _lib.SCHED_TILES), tune.Config(256, 256, 8, _lib.SCHED_SPLIT_TAIL)
+    times = {tune.DEFAULT: 1.00, a: 0.90, b: 0.99}
+    assert tune.worth_keeping(times) == (a, 0.90)
+    # the second measurement must agree
+    assert tune.worth_keeping(times, confirm=lambda c: (0.95, 0.96)) is None
+    assert tune.worth_keeping(times, confirm=lambda c: (0.91, 1.00)) == (a, 0.90)
+    # within the margin of the library's choice: no entry
+    assert tune.worth_keeping({tune.DEFAULT: 1.00, a: 0.98}) is None
+    assert tune.worth_keeping({tune.DEFAULT: 1.00, a: 1.10}) is None
 
 
 def test_install_and_pick():
