@@ -995,9 +995,12 @@ def main():
                "unit": "TFLOPS", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
 
     if rank == 0 and args.detail:
-        for p, t in zip(probs, per):
-            print(json.dumps({"pass": p["pass_"], "shape": p["shape"], "us": round(t * 1e6, 1),
-                              "tflops": round(p["flops"] / t / 1e12, 1)}), file=sys.stderr)
+        for i, (p, t) in enumerate(zip(probs, per)):
+            row = {"pass": p["pass_"], "shape": p["shape"], "us": round(t * 1e6, 1),
+                   "tflops": round(p["flops"] / t / 1e12, 1)}
+            if phases is not None:
+                row["phases_us"] = [round(x * 1e6, 1) for x in phases[i]]
+            print(json.dumps(row), file=sys.stderr)
 
     ceiling = measured_mxfp8_ceiling(dev) if rank == 0 and not args.no_extras else None
     peaks, peaks_src = load_peaks()
