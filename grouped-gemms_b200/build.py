@@ -74,7 +74,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
         srcs = units()
         with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 1)) as ex:
             objs = list(ex.map(compile_one, srcs))
-        cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT + ".tmp", *objs]
+        # only the C ABI is exported: internal symbols stay local to this copy
+        cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared",
+               "-Xlinker", "--version-script=" + os.path.join(CSRC, "exports.map"), "-o", OUT + ".tmp", *objs]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -8,6 +8,11 @@
 #include "gemm_launch.cuh"
 
 namespace mxgg {
+// Internal to each build's translation unit: a function-local static of a
+// template with external linkage would be one object shared by every copy of
+// the library loaded in the process (a unique symbol), so a second copy
+// would skip setting its own kernels' shared-memory attribute.
+namespace {
 
 constexpr int kMaxLaunchDevices = 64;
 
@@ -68,4 +73,5 @@ cudaError_t launch_gemm_build(const GemmLaunch& l) {
   return launch_gemm_out<128, 6, 2, 1, kFeat>(l);
 }
 
+}  // namespace
 }  // namespace mxgg
