@@ -1177,6 +1177,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int lk = 0, ls = 0;
     Unit lu;
     bool lhas = false;
+    // this lane's 16 bytes of the unit's first A and B atoms (per-unit slab
+    // clamps and address arithmetic stay out of the per-stage path): stage
+    // ls of the unit is 512 bytes further per stage, [ls * 32]
+    const uint4* pa = nullptr;
+    const uint4* pb[kB];
     auto advance = [&]() -> bool {
       while (true) {
         if (lhas && ls + 1 < lu.st_count) {
@@ -1186,6 +1191,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!next_unit<BN, kTileM, kSplit>(sm, p, lk, unit0, unit_stride, num_units, lu)) return false;
         lhas = true;
         ls = -1;
+        const int sa = min(lu.a_sub + (int)rank, a_last);
+        pa = reinterpret_cast<const uint4*>(p.sfa_atoms + ((long long)sa * p.stages + lu.st_begin) * 512) + lane;
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          const int sb = min(lu.b_tile + b, lu.b_last);
+          pb[b] = reinterpret_cast<const uint4*>(p.sfb_atoms + ((long long)sb * p.stages + lu.st_begin) * 512) + lane;
+        }
       }
     };
     bool ok = true;
@@ -1213,14 +1225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // slabs past a group's or an expert's rows hold other rows' scales (or
       // are clamped to the last slab): they only feed rows that are never stored
-      const long long st = lu.st_begin + ls;
-      const int sa = min(lu.a_sub + (int)rank, a_last);
-      r[0] = __ldg(reinterpret_cast<const uint4*>(p.sfa_atoms + ((long long)sa * p.stages + st) * 512) + lane);
+      r[0] = __ldg(pa + ls * 32);
 #pragma unroll
-      for (int b = 0; b < kB; ++b) {
-        const int sb = min(lu.b_tile + b, lu.b_last);
-        r[1 + b] = __ldg(reinterpret_cast<const uint4*>(p.sfb_atoms + ((long long)sb * p.stages + st) * 512) + lane);
-      }
+      for (int b = 0; b < kB; ++b) r[1 + b] = __ldg(pb[b] + ls * 32);
     };
     // the atoms are written by the scale-pack kernel that precedes this grid
     ptx::griddep_wait();
