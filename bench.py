@@ -20,8 +20,10 @@
   computes M rows: weak scaling).  fwd and dgrad stream their rows to the
   hosting ranks over NVLink and send the output tiles back from the GEMM's
   epilogue (``mxgg.ep.FusedExpertParallel``; ``--ep-impl nccl`` for the NCCL
-  all-to-all baseline).  wgrad runs on the hosting rank, plus an all-reduce
-  over replicated experts when E < N.  Times are the max over ranks;
+  all-to-all baseline).  wgrad runs on the hosting rank; replicated experts
+  (E < N) sum their gradients in place over peer memory
+  (``mxgg.ep.ReplicaSum``; an NCCL all-reduce with ``--ep-impl nccl``).
+  Times are the max over ranks;
   ``expert_parallel`` splits them into phases.
 * ``moe_layer``: BASELINE config 5, weak-scaled (8 experts and 16384 tokens
   per GPU; 64 and 131072 at 8 GPUs): a top-2 MoE layer forward, up
@@ -181,7 +183,8 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123, impl="fused
     that every rank computes M rows.  fwd and dgrad
     run dispatch -> segment GEMM -> combine; wgrad runs on the hosting rank
     over the tokens it received (expert-major, as the forward's dispatch left
-    them) and sums replicas' gradients with an all-reduce.  Per-rank FLOPs
+    them) and sums replicas' gradients (peer-memory replica sum, or an NCCL
+    all-reduce for impl "nccl").  Per-rank FLOPs
     are 2*rows*N*K over the rows that rank computes; every rank sends all M of
     its rows, so the ranks' total is world * 2*M*N*K."""
     import torch
@@ -244,6 +247,13 @@ def build_ep_problems(device, shapes, passes, world, rank, seed=123, impl="fused
         for p in probs:
             if p["pass_"] != "wgrad":
                 p["fused"] = (fx, fx.plan(p["counts"], ep.ExpertPlacement(world, p["shape"][0])))
+    rep = [p for p in probs if p["pass_"] == "wgrad" and p["plan"].placement.replicas > 1]
+    if impl == "fused" and rep:
+        # replicated experts sum their weight gradients in place over peer memory
+        nbytes = max(p["plan"].placement.local * p["shape"][2] * p["shape"][3] * 2 for p in rep)
+        rs = ep.ReplicaSum(nbytes)
+        for p in rep:
+            p["rsum"] = rs
     torch.cuda.synchronize()
     return probs
 
@@ -313,10 +323,21 @@ def run_ep_problem(p, marks=None):
     if p["pass_"] == "wgrad":
         if marks:
             marks[0].record()
-        out = kernels.triton_mxfp8_wgrad(*p["args"])
-        if marks:
-            marks[1].record()
-        ep.replica_allreduce(plan.placement, out, p.get("groups"))
+        if "rsum" in p:
+            # the gradient goes straight into this rank's peer-visible replica buffer
+            from mxgg import ops, tune
+            go_q, _, ia_q, _, offs = p["args"]
+            L, N, K = offs.shape[0], go_q.shape[0], ia_q.shape[0]
+            out = ops.wgrad_into(*p["args"], p["rsum"].buffer((L, N, K), torch_bf16()),
+                                 tune.call_config(tune.pick("wgrad", L, N, K)))
+            if marks:
+                marks[1].record()
+            p["rsum"].sum_(plan.placement, out)
+        else:
+            out = kernels.triton_mxfp8_wgrad(*p["args"])
+            if marks:
+                marks[1].record()
+            ep.replica_allreduce(plan.placement, out, p.get("groups"))
         if marks:
             marks[2].record()
         return out
@@ -1118,6 +1139,8 @@ def main():
         barrier(world)
         for fx in {id(p["fused"][0]): p["fused"][0] for p in probs if "fused" in p}.values():
             fx.close()
+        for rs in {id(p["rsum"]): p["rsum"] for p in probs if "rsum" in p}.values():
+            rs.close()
         import torch.distributed as dist
         dist.destroy_process_group()
     if parity is not None and (parity["max_rel_l2"] > parity["tolerance"] or parity["device_status"] != 0):

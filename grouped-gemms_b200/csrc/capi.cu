@@ -1110,6 +1110,35 @@ int mxgg_peer_barrier(void* const* flags, int32_t world, int32_t rank, int32_t e
   return MXGG_OK;
 }
 
+int mxgg_replica_sum(void* const* bufs, int32_t n, int32_t me, int64_t elems, int dtype, void* stream) {
+  if (!bufs || n < 1 || n > kMaxDst || me < 0 || me >= n || elems < 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_replica_sum: bad arguments (n %d, me %d, elems %lld)", (int)n, (int)me,
+                (long long)elems);
+  const int es = dtype == MXGG_DTYPE_F32 ? 4 : (dtype == MXGG_DTYPE_BF16 || dtype == MXGG_DTYPE_F16) ? 2 : 0;
+  if (es == 0) return fail(MXGG_ERR_INVALID, "mxgg_replica_sum: unknown dtype %d", dtype);
+  if ((elems * es) % 16 != 0)
+    return fail(MXGG_ERR_UNSUPPORTED, "mxgg_replica_sum: %lld bytes is not a multiple of 16", (long long)(elems * es));
+  ReplicaBufs b{};
+  for (int i = 0; i < n; ++i) {
+    if (!bufs[i] || !aligned(bufs[i], 16))
+      return fail(MXGG_ERR_INVALID, "mxgg_replica_sum: null or unaligned buffer of replica %d", i);
+    b.p[i] = static_cast<uint8_t*>(bufs[i]);
+  }
+  if (n == 1 || elems == 0) return MXGG_OK;
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long chunks = elems * es / 16;
+  const long long lo = chunks * me / n, hi = chunks * (me + 1) / n;
+  if (hi <= lo) return MXGG_OK;
+  const unsigned blocks = (unsigned)std::max(1LL, std::min<long long>((hi - lo + 255) / 256, (long long)st->num_sms * 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MXGG_DTYPE_F32) launch_replica_sum<float>(b, n, lo, hi, blocks, s);
+  else if (dtype == MXGG_DTYPE_BF16) launch_replica_sum<__nv_bfloat16>(b, n, lo, hi, blocks, s);
+  else launch_replica_sum<__half>(b, n, lo, hi, blocks, s);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
 int mxgg_inbox_unpack(const void* inbox, void* out, const int32_t* row_blocks, int64_t n_row_blocks,
                       int64_t row_bytes, void* stream) {
   if (n_row_blocks < 0 || row_bytes <= 0 || row_bytes % 64 != 0)

@@ -65,6 +65,7 @@ constexpr int kSfSlotsMax = 5;    // scale slots in TMEM (stages the writers may
 constexpr int kSfRing = 4;        // stages of scale atoms the writers hold in registers
 constexpr int kMaxGroups = 256;   // groups handled by the in-kernel table
 constexpr int kMaxDst = 8;        // output destinations (ranks) of an expert-parallel forward
+constexpr int kMaxSrc = 32;       // source ids of a streamed dispatch (bits of a readiness mask)
 constexpr int kTmemCols = 512;
 
 enum : int { kFwd = 0, kWgrad = 1 };
@@ -156,12 +157,13 @@ struct GemmParams {
   // 2 KB runs at several times the rate of 64-byte row pieces.
   void* inbox_dst[kMaxDst];
   int inbox_chunks;          // 64-byte chunks per output row; 0: no inboxes
-  // Streaming dispatch: the rows of group g come from rank group_dst[g]; the
-  // producer loads a tile only once that rank's slot of src_flags has reached
-  // src_epoch (written, after its copies, by the sender).  Null: no waits.
+  // Streaming dispatch: the rows of group g come from source id group_src[g]
+  // (a rank, or one piece of a rank's rows: ids below kMaxSrc); the producer
+  // loads a tile only once that id's slot of src_flags has reached src_epoch
+  // (written, after its copy, by the sender).  Null: no waits.
   const int* src_flags;
   int src_epoch;
-  const int32_t* group_src;  // source rank of each group's rows (null: group_dst, the rows' owner)
+  const int32_t* group_src;  // source id of each group's rows (null: group_dst, the rows' owner)
   // Rows of source self_src are read in place through the second A map
   // (row + self_row_base) instead of from the receive buffer; they never wait.
   int self_src;              // -1: none
@@ -291,7 +293,7 @@ __device__ __forceinline__ void build_group_table(S* sm, const GemmParams& p, in
     if (p.group_dst) {
       sm->g_dst[i] = min(max(__ldg(p.group_dst + i), 0), p.n_dst - 1);
       sm->g_dst_row[i] = max(__ldg(p.group_dst_row + i), 0);
-      sm->g_src[i] = p.group_src ? min(max(__ldg(p.group_src + i), 0), p.n_dst - 1) : sm->g_dst[i];
+      sm->g_src[i] = p.group_src ? min(max(__ldg(p.group_src + i), 0), kMaxSrc - 1) : sm->g_dst[i];
     } else {
       sm->g_dst[i] = 0;
       sm->g_dst_row[i] = -1;

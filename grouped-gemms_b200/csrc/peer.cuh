@@ -79,4 +79,77 @@ __global__ void __launch_bounds__(256) inbox_unpack_kernel(const uint8_t* __rest
   }
 }
 
+// Sums the n replicas of a flat array that n GPUs hold, one copy each, in
+// buffers this process has mapped (b.p[r]: replica r's buffer).  The replica
+// running this kernel owns the 16-byte chunks [lo, hi): it loads each chunk
+// from every replica (its own over HBM, the peers' over NVLink), adds them in
+// fp32 in replica order 0, 1, ..., n - 1, rounds once to T and stores the sum
+// into every replica.  The replicas own disjoint chunk ranges, so each
+// element is summed once, in the same order, and every replica ends with the
+// same bits.  Inputs are published before the launch and the sums after it
+// by mxgg_peer_barrier over the replicas.
+struct ReplicaBufs {
+  uint8_t* p[kMaxDst];
+};
+
+template <typename T>
+__device__ __forceinline__ float elem_to_float(T v);
+template <>
+__device__ __forceinline__ float elem_to_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float elem_to_float<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float elem_to_float<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T float_to_elem(float v);
+template <>
+__device__ __forceinline__ float float_to_elem<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 float_to_elem<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half float_to_elem<__half>(float v) { return __float2half_rn(v); }
+
+template <typename T, int NR>
+__global__ void __launch_bounds__(256) replica_sum_kernel(const ReplicaBufs b, long long lo, long long hi) {
+  constexpr int kL = 16 / (int)sizeof(T);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long c = lo + (long long)blockIdx.x * blockDim.x + threadIdx.x; c < hi; c += stride) {
+    uint4 v[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) v[r] = __ldcs(reinterpret_cast<const uint4*>(b.p[r]) + c);
+    float acc[kL];
+    {
+      const T* e = reinterpret_cast<const T*>(&v[0]);
+#pragma unroll
+      for (int i = 0; i < kL; ++i) acc[i] = elem_to_float<T>(e[i]);
+    }
+#pragma unroll
+    for (int r = 1; r < NR; ++r) {
+      const T* e = reinterpret_cast<const T*>(&v[r]);
+#pragma unroll
+      for (int i = 0; i < kL; ++i) acc[i] += elem_to_float<T>(e[i]);
+    }
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int i = 0; i < kL; ++i) oe[i] = float_to_elem<T>(acc[i]);
+#pragma unroll
+    for (int r = 0; r < NR; ++r) __stcs(reinterpret_cast<uint4*>(b.p[r]) + c, o);
+  }
+}
+
+template <typename T>
+void launch_replica_sum(const ReplicaBufs& b, int n, long long lo, long long hi, unsigned blocks, cudaStream_t s) {
+  switch (n) {
+    case 2: replica_sum_kernel<T, 2><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    case 3: replica_sum_kernel<T, 3><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    case 4: replica_sum_kernel<T, 4><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    case 5: replica_sum_kernel<T, 5><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    case 6: replica_sum_kernel<T, 6><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    case 7: replica_sum_kernel<T, 7><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+    default: replica_sum_kernel<T, 8><<<blocks, 256, 0, s>>>(b, lo, hi); break;
+  }
+}
+
 }  // namespace mxgg

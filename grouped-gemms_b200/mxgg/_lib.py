@@ -104,6 +104,7 @@ SIGNATURES = {
     "mxgg_ipc_close": (_int, [_vp]),
     "mxgg_copy_async": (_int, [_vp, _vp, _i64, _vp]),
     "mxgg_peer_barrier": (_int, [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp]),
+    "mxgg_replica_sum": (_int, [ctypes.POINTER(_vp), _i32, _i32, _i64, _int, _vp]),
     "mxgg_wgrad_accumulate": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
     "mxgg_grouped_mm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "mxgg_quantize_mx": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _int, _int, _vp]),

@@ -198,6 +198,84 @@ def replica_groups(placement: ExpertPlacement) -> dict:
     return out
 
 
+class ReplicaSum:
+    """Sums replicated experts' weight gradients over NVLink peer memory, in
+    place: the fused counterpart of `replica_allreduce`.
+
+    Collective to construct (every rank allocates `max_bytes` that its peers
+    map).  Per step, on every rank:
+
+        g = rs.buffer((L, N, K), torch.bfloat16)     # this rank's replica
+        mxgg.ops.wgrad_into(..., out=g)              # write the gradient there
+        rs.sum_(placement, g)                        # collective over all ranks
+
+    `sum_` runs a cross-GPU barrier over each replica group, then every
+    replica sums its 1/R share of the array from all R replicas (fp32, in
+    replica order, one rounding) and stores the result into all of them, then
+    a second barrier: each rank's NVLink traffic is 2 (R-1)/R of the array,
+    as for a ring all-reduce, but in one kernel at copy speed.  All replicas
+    end with identical bits; for R = 2 they equal NCCL's bf16 / fp32 sum.
+    The waits are bounded (status bit 64 on timeout, raised by
+    `check_status` of a `FusedExpertParallel` or `mxgg.device_status`)."""
+
+    def __init__(self, max_bytes: int, group=None):
+        from .peer import PeerBuffer
+        dist = _dist()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer-memory replica sum reaches at most 8 ranks (one NVLink domain)")
+        self.max_bytes = int(max_bytes)
+        self.buf = PeerBuffer(max(self.max_bytes, 256), group)
+        self.flags = PeerBuffer(256, group)
+        self.epoch = 0
+
+    def close(self) -> None:
+        self.buf.close()
+        self.flags.close()
+
+    def buffer(self, shape, dtype: torch.dtype) -> Tensor:
+        """This rank's replica buffer as a tensor (valid until the next `buffer` use)."""
+        return self.buf.view(shape, dtype)
+
+    def sum_(self, placement: ExpertPlacement, t: Tensor) -> Tensor:
+        """Collective: every replica of this rank's experts gets the sum of
+        all replicas' `t` (no-op without replicas).  `t` is best the tensor
+        `buffer` returned; any other contiguous tensor is copied in and out."""
+        import ctypes
+        from . import _lib
+        from .ops import _OUT_DTYPES
+        if placement.world != self.world:
+            raise ValueError("placement and process group disagree on the world size")
+        if placement.replicas == 1:
+            return t
+        if t.dtype not in _OUT_DTYPES or not t.is_contiguous():
+            raise ValueError("sum_ takes a contiguous bf16, fp16 or fp32 tensor")
+        nbytes = t.numel() * t.element_size()
+        if nbytes > self.max_bytes:
+            raise ValueError(f"{nbytes} bytes exceed the {self.max_bytes}-byte replica buffers")
+        inplace = t.data_ptr() == self.buf.ptrs[self.rank]
+        if not inplace:
+            self.buffer(t.shape, t.dtype).copy_(t)
+        ranks = placement.replica_group(self.rank)
+        me = ranks.index(self.rank)
+        lib = _lib.load()
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        flags = (ctypes.c_void_p * len(ranks))(*[self.flags.ptrs[r] for r in ranks])
+        bufs = (ctypes.c_void_p * len(ranks))(*[self.buf.ptrs[r] for r in ranks])
+        # every rank takes the same epochs in the same order (each sum_ is collective)
+        self.epoch += 1
+        _lib.check(lib.mxgg_peer_barrier(flags, len(ranks), me, self.epoch, stream), "mxgg_peer_barrier")
+        _lib.check(lib.mxgg_replica_sum(bufs, len(ranks), me, t.numel(), _OUT_DTYPES[t.dtype], stream),
+                   "mxgg_replica_sum")
+        self.epoch += 1
+        _lib.check(lib.mxgg_peer_barrier(flags, len(ranks), me, self.epoch, stream), "mxgg_peer_barrier")
+        if not inplace:
+            t.copy_(self.buffer(t.shape, t.dtype))
+        return t
+
+
 # ----------------------------------------------------------------------------
 # Fused path: peer-memory dispatch, combine fused into the GEMM epilogue.
 # ----------------------------------------------------------------------------
@@ -207,7 +285,7 @@ class _Segments:
     expert: Tensor               # local expert of each segment
     dst: Tensor                  # output destination of each segment's rows
     dst_row: Tensor              # first row of the segment there
-    src: Tensor                  # rank each segment's rows come from
+    src: Tensor                  # source id of each segment's rows: rank + world * piece
 
 
 @dataclass
@@ -222,7 +300,8 @@ class FusedPlan:
 
     rows_local: int
     rows_recv: int               # all rows this rank multiplies (its own included)
-    copies: List[tuple]          # (dest rank, first row there, first local row, rows) to peers, in sending order
+    copies: List[tuple]          # (dest rank, first row there, first local row, rows, flag slot there) to
+                                 #  peers, in sending order
     pack: List[tuple]            # (dest rank, cumulative segment ends (device), first 128-row scale slab
                                  #  there, first local row, rows), this rank included
     self_base: int               # local row of the first row this rank routes to itself
@@ -233,19 +312,59 @@ class FusedPlan:
     remote_blocks: Tensor        # this rank's 32-row blocks computed by peers (unpacked from its inbox)
 
 
-def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int) -> dict:
+MAX_SOURCE_IDS = 32          # source-flag slots the GEMM tracks (a 32-bit readiness mask)
+MAX_SEGMENTS = 256           # segments the GEMM's in-kernel group table holds
+PIECE_ALIGN = 256            # rows: a piece cut lands on the GEMM's tile grid of its segment
+MAX_PIECES = 4               # pieces per (source, destination) block
+
+
+def _piece_cuts(seg_rows: List[int], n_pieces: int, align: int = PIECE_ALIGN) -> List[int]:
+    """Row offsets inside one source's block (ascending, neither 0 nor the
+    block's end) that cut it into about `n_pieces` equal pieces.  Each cut
+    is moved forward to a segment start or to a multiple of `align` rows
+    past one, so that no tile of the GEMM straddles two pieces and the
+    128-row scale slabs of the cut segments are those of the uncut ones."""
+    total = sum(seg_rows)
+    cuts: List[int] = []
+    for c in range(1, n_pieces):
+        t = (c * total) // n_pieces
+        lo, cut = 0, total
+        for r in seg_rows:
+            if t < lo + r:
+                cut = lo + min(-(-(t - lo) // align) * align, r)
+                break
+            lo += r
+        if 0 < cut < total and (not cuts or cut > cuts[-1]):
+            cuts.append(cut)
+    return cuts
+
+
+def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int, piece_rows: int = 2048) -> dict:
     """The fused path's routing arithmetic for `rank`, from every rank's
     per-expert row counts C[s][e] (rows sorted by expert on each rank).
 
     Receiver d's layout: sources in arrival order d, d-1, d-2, ..., each
-    source's rows grouped by d's local experts.  Returns plain lists:
-      copies   (dest, first row there, first local row, rows), to peers, in sending order d+1, d+2, ...
+    source's rows grouped by d's local experts.  A peer's block of rows
+    travels in up to MAX_PIECES pieces of at least `piece_rows` rows (0: one
+    piece), each copied and flagged on its own, so the GEMM starts on a
+    piece as soon as it lands instead of waiting for the whole block; the
+    segments are cut at the pieces' edges and carry the piece's source id
+    s + world * piece (flag slot of that id).  Returns plain lists:
+      copies   (dest, first row there, first local row, rows, flag slot there), to peers, in sending
+               order d+1, d+2, ...
       pack     (dest, cumulative segment ends, first 128-row scale slab there, first local row, rows),
                this rank included
-      seg      offs / expert / src / dst_row / local_row of this rank's receive segments
+      seg      offs / expert / src / dst / dst_row / local_row of this rank's receive segments
       self_base, rows_recv, rows_local, dst_rows, need_recv, inbox_ok, remote_blocks
     """
     world, E = pl.world, pl.n_experts
+    max_pieces = min(MAX_PIECES, MAX_SOURCE_IDS // world)
+    if piece_rows <= 0 or world * pl.local + world * (max_pieces - 1) > MAX_SEGMENTS:
+        max_pieces = 1
+
+    def n_pieces(rows):
+        return max(1, min(max_pieces, rows // piece_rows)) if max_pieces > 1 else 1
+
     send = [[0] * world for _ in range(world)]
     start = [[0] * world for _ in range(world)]
     seen = [[False] * world for _ in range(world)]
@@ -278,22 +397,34 @@ def fused_layout(C: List[List[int]], pl: ExpertPlacement, rank: int) -> dict:
         d = (rank + j) % world
         if send[rank][d]:
             if d != rank:
-                copies.append((d, recv_off[rank][d], start[rank][d], send[rank][d]))
+                b = [0] + _piece_cuts(seg_rows(rank, d), n_pieces(send[rank][d])) + [send[rank][d]]
+                for c in range(len(b) - 1):
+                    copies.append((d, recv_off[rank][d] + b[c], start[rank][d] + b[c], b[c + 1] - b[c],
+                                   rank + world * c))
             cum, acc = [], 0
             for c in seg_rows(rank, d):
                 acc += c
                 cum.append(acc)
             pack.append((d, cum, m0[rank][d], start[rank][d], send[rank][d]))
-    seg = {"offs": [], "expert": [], "src": [], "dst_row": [], "local_row": []}
+    seg = {"offs": [], "expert": [], "src": [], "dst": [], "dst_row": [], "local_row": []}
     total = 0
     for s in order(rank):
-        for le, (e, rows) in enumerate(zip(pl.experts_of(rank), seg_rows(s, rank))):
-            seg["local_row"].append(total)
-            total += rows
-            seg["offs"].append(total)
-            seg["expert"].append(le)
-            seg["src"].append(s)
-            seg["dst_row"].append(sum(C[s][:e]))
+        rows_s = seg_rows(s, rank)
+        # own rows are read in place and never wait: one piece
+        cuts = [] if s == rank else _piece_cuts(rows_s, n_pieces(send[s][rank]))
+        pos = 0                         # row inside the source's block
+        for le, (e, rows) in enumerate(zip(pl.experts_of(rank), rows_s)):
+            edges = [pos] + [c for c in cuts if pos < c < pos + rows] + [pos + rows]
+            for a, b in zip(edges[:-1], edges[1:]):
+                piece = sum(1 for c in cuts if c <= a)
+                seg["local_row"].append(total)
+                total += b - a
+                seg["offs"].append(total)
+                seg["expert"].append(le)
+                seg["src"].append(s + world * piece)
+                seg["dst"].append(s)
+                seg["dst_row"].append(sum(C[s][:e]) + a - pos)
+            pos += rows
     blocks, row = [], 0
     for e in range(E):
         if pl.dest(rank, e) != rank:
@@ -315,10 +446,10 @@ class FusedExpertParallel:
     1. each rank packs the scale atoms of its rows straight into every
        destination's atom buffer (in the destination's tile numbering), then,
        on a side stream, copies its rows into the destinations' receive
-       buffers one destination after another (copy engine; its own rows first)
-       and after each copy raises that destination's flag for it;
+       buffers one destination after another (copy engine), a large block in
+       up to four pieces, and after each copy raises that piece's flag there;
     2. meanwhile the GEMM runs over the whole receive buffer: its producer
-       loads a segment's tiles as soon as the segment's source has raised its
+       loads a segment's tiles as soon as the segment's piece has raised its
        flag (a bounded wait), and its epilogue sends every output block to the
        rank that owns the rows (TMA stores for its own rows; 2 KB bulk copies
        into the owner's inbox for peers'), so both transfers overlap the math;
@@ -349,7 +480,7 @@ class FusedExpertParallel:
         self.out = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
         self.inbox = PeerBuffer(max(self.max_local_rows * self.max_n * 4, 256), group)
         self.flags = PeerBuffer(256, group)          # barrier slots
-        self.src_flags = PeerBuffer(256, group)      # streaming-dispatch slots, one per source
+        self.src_flags = PeerBuffer(4 * MAX_SOURCE_IDS, group)   # streaming-dispatch slots, one per source id
         self.epoch = 0
         self.src_epoch = 0
         self._side = torch.cuda.Stream()
@@ -365,11 +496,15 @@ class FusedExpertParallel:
             b.close()
 
     # -------------------------------------------------------------- planning
-    def plan(self, expert_counts: Sequence[int], placement: Optional[ExpertPlacement] = None) -> FusedPlan:
+    def plan(self, expert_counts: Sequence[int], placement: Optional[ExpertPlacement] = None,
+             piece_rows: int = 2048) -> FusedPlan:
         """Collective: all-gather every rank's per-expert counts and derive the
         copies, atom packing, segment tables and output heights.  The shared
         buffers do not depend on the placement, so one instance serves several
-        (`placement` overrides the constructor's for this plan).
+        (`placement` overrides the constructor's for this plan).  A peer's
+        block of at least 2 * `piece_rows` rows travels in pieces that the GEMM
+        starts on one by one (`fused_layout`); every rank must pass the same
+        value.
 
         It also gathers every rank's device status word (read and cleared
         here) and raises MxggError on all ranks alike when any of them is set:
@@ -400,7 +535,7 @@ class FusedExpertParallel:
             raise _lib.MxggError("fused expert parallelism: a device-side wait gave up in the previous call "
                                  "(rank: status word) " + ", ".join(f"{r}: {v:#x}" for r, v in sorted(bad.items())))
         C = [row[:E] for row in gathered]                     # C[s][e]
-        lay = fused_layout(C, pl, rank)
+        lay = fused_layout(C, pl, rank, piece_rows)
         for d in range(world):
             if lay["need_recv"][d] > self._caps[d][0] or lay["dst_rows"][d] > self._caps[d][1]:
                 raise ValueError(f"fused EP buffers of rank {d} too small: {lay['need_recv'][d]} received / "
@@ -411,7 +546,7 @@ class FusedExpertParallel:
         o, x, sr = i32(seg["offs"]), i32(seg["expert"]), i32(seg["src"])
         return FusedPlan(rows_local=lay["rows_local"], rows_recv=lay["rows_recv"], copies=lay["copies"], pack=pack,
                          self_base=lay["self_base"],
-                         seg=_Segments(o, x, sr, i32(seg["dst_row"]), sr),
+                         seg=_Segments(o, x, i32(seg["dst"]), i32(seg["dst_row"]), sr),
                          local_seg=_Segments(o, x, i32([rank] * len(seg["offs"])), i32(seg["local_row"]), sr),
                          dst_rows=lay["dst_rows"], inbox_ok=lay["inbox_ok"],
                          remote_blocks=i32(lay["remote_blocks"] if lay["inbox_ok"] else []))
@@ -467,11 +602,11 @@ class FusedExpertParallel:
         side = self._side
         side.wait_stream(cur)
         ssp = ctypes.c_void_p(side.cuda_stream)
-        for (d, dst_row, src_row, rows) in plan.copies:
+        for (d, dst_row, src_row, rows, slot) in plan.copies:
             _lib.check(lib.mxgg_copy_async(ctypes.c_void_p(self.recv_a.ptrs[d] + dst_row * K),
                                            ctypes.c_void_p(a_q.data_ptr() + src_row * K), rows * K, ssp),
                        "mxgg_copy_async")
-            _lib.check(lib.mxgg_peer_signal(ctypes.c_void_p(self.src_flags.ptrs[d] + 4 * self.rank),
+            _lib.check(lib.mxgg_peer_signal(ctypes.c_void_p(self.src_flags.ptrs[d] + 4 * slot),
                                             self.src_epoch, ssp), "mxgg_peer_signal")
         # (a destination this rank sends no rows to never waits for it: its segments are empty)
         a_q.record_stream(side)

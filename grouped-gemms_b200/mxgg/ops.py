@@ -347,20 +347,34 @@ def _wgrad_impl(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, 
     _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, what="mxgg::wgrad")
     if out_dtype not in _OUT_DTYPES:
         raise TypeError(f"mxgg::wgrad: unsupported out_dtype {out_dtype}")
+    out = torch.empty((offs.shape[0], go_t.shape[0], ia_t.shape[0]), dtype=out_dtype, device=go_t.device)
+    wgrad_into(go_t, go_scale, ia_t, ia_scale, offs, out, cfg, scale_layout)
+    return out
+
+
+def wgrad_into(go_t: Tensor, go_scale: Tensor, ia_t: Tensor, ia_scale: Tensor, offs: Tensor, out: Tensor,
+               cfg: Optional[List[int]] = None, scale_layout: int = 0) -> Tensor:
+    """The weight gradient written into an existing contiguous (E, N, K)
+    tensor of any output dtype (for example a buffer peers can read, which
+    the replicas of an expert then sum in place); returns `out`."""
+    _require_cuda(go_t, go_scale, ia_t, ia_scale, offs, out, what="mxgg::wgrad")
+    if out.dtype not in _OUT_DTYPES:
+        raise TypeError(f"mxgg::wgrad: unsupported out dtype {out.dtype}")
     N, M = go_t.shape
     K = ia_t.shape[0]
     E = offs.shape[0]
+    if out.shape != (E, N, K) or not out.is_contiguous():
+        raise ValueError(f"mxgg::wgrad: out must be a contiguous ({E}, {N}, {K}) tensor")
     go_t = go_t.contiguous()
     ia_t = ia_t.contiguous()
     go_scale = as_u8(go_scale).contiguous()
     ia_scale = as_u8(ia_scale).contiguous()
     offs = offs.to(torch.int32).contiguous()
-    out = torch.empty((E, N, K), dtype=out_dtype, device=go_t.device)
     lib = _lib.load()
     ws = _workspace(lib.mxgg_wgrad_workspace_size(N, K, M, E), go_t.device)
     with torch.cuda.device(go_t.device):
         _lib.check(lib.mxgg_wgrad_cfg(_ptr(go_t), _ptr(go_scale), _ptr(ia_t), _ptr(ia_scale), _ptr(offs),
-                                      N, K, M, E, _ptr(out), _OUT_DTYPES[out_dtype], _lib.gemm_config(cfg, scale_layout),
+                                      N, K, M, E, _ptr(out), _OUT_DTYPES[out.dtype], _lib.gemm_config(cfg, scale_layout),
                                       _ptr(ws), ws.numel(), _stream(go_t.device)), "mxgg_wgrad")
     return out
 

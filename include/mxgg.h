@@ -254,13 +254,15 @@ int mxgg_grouped_mm_ep(const void* a, const void* b, const void* a_scale, const 
 /* Streaming dispatch for mxgg_grouped_mm_ep.  a_atoms (or null): the A
  * scales already packed into the GEMM's 128x4 atoms by the senders
  * (mxgg_pack_a_atoms, at least mxgg_ep_atom_bytes(M, K, n_segments) bytes,
- * 256-byte aligned); src_flags (or null): a device int32 array indexed by
- * source rank; the GEMM loads a segment's rows only after
- * src_flags[source of s] has reached src_epoch (a bounded wait, status
+ * 256-byte aligned); src_flags (or null): a device int32 array of 32 slots
+ * indexed by source id; the GEMM loads a segment's rows only after
+ * src_flags[source id of s] has reached src_epoch (a bounded wait, status
  * bit 128 on timeout).  Senders publish with mxgg_peer_signal after their
  * copies, so segments start as their rows land instead of after a barrier.
  * segment_src (device int32, or null when every segment's source is its
- * destination segment_dst): the rank each segment's rows come from.
+ * destination segment_dst): the source id of each segment's rows, in
+ * [0, 32): the sending rank, or rank + n_dst * piece when a sender's rows
+ * travel in pieces that it flags one by one.
  * a_self (or null): an (a_self_rows, K) e4m3 tensor holding the rows of
  * source self_src, read in place -- segment rows of that source at receive
  * row r are a_self row r + self_row_base -- so a rank's own rows need no copy
@@ -287,6 +289,21 @@ int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, i
  * needed, and a GEMM filling the GPU while it waits for such flags from its
  * peers cannot hold it back. */
 int mxgg_peer_signal(void* slot, int32_t epoch, void* stream);
+
+/* Sums the n replicas of an array of `elems` elements of `dtype`
+ * (MXGG_DTYPE_BF16 / F16 / F32) that n GPUs hold, one copy each -- the
+ * weight gradients of a replicated expert -- in place over NVLink.  bufs is
+ * a HOST array of the n replicas' buffers as this process addresses them
+ * (its own, and the peers' mapped by mxgg_ipc_open), bufs[me] this GPU's.
+ * Replica `me` takes its 1/n share of the array's 16-byte chunks: loads them
+ * from every replica, adds in fp32 in replica order 0..n-1, rounds once and
+ * stores the sum into every replica, so all copies end bit-identical.  Every
+ * replica calls it with the same bufs order, n and elems and its own `me`,
+ * between two mxgg_peer_barrier calls over the replicas (the first publishes
+ * the inputs, the second the sums).  elems * element size must be a multiple
+ * of 16 and the buffers 16-byte aligned; n <= 8.  The reference has no
+ * multi-GPU path; this replaces an all-reduce over the replica group. */
+int mxgg_replica_sum(void* const* bufs, int32_t n, int32_t me, int64_t elems, int dtype, void* stream);
 
 /* Copies the listed 32-row blocks (device int32 row-block indices) of an
  * inbox filled by peers' mxgg_grouped_mm_ep into the row-major output whose

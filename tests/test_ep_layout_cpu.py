@@ -25,10 +25,12 @@ def _cases():
     return out
 
 
+@pytest.mark.parametrize("piece_rows", [2048, 64])
 @pytest.mark.parametrize("world,E,align,C", _cases())
-def test_fused_layout_moves_every_row(world, E, align, C):
+def test_fused_layout_moves_every_row(world, E, align, C, piece_rows):
+    """piece_rows 64 cuts most peer blocks into pieces (up to four each)."""
     pl = ExpertPlacement(world, E)
-    lays = [fused_layout(C, pl, r) for r in range(world)]
+    lays = [fused_layout(C, pl, r, piece_rows=piece_rows) for r in range(world)]
     # each rank's local rows, tagged (owner, local row, expert)
     local = []
     for s in range(world):
@@ -38,10 +40,13 @@ def test_fused_layout_moves_every_row(world, E, align, C):
         local.append(rows)
     # receive buffers: peers' copies; a rank's own slot stays empty (read in place)
     recv = [[None] * lays[d]["rows_recv"] for d in range(world)]
+    slot_of = [[None] * lays[d]["rows_recv"] for d in range(world)]   # flag slot raised after the row's copy
     for s in range(world):
-        for (d, dst_row, src_row, rows) in lays[s]["copies"]:
-            assert d != s
+        for (d, dst_row, src_row, rows, slot) in lays[s]["copies"]:
+            assert d != s and rows > 0
+            assert slot % world == s and 0 <= slot < 32
             recv[d][dst_row:dst_row + rows] = local[s][src_row:src_row + rows]
+            slot_of[d][dst_row:dst_row + rows] = [slot] * rows
     for d in range(world):
         lay = lays[d]
         seg = lay["seg"]
@@ -50,12 +55,17 @@ def test_fused_layout_moves_every_row(world, E, align, C):
         g_cum = 0          # 128-row scale slabs of the segments so far
         first_slab = {}
         for i, hi in enumerate(seg["offs"]):
-            src, le = seg["src"][i], seg["expert"][i]
+            sid, le = seg["src"][i], seg["expert"][i]
+            src = sid % world
+            assert seg["dst"][i] == src
             e = pl.experts_of(d)[le]
             first_slab.setdefault(src, g_cum)
             for k, r in enumerate(range(lo, hi)):
                 row = local[d][lay["self_base"] + r] if src == d else recv[d][r]
                 assert row is not None, "a received row was never copied"
+                if src != d:
+                    # the segment waits on the flag raised after this very row's copy
+                    assert slot_of[d][r] == sid
                 owner, lrow, ex = row
                 assert owner == src and ex == e
                 # the output row goes back to its owner's exact position
@@ -63,6 +73,14 @@ def test_fused_layout_moves_every_row(world, E, align, C):
                 assert seg["local_row"][i] == lo
             g_cum += (hi - lo + 127) // 128
             lo = hi
+        # pieces cut segments only on their 256-row tile grid: the 128-row scale
+        # slabs (and the GEMM's tiles) are those of the uncut segments
+        uncut = 0
+        for s in range(world):
+            for e in pl.experts_of(d):
+                if pl.dest(s, e) == d:
+                    uncut += (C[s][e] + 127) // 128
+        assert g_cum == uncut
         # every row routed to d arrived exactly once
         want = sorted(r for s in range(world) for r in local[s] if pl.dest(s, r[2]) == d)
         got = sorted(local[d][lay["self_base"] + r] if seg["src"][i] == d else recv[d][r]
@@ -83,3 +101,24 @@ def test_fused_layout_moves_every_row(world, E, align, C):
             continue
         remote = {i // 32 for i, (_, _, e) in enumerate(local[r]) if pl.dest(r, e) != r}
         assert set(lay["remote_blocks"]) == remote
+
+
+def test_pieces_cut_large_blocks_on_the_tile_grid():
+    from mxgg.ep import _piece_cuts
+    # one segment of 16640 rows: four pieces, cuts on multiples of 256
+    cuts = _piece_cuts([16640], 4)
+    assert cuts == [4352, 8448, 12544]
+    # a cut moves forward to the next multiple of 256 rows past its segment's start ...
+    assert _piece_cuts([100, 5000], 2) == [2660]
+    # ... or, when the segment ends first, to the next segment's start
+    assert _piece_cuts([1000, 100, 1000], 2) == [1100]
+    # blocks too short for pieces stay whole
+    assert _piece_cuts([300], 1) == []
+    pl = ExpertPlacement(2, 2)
+    C = [[1280, 15360], [15360, 1280]]
+    lay = fused_layout(C, pl, 0)
+    # rank 0 sends 15360 rows to rank 1 in four flagged pieces, slots 0, 2, 4, 6
+    assert [c[4] for c in lay["copies"]] == [0, 2, 4, 6]
+    assert sum(c[3] for c in lay["copies"]) == 15360
+    # it receives rank 1's 15360 rows in four pieces; its own 1280 rows stay whole
+    assert lay["seg"]["src"] == [0, 1, 3, 5, 7]

@@ -58,7 +58,8 @@ def _worker(rank, world, store, q, E, impl, align, big=False):
             from mxgg.ep import FusedExpertParallel
             cap = 8 * 32 * E * (16 if big else 1)             # most rows any rank can hold
             fused = FusedExpertParallel(pl, max_recv_rows=world * cap, max_local_rows=cap, max_k=K, max_n=N)
-            plan = fused.plan(counts)
+            # "fused-pieces": peers' rows travel in pieces of >= 64 rows, each flagged on its own
+            plan = fused.plan(counts, piece_rows=64 if impl == "fused-pieces" else 2048)
             # a first call on other rows, then the checked one: stale rows left
             # in the shared buffers by the first call cannot pass for fresh ones
             A0 = torch.randn(rows, K, generator=g).to(torch.bfloat16).to(dev)
@@ -84,7 +85,8 @@ def _worker(rank, world, store, q, E, impl, align, big=False):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("impl,align", [("nccl", 32), ("fused", 32), ("fused", 16), ("fused-fp4", 32)])
+@pytest.mark.parametrize("impl,align", [("nccl", 32), ("fused", 32), ("fused", 16), ("fused-fp4", 32),
+                                        ("fused-pieces", 32), ("fused-pieces", 16)])
 @pytest.mark.parametrize("E", [4, 1])
 def test_ep_grouped_mm_two_ranks(E, impl, align):
     """align 32: peers' output blocks travel through inboxes; align 16: some
@@ -101,4 +103,62 @@ def test_ep_fused_full_grid():
     not kernels that would need a free SM)."""
     results = run_ranks(_worker, 2, 4, "fused", 32, True)
     for r in range(2):
+        assert results.get(r) == "ok", results.get(r)
+
+
+def _replica_worker(rank, world, store, q, dtype_name):
+    import datetime
+    import torch.distributed as dist
+    try:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+        import mxgg
+        from mxgg.ep import ExpertPlacement, ReplicaSum
+        dev = torch.device("cuda", rank)
+        dt = getattr(torch, dtype_name)
+        shape = (1, 384, 2080)                     # not a multiple of the ranks' shares
+        rs = ReplicaSum(2 * 384 * 2080 * 4)
+        msgs = []
+        for E in [e for e in (1, 2) if world % e == 0 and world // e > 1]:
+            pl = ExpertPlacement(world, E)
+            for inplace in (True, False):
+                g = torch.Generator(device=dev).manual_seed(100 * E + rank)
+                x = torch.randn(shape, generator=g, device=dev).to(dt)
+                t = rs.buffer(shape, dt) if inplace else torch.empty(shape, dtype=dt, device=dev)
+                t.copy_(x)
+                rs.sum_(pl, t)
+                allx = [torch.empty_like(x) for _ in range(world)]
+                dist.all_gather(allx, x)
+                want = torch.zeros(shape, dtype=torch.float32, device=dev)
+                for r in pl.replica_group(rank):           # fp32, replica order, one rounding
+                    want += allx[r].float()
+                want = want.to(dt)
+                # every replica holds the same bits: compare with the group's first replica
+                got_all = [torch.empty_like(x) for _ in range(world)]
+                dist.all_gather(got_all, t.contiguous())
+                first = got_all[pl.replica_group(rank)[0]]
+                if not torch.equal(t, want) or not torch.equal(t, first):
+                    msgs.append(f"E={E} inplace={inplace}: max err {(t.float() - want.float()).abs().max().item()}")
+        st = mxgg.device_status(clear=True)
+        torch.cuda.synchronize()
+        rs.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok" if not msgs and st == 0 else f"status {st}; " + "; ".join(msgs)))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("dtype_name", ["bfloat16", "float32"])
+def test_replica_sum_matches_fp32_sum(dtype_name):
+    """The peer-memory replica sum equals the fp32 sum of every replica in
+    replica order, rounded once, and leaves all replicas bit-identical
+    (2 GPUs: one group of 2; 4 GPUs: groups of 4 and of 2)."""
+    world = 4 if torch.cuda.device_count() >= 4 else 2
+    results = run_ranks(_replica_worker, world, dtype_name)
+    for r in range(world):
         assert results.get(r) == "ok", results.get(r)
