@@ -70,24 +70,76 @@ def geomean(xs):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """SM clock and clock-event reasons while the timed region runs: NVML
+    polled every 20 ms (the library nvidia-smi reads; read-only queries), or
+    `nvidia-smi -lms 200` where the NVML bindings are missing.  A short
+    multi-GPU timed region can end before nvidia-smi has printed a sample,
+    which is why NVML comes first."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device_index):
         self.idx = device_index
         self.proc = None
         self.lines = []
+        self.samples = []          # NVML: (sm MHz, max sm MHz, reason names)
+        self.source = None
+        self._stop = threading.Event()
+        self.t = None
+
+    def _nvml_start(self):
+        import pynvml as nv
+        nv.nvmlInit()
+        h = nv.nvmlDeviceGetHandleByUUID(self.idx) if str(self.idx).startswith("GPU-") \
+            else nv.nvmlDeviceGetHandleByIndex(int(self.idx))
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)            # fails here, not in the thread
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, mx, tuple(n for n, b in bits.items() if r & b)))
+                except Exception:
+                    pass
+                self._stop.wait(0.02)
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
+
+        self.t = threading.Thread(target=poll, daemon=True)
+        self.t.start()
+        self.source = "nvml"
 
     def __enter__(self):
+        try:
+            self._nvml_start()
+            return self
+        except Exception:
+            self.source = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            self.source = "nvidia-smi"
+            # nvidia-smi can take a second or more to start on a many-GPU box,
+            # longer than a short timed region: wait for its first sample (taken
+            # before the load starts, so it is dropped)
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 15:
+                time.sleep(0.05)
+            self.lines.clear()
         except Exception:
             self.proc = None
         return self
@@ -97,6 +149,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        self._stop.set()
+        if self.source == "nvml" and self.t is not None:
+            self.t.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -106,7 +161,10 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for (s_, m_, rs) in self.samples:
+            sm.append(s_)
+            mx = m_
+            reasons.update(rs)
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -116,13 +174,14 @@ class ClockSampler:
                 mx = float(parts[2])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.REASON_NAMES, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
         sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": self.source}
 
 
 # ------------------------------------------------------------------ inputs

@@ -1003,6 +1003,29 @@ int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments) {
   return plan_workspace(kFwd, M, 128, K, n_segments, 1, 256, 256).a_bytes;
 }
 
+// PackParams of one forward-A atom pack (mxgg_pack_a_atoms); returns the warps it needs.
+static long long a_atom_pack_params(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
+                                    int64_t n_segments, void* out, PackParams* pp) {
+  *pp = PackParams{};
+  pp->mode = kFwd;
+  pp->E = (int)n_segments;
+  pp->stages = (int)((K + kBK - 1) / kBK);
+  pp->offs = segment_end_offsets;
+  pp->sfa = static_cast<const uint8_t*>(a_scale);
+  pp->sfb = static_cast<const uint8_t*>(a_scale);
+  pp->rows_a = (int)rows;
+  pp->rows_b = 1;
+  pp->sf_ld = K / 32;
+  const int64_t ld = K / 32;
+  pp->vec = (ld % 16 == 0 && aligned(a_scale, 16)) ? 4 : ((ld % 4 == 0 && aligned(a_scale, 4)) ? 1 : 0);
+  pp->a_slabs = (int)((rows + kBM - 1) / kBM + (n_segments - 1));
+  pp->b_slabs = 0;
+  pp->b_height = 1;
+  pp->a_out = static_cast<uint8_t*>(out);
+  pp->b_out = nullptr;
+  return (long long)pp->a_slabs * ((pp->stages + 3) / 4);
+}
+
 int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
                       int64_t n_segments, void* out, void* stream) {
   if (rows < 0 || K <= 0 || K % 32 != 0 || n_segments < 1 || n_segments > kMaxGroups)
@@ -1012,27 +1035,41 @@ int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, i
   if (!a_scale || !segment_end_offsets || !out) return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms: null pointer");
   DeviceState* st = nullptr;
   if (int rc = get_device_state(&st)) return rc;
-  PackParams pp{};
-  pp.mode = kFwd;
-  pp.E = (int)n_segments;
-  pp.stages = (int)((K + kBK - 1) / kBK);
-  pp.offs = segment_end_offsets;
-  pp.sfa = static_cast<const uint8_t*>(a_scale);
-  pp.sfb = static_cast<const uint8_t*>(a_scale);
-  pp.rows_a = (int)rows;
-  pp.rows_b = 1;
-  pp.sf_ld = K / 32;
-  const int64_t ld = K / 32;
-  pp.vec = (ld % 16 == 0 && aligned(a_scale, 16)) ? 4 : ((ld % 4 == 0 && aligned(a_scale, 4)) ? 1 : 0);
-  pp.a_slabs = (int)((rows + kBM - 1) / kBM + (n_segments - 1));
-  pp.b_slabs = 0;
-  pp.b_height = 1;
-  pp.a_out = static_cast<uint8_t*>(out);
-  pp.b_out = nullptr;
-  const long long chunks = (pp.stages + 3) / 4;
-  const long long warps = (long long)pp.a_slabs * chunks;
+  PackParams pp;
+  const long long warps = a_atom_pack_params(a_scale, segment_end_offsets, rows, K, n_segments, out, &pp);
   const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8));
   pack_scales_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pp);
+  MXGG_CUDA_TRY(cudaGetLastError());
+  return MXGG_OK;
+}
+
+int mxgg_pack_a_atoms_multi(const void* a_scale, int64_t K, int32_t n_dst, const int64_t* first_row,
+                            const int64_t* rows, const int32_t* const* segment_end_offsets,
+                            const int64_t* n_segments, void* const* out, void* stream) {
+  if (n_dst < 0 || n_dst > kMaxDst || K <= 0 || K % 32 != 0)
+    return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms_multi: bad sizes (n_dst %d, K %lld)", (int)n_dst, (long long)K);
+  if (n_dst == 0) return MXGG_OK;
+  if (!a_scale || !first_row || !rows || !segment_end_offsets || !n_segments || !out)
+    return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms_multi: null pointer");
+  PackMulti m{};
+  int n = 0;
+  long long warps = 0;
+  for (int i = 0; i < n_dst; ++i) {
+    if (rows[i] < 0 || first_row[i] < 0 || n_segments[i] < 1 || n_segments[i] > kMaxGroups)
+      return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms_multi: bad sizes of pack %d (rows %lld, segments %lld)", i,
+                  (long long)rows[i], (long long)n_segments[i]);
+    if (rows[i] == 0) continue;
+    if (!segment_end_offsets[i] || !out[i])
+      return fail(MXGG_ERR_INVALID, "mxgg_pack_a_atoms_multi: null pointer in pack %d", i);
+    const void* src = static_cast<const uint8_t*>(a_scale) + first_row[i] * (K / 32);
+    warps = std::max(warps, a_atom_pack_params(src, segment_end_offsets[i], rows[i], K, n_segments[i], out[i], &m.p[n]));
+    ++n;
+  }
+  if (n == 0) return MXGG_OK;
+  DeviceState* st = nullptr;
+  if (int rc = get_device_state(&st)) return rc;
+  const long long blocks = std::max(1LL, std::min<long long>((warps + 7) / 8, (long long)st->num_sms * 8 / n + 1));
+  pack_scales_multi_kernel<<<dim3((unsigned)blocks, (unsigned)n), 256, 0, static_cast<cudaStream_t>(stream)>>>(m);
   MXGG_CUDA_TRY(cudaGetLastError());
   return MXGG_OK;
 }

@@ -78,7 +78,8 @@ __device__ __forceinline__ void load_row_words(const uint8_t* row, const PackPar
 // One warp per (128-row slab, 4-stage chunk).  Lane l owns rows l + 32 c of
 // the slab; a register transpose turns its four rows into the 16-byte atom
 // row it writes for each stage, so every atom store is a coalesced 512 B.
-__global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
+// bx / nbx: this block's index among the blocks that share the work.
+__device__ __forceinline__ void pack_scales_body(const PackParams& p, unsigned bx, unsigned nbx) {
   __shared__ int s_start[kMaxGroups];
   __shared__ int s_cum[kMaxGroups + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -121,16 +122,15 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
     __syncthreads();
   }
   if (p.zero) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < p.zero_count;
-         i += (long long)gridDim.x * blockDim.x)
+    for (long long i = (long long)bx * blockDim.x + threadIdx.x; i < p.zero_count; i += (long long)nbx * blockDim.x)
       p.zero[i] = 0;
   }
   const int chunks = (p.stages + 3) / 4;
   const long long a_work = (long long)p.a_slabs * chunks;
   const long long b_work = (long long)p.b_slabs * chunks;
   const int nb = cdiv_i(max(p.b_height, 1), 128);
-  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long wi = (long long)blockIdx.x * (blockDim.x >> 5) + warp; wi < a_work + b_work; wi += nwarps) {
+  const long long nwarps = (long long)nbx * (blockDim.x >> 5);
+  for (long long wi = (long long)bx * (blockDim.x >> 5) + warp; wi < a_work + b_work; wi += nwarps) {
     const bool side_a = wi < a_work;
     const long long idx = side_a ? wi : wi - a_work;
     const int q = (int)(idx % chunks);
@@ -173,6 +173,20 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
       }
     }
   }
+}
+
+__global__ void __launch_bounds__(256) pack_scales_kernel(const PackParams p) {
+  pack_scales_body(p, blockIdx.x, gridDim.x);
+}
+
+// Several forward-A packs in one launch (an expert-parallel sender packing
+// its rows' scales for every destination): blockIdx.y picks the pack.
+struct PackMulti {
+  PackParams p[kMaxDst];
+};
+
+__global__ void __launch_bounds__(256) pack_scales_multi_kernel(const PackMulti m) {
+  pack_scales_body(m.p[blockIdx.y], blockIdx.x, gridDim.x);
 }
 
 }  // namespace mxgg

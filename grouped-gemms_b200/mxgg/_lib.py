@@ -96,6 +96,8 @@ SIGNATURES = {
     "mxgg_query_tile_m": (_i32, []),
     "mxgg_ep_atom_bytes": (_i64, [_i64, _i64, _i64]),
     "mxgg_pack_a_atoms": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "mxgg_pack_a_atoms_multi": (_int, [_vp, _i64, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                                       ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_vp), _vp]),
     "mxgg_peer_signal": (_int, [_vp, _i32, _vp]),
     "mxgg_inbox_unpack": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "mxgg_ipc_alloc": (_int, [_i64, ctypes.POINTER(_vp), ctypes.c_char_p]),

@@ -20,7 +20,8 @@ source rank s sends expert e's rows to replica s % R, so each replica sees the
 same token count as a single GPU would.  (Splitting N across ranks instead
 would all-gather every token to every rank: world times the dispatch volume
 for weak-scaled token shards.)  Replicated experts sum their weight gradients
-with an all-reduce over the replica group.
+over the replica group: in place over peer memory (``ReplicaSum``), or with
+an NCCL all-reduce (``replica_allreduce``).
 
 Nothing here synchronises the device except ``plan_dispatch``, which needs the
 received counts on the host to size the NCCL transfers.
@@ -594,11 +595,18 @@ class FusedExpertParallel:
         cur = torch.cuda.current_stream()
         sp = ctypes.c_void_p(cur.cuda_stream)
         atom_bytes_per_slab = (K + 127) // 128 * 512
-        for (d, cum, m0, src_row, rows) in plan.pack:
-            _lib.check(lib.mxgg_pack_a_atoms(ctypes.c_void_p(a_s.data_ptr() + src_row * (K // 32)),
-                                             ctypes.c_void_p(cum.data_ptr()), rows, K, cum.numel(),
-                                             ctypes.c_void_p(self.atoms.ptrs[d] + m0 * atom_bytes_per_slab), sp),
-                       "mxgg_pack_a_atoms")
+        n = len(plan.pack)
+        if n:
+            # every destination's atoms in one launch
+            i64 = ctypes.c_int64 * n
+            _lib.check(lib.mxgg_pack_a_atoms_multi(
+                ctypes.c_void_p(a_s.data_ptr()), K, n, i64(*[src_row for (_, _, _, src_row, _) in plan.pack]),
+                i64(*[rows for (_, _, _, _, rows) in plan.pack]),
+                (ctypes.c_void_p * n)(*[cum.data_ptr() for (_, cum, _, _, _) in plan.pack]),
+                i64(*[cum.numel() for (_, cum, _, _, _) in plan.pack]),
+                (ctypes.c_void_p * n)(*[self.atoms.ptrs[d] + m0 * atom_bytes_per_slab
+                                        for (d, _, m0, _, _) in plan.pack]), sp),
+                "mxgg_pack_a_atoms_multi")
         side = self._side
         side.wait_stream(cur)
         ssp = ctypes.c_void_p(side.cuda_stream)

@@ -283,6 +283,15 @@ int64_t mxgg_ep_atom_bytes(int64_t M, int64_t K, int64_t n_segments);
  * ceil(rows / 128) over the receiver's earlier segments). */
 int mxgg_pack_a_atoms(const void* a_scale, const int32_t* segment_end_offsets, int64_t rows, int64_t K,
                       int64_t n_segments, void* out, void* stream);
+/* n_dst <= 8 such packs in one launch, as a sender makes them for all its
+ * destinations: pack i takes rows [first_row[i], first_row[i] + rows[i]) of
+ * a_scale ((rows, K/32) row-major), split by the n_segments[i] device
+ * cumulative ends segment_end_offsets[i], and writes out[i].  HOST arrays
+ * of n_dst entries; packs with rows[i] == 0 are skipped.  The same bytes as
+ * n_dst calls of mxgg_pack_a_atoms, with one launch instead of n_dst. */
+int mxgg_pack_a_atoms_multi(const void* a_scale, int64_t K, int32_t n_dst, const int64_t* first_row,
+                            const int64_t* rows, const int32_t* const* segment_end_offsets,
+                            const int64_t* n_segments, void* const* out, void* stream);
 /* Writes `epoch` into `slot` (usually a peer's flag array) once everything
  * earlier on `stream` is done, as a stream memory operation
  * (cuStreamWriteValue32, with its memory barrier): no kernel, so no SM is

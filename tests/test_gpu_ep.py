@@ -121,7 +121,7 @@ def _replica_worker(rank, world, store, q, dtype_name):
         shape = (1, 384, 2080)                     # not a multiple of the ranks' shares
         rs = ReplicaSum(2 * 384 * 2080 * 4)
         msgs = []
-        for E in [e for e in (1, 2) if world % e == 0 and world // e > 1]:
+        for E in [e for e in (1, 2, 4) if world % e == 0 and world // e > 1]:
             pl = ExpertPlacement(world, E)
             for inplace in (True, False):
                 g = torch.Generator(device=dev).manual_seed(100 * E + rank)
@@ -157,8 +157,9 @@ def _replica_worker(rank, world, store, q, dtype_name):
 def test_replica_sum_matches_fp32_sum(dtype_name):
     """The peer-memory replica sum equals the fp32 sum of every replica in
     replica order, rounded once, and leaves all replicas bit-identical
-    (2 GPUs: one group of 2; 4 GPUs: groups of 4 and of 2)."""
-    world = 4 if torch.cuda.device_count() >= 4 else 2
+    (2 GPUs: one group of 2; 4 GPUs: groups of 4 and of 2; 8 GPUs: 8, 4, 2)."""
+    n = torch.cuda.device_count()
+    world = 8 if n >= 8 else 4 if n >= 4 else 2
     results = run_ranks(_replica_worker, world, dtype_name)
     for r in range(world):
         assert results.get(r) == "ok", results.get(r)
