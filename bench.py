@@ -32,7 +32,9 @@
   weights.
 * ``e2e``: the same geomean measured through the public entry points with
   host (pinned) inputs: H2D of the fp8 operands, scales and offsets, the GEMM,
-  and D2H of the output, all inside the events.
+  and D2H of the output, all inside the events.  On one GPU each call goes
+  through ``mxgg.host.HostPipeline``: four pieces on three streams, so the
+  copies overlap the GEMM pieces (bit-identical results).
 * ``--impl reference``: the reference's CPU path (dequantise + per-group fp32
   matmul, the oracle restatement -- the reference's Triton kernels are
   ROCm-only) timed on this host's cores over a bounded sample.
@@ -895,8 +897,18 @@ def time_problems(probs, steps, warmup, world, flush):
 
 
 def time_e2e(probs, steps, warmup, world):
-    """Same sweep through the public API with pinned host inputs/outputs."""
+    """Same sweep through the public API with pinned host inputs/outputs.
+
+    One GPU: each call goes through ``mxgg.host.HostPipeline`` (the call cut
+    into pieces on three streams, so the copies in and out overlap the
+    GEMMs); the events bracket the whole call, first copy in to last copy
+    out.  Expert parallel (N > 1): the rank's inputs are copied in, the call
+    runs, its output is copied out, one after another."""
     import torch
+    pipe = None
+    if world == 1:
+        from mxgg.host import HostPipeline
+        pipe = HostPipeline(pieces=4)
     max_in = max(sum(t.numel() * t.element_size() for t in p["args"]) for p in probs)
     host_in = torch.empty(max_in + 4096 * 8, dtype=torch.uint8, pin_memory=True)
     per = []
@@ -910,20 +922,33 @@ def time_e2e(probs, steps, warmup, world):
             hv.copy_(t.contiguous().view(torch.uint8).reshape(-1))
             host_views.append((hv, t.shape, t.dtype))
             off += (nb + 511) // 512 * 512
-        dev_args = [torch.empty(shape, dtype=dt, device="cuda") for (_, shape, dt) in host_views]
         out_like = run_problem(p)
         host_out = torch.empty(out_like.shape, dtype=out_like.dtype, pin_memory=True)
         del out_like
-        q = dict(p)
-        q["args"] = tuple(dev_args)
+        if pipe is not None:
+            hosts = [hv.view(dt).view(shape) for (hv, shape, dt) in host_views]
+            ends = p["args"][4].tolist()                  # the offsets travel inside the call (pinned table)
+
+            def call():
+                if p["pass_"] == "wgrad":
+                    pipe.wgrad(*hosts[:4], ends, host_out)
+                else:
+                    pipe.grouped_mm(*hosts[:4], ends, host_out, host_out.dtype)
+        else:
+            dev_args = [torch.empty(shape, dtype=dt, device="cuda") for (_, shape, dt) in host_views]
+            q = dict(p)
+            q["args"] = tuple(dev_args)
+
+            def call():
+                for (hv, shape, dt), d in zip(host_views, dev_args):
+                    d.view(torch.uint8).reshape(-1).copy_(hv, non_blocking=True)
+                out = run_problem(q)
+                host_out.copy_(out, non_blocking=True)
         ts = []
         for it in range(warmup + steps):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            for (hv, shape, dt), d in zip(host_views, dev_args):
-                d.view(torch.uint8).reshape(-1).copy_(hv, non_blocking=True)
-            out = run_problem(q)
-            host_out.copy_(out, non_blocking=True)
+            call()
             e.record()
             torch.cuda.synchronize()
             if it >= warmup:
@@ -931,7 +956,7 @@ def time_e2e(probs, steps, warmup, world):
         per.append(sum(ts) / len(ts))
         h2d_total += sum(hv.numel() for hv, _, _ in host_views)
         d2h_total += host_out.numel() * host_out.element_size()
-        del dev_args, host_out
+        del host_out
     per = allreduce_max(per, world)
     return per, h2d_total, d2h_total
 
@@ -1072,7 +1097,9 @@ def main():
     if not args.no_e2e:
         per_e, h2d, d2h = time_e2e(probs, max(1, args.steps), max(1, min(args.warmup, 2)), world)
         e2e = {"value": round(world * geomean([p["flops"] / t / 1e12 for p, t in zip(probs, per_e)]), 1),
-               "unit": "TFLOPS", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+               "unit": "TFLOPS", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "path": ("mxgg.host.HostPipeline: 4 pieces, copies in / GEMMs / copies out on 3 streams"
+                        if world == 1 else "copy in, expert-parallel call, copy out")}
 
     if rank == 0 and args.detail:
         for i, (p, t) in enumerate(zip(probs, per)):
