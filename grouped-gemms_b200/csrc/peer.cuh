@@ -54,9 +54,10 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerFlags f, int
 // Unpacks this rank's inbox: for each listed 32-row block and each 64-byte
 // column chunk, the 2 KB block (rows in the 64-byte swizzle of the GEMM's
 // staging buffer: row r's chunk j at r * 64 + (j ^ ((r >> 1) & 3)) * 16)
-// goes to rows [32 * rb, 32 * rb + 32) of the row-major output.  One warp per
-// block; consecutive warps take consecutive chunks of a row block, so each
-// output line is completed in L2 before it is written back.
+// goes to rows [32 * rb, 32 * rb + 32) of the row-major output.  One warp
+// per block, four passes: in pass i lane l moves the block's 16-byte piece
+// q = 32 i + l (row q / 4), so every load is 512 contiguous bytes and every
+// store covers eight rows with whole 64-byte runs (full 32-byte sectors).
 __global__ void __launch_bounds__(256) inbox_unpack_kernel(const uint8_t* __restrict__ inbox,
                                                            uint8_t* __restrict__ out,
                                                            const int32_t* __restrict__ row_blocks, int n_rb,
@@ -68,14 +69,17 @@ __global__ void __launch_bounds__(256) inbox_unpack_kernel(const uint8_t* __rest
     const int rbi = (int)(w / chunks);
     const int cc = (int)(w - (long long)rbi * chunks);
     const long long rb = __ldg(row_blocks + rbi);
-    const uint4* src = reinterpret_cast<const uint4*>(inbox + (rb * chunks + cc) * 2048) + lane * 4;
+    const uint4* src = reinterpret_cast<const uint4*>(inbox + (rb * chunks + cc) * 2048);
     uint4 v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __ldcs(src + j);
-    uint4* dst = reinterpret_cast<uint4*>(out + (rb * 32 + lane) * row_bytes + (long long)cc * 64);
-    const int sw = (lane >> 1) & 3;
+    for (int i = 0; i < 4; ++i) v[i] = __ldcs(src + 32 * i + lane);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j ^ sw] = v[j];
+    for (int i = 0; i < 4; ++i) {
+      const int q = 32 * i + lane;
+      const int r = q >> 2;
+      const int j = (q & 3) ^ ((r >> 1) & 3);
+      *reinterpret_cast<uint4*>(out + (rb * 32 + r) * row_bytes + (long long)cc * 64 + j * 16) = v[i];
+    }
   }
 }
 
