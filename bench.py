@@ -385,15 +385,14 @@ def run_ep_problem(p, marks=None):
         if marks:
             marks[0].record()
         if "rsum" in p:
-            # the gradient goes straight into this rank's peer-visible replica buffer
-            from mxgg import ops, tune
+            # the gradient goes straight into this rank's peer-visible replica
+            # buffer; on large grids the first part's replica sum overlaps the
+            # second part's GEMM (the finish phase is then the second sum)
+            from mxgg import tune
             go_q, _, ia_q, _, offs = p["args"]
             L, N, K = offs.shape[0], go_q.shape[0], ia_q.shape[0]
-            out = ops.wgrad_into(*p["args"], p["rsum"].buffer((L, N, K), torch_bf16()),
-                                 tune.call_config(tune.pick("wgrad", L, N, K)))
-            if marks:
-                marks[1].record()
-            p["rsum"].sum_(plan.placement, out)
+            out = p["rsum"].wgrad_sum(plan.placement, *p["args"], cfg=tune.call_config(tune.pick("wgrad", L, N, K)),
+                                      gemm_done=marks[1] if marks else None)
         else:
             out = kernels.triton_mxfp8_wgrad(*p["args"])
             if marks:

@@ -231,6 +231,8 @@ class ReplicaSum:
         self.buf = PeerBuffer(max(self.max_bytes, 256), group)
         self.flags = PeerBuffer(256, group)
         self.epoch = 0
+        self._side = torch.cuda.Stream()
+        self._pairs = max(1, torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2)
 
     def close(self) -> None:
         self.buf.close()
@@ -242,8 +244,9 @@ class ReplicaSum:
 
     def sum_(self, placement: ExpertPlacement, t: Tensor) -> Tensor:
         """Collective: every replica of this rank's experts gets the sum of
-        all replicas' `t` (no-op without replicas).  `t` is best the tensor
-        `buffer` returned; any other contiguous tensor is copied in and out."""
+        all replicas' `t` (no-op without replicas).  A tensor inside this
+        rank's buffer (`buffer`, or a part of it) is summed where it lies;
+        any other contiguous tensor is copied in and out."""
         import ctypes
         from . import _lib
         from .ops import _OUT_DTYPES
@@ -256,15 +259,19 @@ class ReplicaSum:
         nbytes = t.numel() * t.element_size()
         if nbytes > self.max_bytes:
             raise ValueError(f"{nbytes} bytes exceed the {self.max_bytes}-byte replica buffers")
-        inplace = t.data_ptr() == self.buf.ptrs[self.rank]
+        # a tensor inside this rank's buffer is summed where it lies (at the
+        # same offset in every replica); any other is copied in and out
+        off = t.data_ptr() - self.buf.ptrs[self.rank]
+        inplace = 0 <= off and off + nbytes <= self.max_bytes and off % 16 == 0
         if not inplace:
+            off = 0
             self.buffer(t.shape, t.dtype).copy_(t)
         ranks = placement.replica_group(self.rank)
         me = ranks.index(self.rank)
         lib = _lib.load()
         stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         flags = (ctypes.c_void_p * len(ranks))(*[self.flags.ptrs[r] for r in ranks])
-        bufs = (ctypes.c_void_p * len(ranks))(*[self.buf.ptrs[r] for r in ranks])
+        bufs = (ctypes.c_void_p * len(ranks))(*[self.buf.ptrs[r] + off for r in ranks])
         # every rank takes the same epochs in the same order (each sum_ is collective)
         self.epoch += 1
         _lib.check(lib.mxgg_peer_barrier(flags, len(ranks), me, self.epoch, stream), "mxgg_peer_barrier")
@@ -275,6 +282,65 @@ class ReplicaSum:
         if not inplace:
             t.copy_(self.buffer(t.shape, t.dtype))
         return t
+
+    def split_rows(self, L: int, N: int, K: int) -> Optional[int]:
+        """Where `wgrad_sum` cuts a one-expert gradient along N, or None.
+
+        The two launches must not take more rounds of 256 x 256 tiles over
+        the GPU's CTA pairs than one launch would (a cut that adds a round
+        costs more than the overlap saves), and the grid must hold at least
+        four rounds.  Among the cuts that qualify, the one nearest the middle."""
+        if L != 1:
+            return None
+        P = self._pairs
+        nt, kt = -(-N // 256), -(-K // 256)
+        if nt < 2 or nt * kt < 4 * P:
+            return None
+        rounds = -(-nt * kt // P)
+        best = None
+        for a in range(1, nt):
+            if -(-a * kt // P) + -(-(nt - a) * kt // P) <= rounds:
+                if best is None or abs(2 * a - nt) < abs(2 * best - nt):
+                    best = a
+        return None if best is None else 256 * best
+
+    def wgrad_sum(self, placement: ExpertPlacement, go_t: Tensor, go_scale: Tensor, ia_t: Tensor,
+                  ia_scale: Tensor, offs: Tensor, cfg=None, out_dtype: torch.dtype = torch.bfloat16,
+                  gemm_done: Optional["torch.cuda.Event"] = None) -> Tensor:
+        """Collective: this rank's weight gradient (`mxgg.ops.wgrad_into`,
+        row-major scales) written into its replica buffer and summed over the
+        replicas; returns the (L, N, K) buffer view.
+
+        With one local expert, no tuned config and a large enough grid
+        (`split_rows`), the gradient is computed in two launches cut along N,
+        and the first part's replica sum runs on a side stream while the
+        second part computes: the sum's NVLink traffic overlaps the GEMM.
+        Each part is whole tiles of the same grid, so the bits are those of
+        one launch.  `gemm_done`, if given, is recorded on the current stream
+        after the last GEMM launch (for timing the phases)."""
+        from .ops import wgrad_into
+        L, N, K = offs.shape[0], go_t.shape[0], ia_t.shape[0]
+        out = self.buffer((L, N, K), out_dtype)
+        cut = self.split_rows(L, N, K) if placement.replicas > 1 and cfg is None else None
+        if cut is None:
+            wgrad_into(go_t, go_scale, ia_t, ia_scale, offs, out, cfg)
+            if gemm_done is not None:
+                gemm_done.record()
+            return self.sum_(placement, out)
+        flat = out.view(N, K)
+        first, second = flat[:cut].view(1, cut, K), flat[cut:].view(1, N - cut, K)
+        wgrad_into(go_t[:cut], go_scale[:cut], ia_t, ia_scale, offs, first)
+        cur = torch.cuda.current_stream()
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            self.sum_(placement, first)
+        wgrad_into(go_t[cut:], go_scale[cut:], ia_t, ia_scale, offs, second)
+        if gemm_done is not None:
+            gemm_done.record()
+        # every rank's second sum starts after its first: the barriers' epochs stay in order
+        cur.wait_stream(self._side)
+        self.sum_(placement, second)
+        return out
 
 
 # ----------------------------------------------------------------------------

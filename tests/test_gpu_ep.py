@@ -163,3 +163,59 @@ def test_replica_sum_matches_fp32_sum(dtype_name):
     results = run_ranks(_replica_worker, world, dtype_name)
     for r in range(world):
         assert results.get(r) == "ok", results.get(r)
+
+
+def _replica_wgrad_worker(rank, world, store, q, N, K):
+    import datetime
+    import torch.distributed as dist
+    try:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+        import mxgg
+        import utils
+        from mxgg.ep import ExpertPlacement, ReplicaSum
+        dev = torch.device("cuda", rank)
+        M = 1024
+        pl = ExpertPlacement(world, 1)                       # one expert, `world` replicas
+        g = torch.Generator(device=dev).manual_seed(40 + rank)
+        go = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        go_s, go_q = utils.to_mx_dim1(go)
+        x_s, x_q = utils.to_mx_dim1(x)
+        offs = torch.tensor([M], dtype=torch.int32, device=dev)
+        mine = mxgg.ops.wgrad(go_q, go_s, x_q, x_s, offs, torch.bfloat16)   # one launch, default schedule
+        rs = ReplicaSum(N * K * 2)
+        split = rs.split_rows(1, N, K)
+        msgs = []
+        for it in range(2):                                  # the second call reuses the buffer
+            got = rs.wgrad_sum(pl, go_q, go_s, x_q, x_s, offs)
+            allg = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allg, mine)
+            want = torch.zeros_like(mine, dtype=torch.float32)
+            for r in pl.replica_group(rank):
+                want += allg[r].float()
+            if not torch.equal(got, want.to(torch.bfloat16)):
+                msgs.append(f"call {it}: max err {(got.float() - want).abs().max().item()}")
+        st = mxgg.device_status(clear=True)
+        torch.cuda.synchronize()
+        rs.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok" if not msgs and st == 0 else f"split {split}, status {st}; " + "; ".join(msgs)))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("N,K", [(5120, 5120), (1024, 768)])
+def test_replica_wgrad_sum_overlapped(N, K):
+    """ReplicaSum.wgrad_sum: the gradient computed in two launches (N=K=5120:
+    the first part's replica sum overlaps the second part's GEMM) or one
+    (a small grid), summed over the replicas, equals the fp32 sum of every
+    replica's one-launch gradient in replica order, rounded once."""
+    results = run_ranks(_replica_wgrad_worker, 2, N, K)
+    for r in range(2):
+        assert results.get(r) == "ok", results.get(r)
