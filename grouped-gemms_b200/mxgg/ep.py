@@ -199,6 +199,30 @@ def replica_groups(placement: ExpertPlacement) -> dict:
     return out
 
 
+def wgrad_split_rows(L: int, N: int, K: int, pairs: int) -> Optional[int]:
+    """Where a one-expert (L == 1) weight gradient of N x K is cut along N
+    into two launches whose parts overlap the replica sum, or None.
+
+    The two launches must not take more rounds of 256 x 256 tiles over
+    `pairs` CTA pairs than one launch would (a cut that adds a round costs
+    more than the overlap saves), and the grid must hold at least four
+    rounds.  Among the cuts that qualify, the one nearest the middle; the
+    cut is a multiple of 256 rows, so both parts are whole tiles of the
+    one-launch grid."""
+    if L != 1 or pairs < 1:
+        return None
+    nt, kt = -(-N // 256), -(-K // 256)
+    if nt < 2 or nt * kt < 4 * pairs:
+        return None
+    rounds = -(-nt * kt // pairs)
+    best = None
+    for a in range(1, nt):
+        if -(-a * kt // pairs) + -(-(nt - a) * kt // pairs) <= rounds:
+            if best is None or abs(2 * a - nt) < abs(2 * best - nt):
+                best = a
+    return None if best is None else 256 * best
+
+
 class ReplicaSum:
     """Sums replicated experts' weight gradients over NVLink peer memory, in
     place: the fused counterpart of `replica_allreduce`.
@@ -284,25 +308,9 @@ class ReplicaSum:
         return t
 
     def split_rows(self, L: int, N: int, K: int) -> Optional[int]:
-        """Where `wgrad_sum` cuts a one-expert gradient along N, or None.
-
-        The two launches must not take more rounds of 256 x 256 tiles over
-        the GPU's CTA pairs than one launch would (a cut that adds a round
-        costs more than the overlap saves), and the grid must hold at least
-        four rounds.  Among the cuts that qualify, the one nearest the middle."""
-        if L != 1:
-            return None
-        P = self._pairs
-        nt, kt = -(-N // 256), -(-K // 256)
-        if nt < 2 or nt * kt < 4 * P:
-            return None
-        rounds = -(-nt * kt // P)
-        best = None
-        for a in range(1, nt):
-            if -(-a * kt // P) + -(-(nt - a) * kt // P) <= rounds:
-                if best is None or abs(2 * a - nt) < abs(2 * best - nt):
-                    best = a
-        return None if best is None else 256 * best
+        """Where `wgrad_sum` cuts a one-expert gradient along N, or None
+        (`wgrad_split_rows` over this GPU's CTA pairs)."""
+        return wgrad_split_rows(L, N, K, self._pairs)
 
     def wgrad_sum(self, placement: ExpertPlacement, go_t: Tensor, go_scale: Tensor, ia_t: Tensor,
                   ia_scale: Tensor, offs: Tensor, cfg=None, out_dtype: torch.dtype = torch.bfloat16,

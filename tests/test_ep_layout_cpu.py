@@ -122,3 +122,21 @@ def test_pieces_cut_large_blocks_on_the_tile_grid():
     assert sum(c[3] for c in lay["copies"]) == 15360
     # it receives rank 1's 15360 rows in four pieces; its own 1280 rows stay whole
     assert lay["seg"]["src"] == [0, 1, 3, 5, 7]
+
+
+@pytest.mark.parametrize("N,K,want", [(5120, 5120, 2560), (8192, 5120, 3584), (8192, 8192, 4096),
+                                      (5120, 8192, 2304), (2048, 2048, None), (2048, 8192, None)])
+def test_wgrad_split_rows(N, K, want):
+    """The cut of the overlapped replica sum: on the 256-row tile grid, no
+    extra round of tiles over 74 CTA pairs, nearest the middle; small grids
+    are not cut."""
+    from mxgg.ep import wgrad_split_rows
+    P = 74
+    cut = wgrad_split_rows(1, N, K, P)
+    assert cut == want
+    if cut is not None:
+        nt, kt = N // 256, K // 256
+        a = cut // 256
+        assert cut % 256 == 0 and 0 < cut < N
+        assert -(-a * kt // P) + -(-(nt - a) * kt // P) <= -(-nt * kt // P)
+    assert wgrad_split_rows(2, N, K, P) is None          # several local experts: one launch
