@@ -33,7 +33,7 @@
 * ``e2e``: the same geomean measured through the public entry points with
   host (pinned) inputs: H2D of the fp8 operands, scales and offsets, the GEMM,
   and D2H of the output, all inside the events.  On one GPU each call goes
-  through ``mxgg.host.HostPipeline``: four pieces on three streams, so the
+  through ``mxgg.host.HostPipeline``: eight pieces on three streams, so the
   copies overlap the GEMM pieces (bit-identical results).
 * ``--impl reference``: the reference's CPU path (dequantise + per-group fp32
   matmul, the oracle restatement -- the reference's Triton kernels are
@@ -907,7 +907,7 @@ def time_e2e(probs, steps, warmup, world):
     pipe = None
     if world == 1:
         from mxgg.host import HostPipeline
-        pipe = HostPipeline(pieces=4)
+        pipe = HostPipeline(pieces=8)
     max_in = max(sum(t.numel() * t.element_size() for t in p["args"]) for p in probs)
     host_in = torch.empty(max_in + 4096 * 8, dtype=torch.uint8, pin_memory=True)
     per = []
@@ -1097,7 +1097,7 @@ def main():
         per_e, h2d, d2h = time_e2e(probs, max(1, args.steps), max(1, min(args.warmup, 2)), world)
         e2e = {"value": round(world * geomean([p["flops"] / t / 1e12 for p, t in zip(probs, per_e)]), 1),
                "unit": "TFLOPS", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "path": ("mxgg.host.HostPipeline: 4 pieces, copies in / GEMMs / copies out on 3 streams"
+               "path": ("mxgg.host.HostPipeline: 8 pieces, copies in / GEMMs / copies out on 3 streams"
                         if world == 1 else "copy in, expert-parallel call, copy out")}
 
     if rank == 0 and args.detail:

@@ -45,7 +45,7 @@ class HostPipeline:
     stream, and the current stream waits for its last copy out, so events
     recorded around the call on that stream bracket all of it."""
 
-    def __init__(self, device: Optional[torch.device] = None, pieces: int = 4):
+    def __init__(self, device: Optional[torch.device] = None, pieces: int = 8):
         if pieces < 1:
             raise ValueError("pieces must be >= 1")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
