@@ -38,6 +38,40 @@ def _bytes(t: Tensor) -> Tensor:
     return t.contiguous().view(torch.uint8).reshape(-1)
 
 
+def row_cuts(rows: int, pieces: int, align: int = 256) -> List[int]:
+    """Cut points [0, ..., rows] of about `pieces` equal runs of rows, on
+    multiples of `align` (fewer runs when `rows` is short)."""
+    cuts = [0]
+    for c in range(1, pieces):
+        x = (c * rows // pieces) // align * align
+        if cuts[-1] < x < rows:
+            cuts.append(x)
+    cuts.append(rows)
+    return cuts
+
+
+def group_pieces(ends: Sequence[int], row_bytes: int, expert_bytes: int,
+                 pieces: int) -> List[Tuple[int, int, int, int]]:
+    """(first group, end group, first row, end row) of each piece of a
+    forward call: with several groups, runs of whole groups of about equal
+    bytes to copy in (their rows plus their experts' weights); with one,
+    runs of rows."""
+    E, M = len(ends), (ends[-1] if ends else 0)
+    if E >= 2 and pieces > 1:
+        starts = [0] + list(ends[:-1])
+        cost = [(ends[g] - starts[g]) * row_bytes + expert_bytes for g in range(E)]
+        total, acc, out, g0 = sum(cost), 0, [], 0
+        for g in range(E):
+            acc += cost[g]
+            if acc * pieces >= total * (len(out) + 1) and g + 1 < E and len(out) + 1 < pieces:
+                out.append((g0, g + 1, starts[g0], ends[g]))
+                g0 = g + 1
+        out.append((g0, E, starts[g0], M))
+        return out
+    cuts = row_cuts(M, pieces)
+    return [(0, E, cuts[c], cuts[c + 1]) for c in range(len(cuts) - 1)]
+
+
 class HostPipeline:
     """Three streams (copy in, compute, copy out) and device staging buffers,
     reused from call to call.  Host tensors must be pinned and contiguous.
@@ -79,32 +113,8 @@ class HostPipeline:
     def _finish(self) -> None:
         torch.cuda.current_stream(self.device).wait_stream(self.d2h)
 
-    @staticmethod
-    def _row_cuts(rows: int, pieces: int, align: int = 256) -> List[int]:
-        cuts = [0]
-        for c in range(1, pieces):
-            x = (c * rows // pieces) // align * align
-            if cuts[-1] < x < rows:
-                cuts.append(x)
-        cuts.append(rows)
-        return cuts
-
     def _group_pieces(self, ends: Sequence[int], row_bytes: int, expert_bytes: int) -> List[Tuple[int, int, int, int]]:
-        """(first group, end group, first row, end row) of each piece."""
-        E, M = len(ends), ends[-1] if ends else 0
-        if E >= 2 and self.pieces > 1:
-            starts = [0] + list(ends[:-1])
-            cost = [(ends[g] - starts[g]) * row_bytes + expert_bytes for g in range(E)]
-            total, acc, out, g0 = sum(cost), 0, [], 0
-            for g in range(E):
-                acc += cost[g]
-                if acc * self.pieces >= total * (len(out) + 1) and g + 1 < E and len(out) + 1 < self.pieces:
-                    out.append((g0, g + 1, starts[g0], ends[g]))
-                    g0 = g + 1
-            out.append((g0, E, starts[g0], M))
-            return out
-        cuts = self._row_cuts(M, self.pieces)
-        return [(0, E, cuts[c], cuts[c + 1]) for c in range(len(cuts) - 1)]
+        return group_pieces(ends, row_bytes, expert_bytes, self.pieces)
 
     # ------------------------------------------------------------ calls
     def grouped_mm(self, a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor, group_end_offsets,
@@ -182,7 +192,7 @@ class HostPipeline:
         E = len(ends)
         if out.shape != (E, N, K):
             raise ValueError(f"wgrad: out must be ({E}, {N}, {K})")
-        cuts = self._row_cuts(N, self.pieces)
+        cuts = row_cuts(N, self.pieces)
         g_d, gs_d = self._buf("a", go_t), self._buf("as", go_scale)
         x_d, xs_d = self._buf("b", ia_t), self._buf("bs", ia_scale)
         offs_h = torch.tensor(ends, dtype=torch.int32).pin_memory()
